@@ -1,0 +1,123 @@
+/*
+ * oeqb200.h -- C ABI of the B200-native Clebsch-Gordan tensor-product library
+ * (liboeqb200.so).
+ *
+ * Every entry point takes plain pointers and sizes, returns 0 on success and a
+ * non-zero OEQB_ERR_* code on failure (the message is available from
+ * oeqb_last_error()), and never aborts the process.  Device pointers must live on the
+ * device the plan was created for; `stream` is a cudaStream_t (NULL = legacy default
+ * stream).  All launches are asynchronous on that stream.
+ *
+ * The entry points replace the reference's JIT runtime interfaces:
+ *   plan create        <- JITTPImpl / JITConvImpl constructors + NVRTC compile
+ *                         (openequivariance/extension/tensorproducts.hpp:22-49,
+ *                          convolution.hpp:37-77, backend/backend_cuda.hpp:199-301)
+ *   oeqb_tp_*          <- JITTPImpl::exec_tensor_product / backward / double_backward
+ *                         (openequivariance/extension/tensorproducts.hpp:77-116)
+ *   oeqb_conv_*        <- JITConvImpl::exec_conv / backward / double_backward
+ *                         (openequivariance/extension/convolution.hpp:79-186)
+ *   oeqb_sc_*          <- group_gemm + the torch glue of the MACE symmetric contraction
+ *                         (openequivariance/extension/group_mm.hpp:38-141,
+ *                          _torch/symmetric_contraction/SymmetricContraction.py:220-336)
+ *
+ * Problem descriptor (little-endian, produced by openequivariance_b200.plan.pack_descriptor):
+ *   int64 header[16] = { magic 0x4251454F ("OEQB"), version 1, dtype (1=f32, 2=f64),
+ *                        layout (0=mul_ir, 1=ir_mul), mode (0=uvu, 1=uvw), shared_weights,
+ *                        n_irreps_in1, n_irreps_in2, n_irreps_out, n_instructions,
+ *                        L1_dim, L2_dim, L3_dim, weight_numel, n_cg_entries,
+ *                        flags (bit0 deterministic conv, bit1 Kahan summation) }
+ *   int64 irreps[(n1+n2+n3)][3]         = { mul, l, offset } for in1, in2, out in order
+ *   instructions[n_instructions]        = { int64 i_in1, i_in2, i_out, weight_offset,
+ *                                           cg_offset, cg_nnz; double path_weight }
+ *   cg[n_cg_entries]                    = { int64 i, j, k; double value }
+ * Weights are in the reference's "oeq" order (multiplicities split in chunks of 32,
+ * uvu blocks [v][u], uvw blocks [v][u][w]).
+ */
+#ifndef OEQB200_H_
+#define OEQB200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define OEQB_OK 0
+#define OEQB_ERR_INVALID 1      /* bad argument or descriptor */
+#define OEQB_ERR_UNSUPPORTED 2  /* problem outside the supported subset */
+#define OEQB_ERR_CUDA 3         /* CUDA runtime error */
+#define OEQB_ERR_DEVICE 4       /* a kernel flagged an out-of-range index */
+
+typedef struct oeqb_plan oeqb_plan;
+
+/* Library version string. */
+const char* oeqb_version(void);
+
+/* Message of the last failing call on this host thread ("" if none). */
+const char* oeqb_last_error(void);
+
+/* Builds a plan for `device` from a problem descriptor (see above).  Replaces the
+ * reference's per-problem NVRTC compile: kernels are compiled ahead of time for
+ * sm_100a and specialised per degree triple; the plan only uploads tables. */
+int oeqb_plan_create(const void* descriptor, size_t nbytes, int device, oeqb_plan** out);
+int oeqb_plan_destroy(oeqb_plan* plan);
+
+/* Bytes of workspace the convolution entry points need (0 for this implementation;
+ * kept so callers that allocate the reference's workspace keep working). */
+size_t oeqb_conv_workspace_bytes(const oeqb_plan* plan, int64_t nnz, int64_t node_count);
+
+/* Synchronises `stream` and reports (then clears) the plan's device error flag:
+ * 0 = clean, 1 = an edge index was out of range, 2 = a permutation entry was out of
+ * range.  Kernels skip such entries instead of faulting. */
+int oeqb_plan_check_status(oeqb_plan* plan, int* status, void* stream);
+
+/* ---- batch tensor product (replaces tensorproducts.hpp:77-88) ----
+ * L1_in [batch, L1_dim], L2_in [batch, L2_dim], W [batch, weight_numel] or
+ * [weight_numel] when the weights are shared, L3_out [batch, L3_dim]. */
+int oeqb_tp_forward(oeqb_plan* plan, int64_t batch, const void* L1_in, const void* L2_in,
+                    const void* W, void* L3_out, void* stream);
+
+/* (tensorproducts.hpp:90-100) All gradients are outputs; shared-weight W_grad is
+ * zeroed by the call before accumulation. */
+int oeqb_tp_backward(oeqb_plan* plan, int64_t batch, const void* L1_in, void* L1_grad,
+                     const void* L2_in, void* L2_grad, const void* W, void* W_grad,
+                     const void* L3_grad, void* stream);
+
+/* (tensorproducts.hpp:102-116) Inputs L1_in, L2_in, W, L3_grad and the upstream
+ * gradients L1_dgrad, L2_dgrad, W_dgrad; outputs L1_grad, L2_grad, W_grad, L3_dgrad. */
+int oeqb_tp_double_backward(oeqb_plan* plan, int64_t batch, const void* L1_in,
+                            const void* L2_in, const void* W, const void* L3_grad,
+                            const void* L1_dgrad, const void* L2_dgrad, const void* W_dgrad,
+                            void* L1_grad, void* L2_grad, void* W_grad, void* L3_dgrad,
+                            void* stream);
+
+/* ---- fused graph convolution (replaces convolution.hpp:79-186) ----
+ * z[rows[e]] += TP(x[cols[e]], y[e], W[e]).  rows/cols are int64 [nnz]; L1_in and L3_out
+ * have node_count rows, L2_in and W (unless shared) have nnz rows.  In deterministic
+ * mode rows must be sorted (receiver-major) and transpose_perm[p] is the index of the
+ * p-th edge in sender-sorted order; results are bitwise reproducible.  Outputs are
+ * zero-initialised by the call. */
+int oeqb_conv_forward(oeqb_plan* plan, const void* L1_in, const void* L2_in, const void* W,
+                      void* L3_out, const int64_t* rows, const int64_t* cols, int64_t nnz,
+                      int64_t node_count, void* workspace, size_t workspace_bytes, void* stream);
+
+int oeqb_conv_backward(oeqb_plan* plan, const void* L1_in, void* L1_grad, const void* L2_in,
+                       void* L2_grad, const void* W, void* W_grad, const void* L3_grad,
+                       const int64_t* rows, const int64_t* cols, int64_t nnz,
+                       int64_t node_count, void* workspace, size_t workspace_bytes,
+                       const int64_t* transpose_perm, void* stream);
+
+int oeqb_conv_double_backward(oeqb_plan* plan, const void* L1_in, const void* L2_in,
+                              const void* W, const void* L3_grad, const void* L1_dgrad,
+                              const void* L2_dgrad, const void* W_dgrad, void* L1_grad,
+                              void* L2_grad, void* W_grad, void* L3_dgrad, const int64_t* rows,
+                              const int64_t* cols, int64_t nnz, int64_t node_count,
+                              void* workspace, size_t workspace_bytes,
+                              const int64_t* transpose_perm, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* OEQB200_H_ */

@@ -1,0 +1,58 @@
+"""B200-native (sm_100a) Clebsch-Gordan tensor products with the OpenEquivariance API.
+
+Public names mirror the reference package ``openequivariance`` (its ``__init__.py:106-116``):
+``TPProblem``, ``Irreps``, ``TensorProduct``, ``TensorProductConv``, ``transpose_irreps``,
+``torch_to_oeq_dtype`` and ``torch_ext_so_path``, plus the MACE ``SymmetricContraction``.
+Set ``OEQ_NOTORCH=1`` to import only the torch-free problem specification.
+"""
+
+import os
+
+import numpy as np
+
+from .irreps import Instruction, Irrep, Irreps, TPProblem, _MulIr
+
+__version__ = "0.1.0"
+
+if os.environ.get("OEQ_NOTORCH", "0") != "1":
+    import torch
+
+    from .tensor_product import TensorProduct
+    from .tensor_product_conv import TensorProductConv
+    from .utils import torch_to_oeq_dtype, transpose_irreps
+
+    torch.serialization.add_safe_globals(
+        [TensorProduct, TensorProductConv, TPProblem, Irrep, Irreps, _MulIr, Instruction,
+         np.float32, np.float64]
+    )
+
+
+def torch_ext_so_path():
+    """Path of the ``.so`` to link when using the operators from the PyTorch C++ API."""
+    from ._ext import TORCH_LIB_PATH
+
+    return str(TORCH_LIB_PATH)
+
+
+class _JaxUnavailable:
+    """JAX is outside this package's scope; mirrors the reference's error stub."""
+
+    def TensorProduct(self, *args, **kwargs):
+        raise ImportError("openequivariance_b200 has no JAX frontend")
+
+    def TensorProductConv(self, *args, **kwargs):
+        raise ImportError("openequivariance_b200 has no JAX frontend")
+
+
+jax = _JaxUnavailable()
+
+__all__ = [
+    "TPProblem",
+    "Irreps",
+    "TensorProduct",
+    "TensorProductConv",
+    "torch_to_oeq_dtype",
+    "torch_ext_so_path",
+    "jax",
+    "transpose_irreps",
+]

@@ -1,0 +1,674 @@
+// Host runtime behind the C ABI in include/oeqb200.h: descriptor parsing, plan tables,
+// launch configuration and the kernel sequences of every pass.
+//
+// Kernel sequences follow the reference's JIT wrappers (extension/tensorproducts.hpp:77-116,
+// extension/convolution.hpp:79-186): one launch per pass for the batch forward/backward,
+// two for the double backward (part A = three forward terms into L3_dgrad, part B = two
+// backward terms into the input gradients).  The reference's deterministic convolution
+// needs an extra fixup launch per pass; this build snaps each warp's edge range to row
+// boundaries instead, so every pass is a single launch.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <set>
+#include <string>
+#include <unordered_map>
+#include <vector>
+
+#include "oeqb200.h"
+#include "tp_core.cuh"
+
+namespace oeqb {
+template <class T>
+const void* batch_kernel_ptr(int kind, bool uvw, bool db, int policy);
+template <class T>
+const void* det_kernel_ptr(int kind, bool uvw, bool db, bool kahan);
+}  // namespace oeqb
+
+using namespace oeqb;
+
+// Launch policies of the batch/atomic kernel table (tp_kernels.cuh: enum Policy).
+constexpr int kBatch = 0;
+constexpr int kConvAtomic = 1;
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const std::string& msg) {
+  g_last_error = msg;
+  return code;
+}
+
+#define OEQB_CUDA(expr)                                                                  \
+  do {                                                                                   \
+    cudaError_t e_ = (expr);                                                             \
+    if (e_ != cudaSuccess)                                                               \
+      return fail(OEQB_ERR_CUDA, std::string(#expr " failed: ") + cudaGetErrorString(e_)); \
+  } while (0)
+
+constexpr int64_t kMagic = 0x4251454F;
+
+struct DevArrays {
+  size_t ir1, ir2, ir3, ins_f, grp_f, zb_f, ins_b, grp_b, zb_b, cg, total;
+};
+
+struct KernelCfg {
+  int blocks_per_sm = 0;
+};
+
+}  // namespace
+
+struct oeqb_plan {
+  int device = 0;
+  int dtype = 1;
+  int layout = 0;
+  int uvw = 0;
+  int shared_w = 0;
+  int det = 0;
+  int kahan = 0;
+  int n1 = 0, n2 = 0, n3 = 0, nins = 0;
+  int L1dim = 0, L2dim = 0, L3dim = 0, wnumel = 0;
+  int lgG = 0;
+  std::vector<IrrepD> ir1, ir2, ir3;
+  std::vector<InstrD> ins_f, ins_b;
+  std::vector<GroupD> grp_f, grp_b;
+  std::vector<int> zb_f, zb_b;
+  std::vector<CGEntry> cg;
+  DevArrays off{};
+  unsigned char* dmem = nullptr;
+  int* d_status = nullptr;
+  int ws_elems = 0, off_t = 0, off_t2 = 0, off_gz = 0, off_dy = 0;
+  size_t desc_f = 0, desc_b = 0;
+  int sm_count = 148;
+  std::mutex mu;
+  std::unordered_map<const void*, int> occ;  // kernel -> resident blocks per SM
+  size_t elem() const { return dtype == 2 ? 8 : 4; }
+};
+
+namespace {
+
+size_t align16(size_t x) { return (x + 15) & ~size_t(15); }
+
+size_t desc_bytes(const oeqb_plan& p, size_t ngrp, size_t nzero) {
+  return align16(sizeof(InstrD) * p.nins + sizeof(IrrepD) * (p.n1 + p.n2 + p.n3) +
+                 sizeof(GroupD) * ngrp + sizeof(int) * nzero);
+}
+
+// Group instructions by the irrep whose output/gradient they produce (stable order).
+void make_groups(const std::vector<InstrD>& ins, bool by_out, int nirreps,
+                 const std::vector<IrrepD>& irreps, std::vector<InstrD>& out_ins,
+                 std::vector<GroupD>& groups, std::vector<int>& zero_blocks) {
+  std::vector<InstrD> sorted = ins;
+  std::stable_sort(sorted.begin(), sorted.end(), [&](const InstrD& a, const InstrD& b) {
+    return by_out ? a.i3 < b.i3 : a.i1 < b.i1;
+  });
+  out_ins = sorted;
+  groups.clear();
+  std::vector<char> used(nirreps, 0);
+  for (size_t i = 0; i < sorted.size();) {
+    const int key = by_out ? sorted[i].i3 : sorted[i].i1;
+    size_t j = i;
+    while (j < sorted.size() && (by_out ? sorted[j].i3 : sorted[j].i1) == key) ++j;
+    GroupD g{key, static_cast<int>(i), static_cast<int>(j - i), 0};
+    groups.push_back(g);
+    used[key] = 1;
+    i = j;
+  }
+  zero_blocks.clear();
+  for (int r = 0; r < nirreps; ++r)
+    if (!used[r] && irreps[r].mul > 0) zero_blocks.push_back(r);
+}
+
+int parse_descriptor(const void* data, size_t n, oeqb_plan& p) {
+  const unsigned char* b = static_cast<const unsigned char*>(data);
+  if (n < 16 * 8) return fail(OEQB_ERR_INVALID, "descriptor too short");
+  int64_t h[16];
+  std::memcpy(h, b, sizeof(h));
+  if (h[0] != kMagic || h[1] != 1) return fail(OEQB_ERR_INVALID, "bad descriptor magic/version");
+  p.dtype = static_cast<int>(h[2]);
+  p.layout = static_cast<int>(h[3]);
+  p.uvw = static_cast<int>(h[4]);
+  p.shared_w = static_cast<int>(h[5]);
+  p.n1 = static_cast<int>(h[6]);
+  p.n2 = static_cast<int>(h[7]);
+  p.n3 = static_cast<int>(h[8]);
+  p.nins = static_cast<int>(h[9]);
+  p.L1dim = static_cast<int>(h[10]);
+  p.L2dim = static_cast<int>(h[11]);
+  p.L3dim = static_cast<int>(h[12]);
+  p.wnumel = static_cast<int>(h[13]);
+  const int64_t ncg = h[14];
+  p.det = static_cast<int>(h[15] & 1);
+  p.kahan = static_cast<int>((h[15] >> 1) & 1);
+  if (p.dtype != 1 && p.dtype != 2) return fail(OEQB_ERR_INVALID, "dtype must be f32 or f64");
+  if (p.layout != 0 && p.layout != 1) return fail(OEQB_ERR_INVALID, "bad layout");
+  if (p.uvw && p.layout == 1)
+    return fail(OEQB_ERR_UNSUPPORTED, "layout='ir_mul' is only supported for pure 'uvu' problems");
+  if (p.kahan && p.dtype != 1)
+    return fail(OEQB_ERR_UNSUPPORTED, "Kahan summation requires float32");
+  if (p.n1 < 0 || p.n2 < 0 || p.n3 < 0 || p.nins <= 0 || ncg < 0)
+    return fail(OEQB_ERR_INVALID, "bad descriptor counts");
+  const size_t need = 16 * 8 + size_t(p.n1 + p.n2 + p.n3) * 24 + size_t(p.nins) * 56 +
+                      size_t(ncg) * 32;
+  if (n < need) return fail(OEQB_ERR_INVALID, "descriptor truncated");
+  size_t pos = 16 * 8;
+  auto rd = [&](void* dst, size_t k) {
+    std::memcpy(dst, b + pos, k);
+    pos += k;
+  };
+  auto read_irreps = [&](int cnt, std::vector<IrrepD>& out, int total_dim) -> int {
+    out.resize(cnt);
+    for (int i = 0; i < cnt; ++i) {
+      int64_t t[3];
+      rd(t, sizeof(t));
+      IrrepD r;
+      r.mul = static_cast<int>(t[0]);
+      r.l = static_cast<int>(t[1]);
+      r.dim = 2 * r.l + 1;
+      r.off = static_cast<int>(t[2]);
+      if (r.mul < 0 || r.l < 0 || r.off < 0 || r.off + r.mul * r.dim > total_dim)
+        return fail(OEQB_ERR_INVALID, "irrep out of range");
+      if (r.dim > kDMax)
+        return fail(OEQB_ERR_UNSUPPORTED, "irreps with l > 7 are not supported");
+      if (p.layout == 0) {
+        r.su = r.dim;
+        r.si = 1;
+      } else {
+        r.su = 1;
+        r.si = r.mul;
+      }
+      out[i] = r;
+    }
+    return 0;
+  };
+  if (int rc = read_irreps(p.n1, p.ir1, p.L1dim)) return rc;
+  if (int rc = read_irreps(p.n2, p.ir2, p.L2dim)) return rc;
+  if (int rc = read_irreps(p.n3, p.ir3, p.L3dim)) return rc;
+  std::vector<InstrD> ins(p.nins);
+  for (int i = 0; i < p.nins; ++i) {
+    int64_t t[6];
+    double pw;
+    rd(t, sizeof(t));
+    rd(&pw, sizeof(pw));
+    InstrD in{};
+    in.i1 = static_cast<int>(t[0]);
+    in.i2 = static_cast<int>(t[1]);
+    in.i3 = static_cast<int>(t[2]);
+    if (in.i1 < 0 || in.i1 >= p.n1 || in.i2 < 0 || in.i2 >= p.n2 || in.i3 < 0 || in.i3 >= p.n3)
+      return fail(OEQB_ERR_INVALID, "instruction irrep index out of range");
+    in.woff = static_cast<int>(t[3]);
+    in.cg_off = static_cast<int>(t[4]);
+    in.cg_nnz = static_cast<int>(t[5]);
+    in.pw = pw;
+    in.m1 = p.ir1[in.i1].mul;
+    in.m2 = p.ir2[in.i2].mul;
+    in.m3 = p.ir3[in.i3].mul;
+    in.l1 = p.ir1[in.i1].l;
+    in.l2 = p.ir2[in.i2].l;
+    in.l3 = p.ir3[in.i3].l;
+    in.code = triple_code(in.l1, in.l2, in.l3);
+    if (in.l1 > kLMaxUnrolled || in.l2 > kLMaxUnrolled || in.l3 > kLMaxUnrolled) in.code = -1;
+    if (!p.uvw && in.m1 != in.m3)
+      return fail(OEQB_ERR_INVALID, "uvu instruction needs equal input/output multiplicity");
+    const int64_t wsize = p.uvw ? int64_t(in.m1) * in.m2 * in.m3 : int64_t(in.m1) * in.m2;
+    if (in.woff < 0 || in.woff + wsize > p.wnumel)
+      return fail(OEQB_ERR_INVALID, "instruction weights out of range");
+    if (in.cg_off < 0 || in.cg_nnz < 0 || in.cg_off + in.cg_nnz > ncg)
+      return fail(OEQB_ERR_INVALID, "instruction CG table out of range");
+    ins[i] = in;
+  }
+  p.cg.resize(ncg);
+  const int d1max = 15;
+  for (int64_t i = 0; i < ncg; ++i) {
+    int64_t t[3];
+    double c;
+    rd(t, sizeof(t));
+    rd(&c, sizeof(c));
+    if (t[0] < 0 || t[1] < 0 || t[2] < 0 || t[0] >= d1max || t[1] >= d1max || t[2] >= d1max)
+      return fail(OEQB_ERR_INVALID, "CG entry out of range");
+    p.cg[i] = CGEntry{static_cast<int>(t[0]), static_cast<int>(t[1]), static_cast<int>(t[2]), 0, c};
+  }
+  make_groups(ins, true, p.n3, p.ir3, p.ins_f, p.grp_f, p.zb_f);
+  make_groups(ins, false, p.n1, p.ir1, p.ins_b, p.grp_b, p.zb_b);
+  // Lane-group size: a power of two covering the largest multiplicity a lane indexes.
+  int mmax = 1;
+  for (const InstrD& in : ins) mmax = std::max(mmax, std::max(in.m1, in.m3));
+  int lg = 0;
+  while ((1 << lg) < std::min(mmax, 32)) ++lg;
+  p.lgG = lg;
+  const int rpw = 32 >> lg;
+  // Per-warp scratch layout (elements of T).
+  int off = 32 * kDMax;  // output staging
+  p.off_t = p.off_t2 = p.off_gz = off;
+  if (p.uvw) {
+    p.off_t = off;
+    off += 32 * kDMax;
+    p.off_t2 = off;
+    off += 32 * kDMax;
+    int gz = 0;
+    for (const InstrD& in : ins) gz = std::max(gz, in.m3 * (2 * in.l3 + 1));
+    p.off_gz = off;
+    off += rpw * gz;
+  }
+  p.off_dy = off;
+  off += rpw * p.L2dim;
+  p.ws_elems = (off + 3) & ~3;
+  p.desc_f = desc_bytes(p, p.grp_f.size(), p.zb_f.size());
+  p.desc_b = desc_bytes(p, p.grp_b.size(), p.zb_b.size());
+  return 0;
+}
+
+template <class V>
+size_t put(std::vector<unsigned char>& buf, const std::vector<V>& v) {
+  size_t at = align16(buf.size());
+  buf.resize(at + sizeof(V) * v.size() + 16);
+  if (!v.empty()) std::memcpy(buf.data() + at, v.data(), sizeof(V) * v.size());
+  return at;
+}
+
+int upload(oeqb_plan& p) {
+  std::vector<unsigned char> buf;
+  p.off.ir1 = put(buf, p.ir1);
+  p.off.ir2 = put(buf, p.ir2);
+  p.off.ir3 = put(buf, p.ir3);
+  p.off.ins_f = put(buf, p.ins_f);
+  p.off.grp_f = put(buf, p.grp_f);
+  p.off.zb_f = put(buf, p.zb_f);
+  p.off.ins_b = put(buf, p.ins_b);
+  p.off.grp_b = put(buf, p.grp_b);
+  p.off.zb_b = put(buf, p.zb_b);
+  p.off.cg = put(buf, p.cg);
+  p.off.total = align16(buf.size());
+  buf.resize(p.off.total);
+  OEQB_CUDA(cudaMalloc(&p.dmem, p.off.total));
+  OEQB_CUDA(cudaMemcpy(p.dmem, buf.data(), p.off.total, cudaMemcpyHostToDevice));
+  OEQB_CUDA(cudaMalloc(&p.d_status, sizeof(int)));
+  OEQB_CUDA(cudaMemset(p.d_status, 0, sizeof(int)));
+  return 0;
+}
+
+template <class T>
+Args<T> base_args(const oeqb_plan& p, bool fwd_order) {
+  Args<T> a{};
+  a.ir1 = reinterpret_cast<const IrrepD*>(p.dmem + p.off.ir1);
+  a.ir2 = reinterpret_cast<const IrrepD*>(p.dmem + p.off.ir2);
+  a.ir3 = reinterpret_cast<const IrrepD*>(p.dmem + p.off.ir3);
+  a.ins = reinterpret_cast<const InstrD*>(p.dmem + (fwd_order ? p.off.ins_f : p.off.ins_b));
+  a.grp = reinterpret_cast<const GroupD*>(p.dmem + (fwd_order ? p.off.grp_f : p.off.grp_b));
+  a.zero_blocks = reinterpret_cast<const int*>(p.dmem + (fwd_order ? p.off.zb_f : p.off.zb_b));
+  a.cgtab = reinterpret_cast<const CGEntry*>(p.dmem + p.off.cg);
+  a.n1 = p.n1;
+  a.n2 = p.n2;
+  a.n3 = p.n3;
+  a.nins = p.nins;
+  a.ngrp = static_cast<int>(fwd_order ? p.grp_f.size() : p.grp_b.size());
+  a.nzero = static_cast<int>(fwd_order ? p.zb_f.size() : p.zb_b.size());
+  a.L1dim = p.L1dim;
+  a.L2dim = p.L2dim;
+  a.L3dim = p.L3dim;
+  a.wnumel = p.wnumel;
+  a.shared_w = p.shared_w;
+  a.lgG = p.lgG;
+  a.ws_elems = p.ws_elems;
+  a.off_t = p.off_t;
+  a.off_t2 = p.off_t2;
+  a.off_gz = p.off_gz;
+  a.off_dy = p.off_dy;
+  a.status = p.d_status;
+  return a;
+}
+
+// Raises a kernel's dynamic shared-memory limit to the device maximum, once per
+// (device, kernel), so plans of different sizes never lower each other's limit.
+std::mutex g_attr_mu;
+std::set<std::pair<int, const void*>> g_attr_done;
+
+int allow_max_smem(int device, const void* kernel) {
+  std::lock_guard<std::mutex> g(g_attr_mu);
+  if (g_attr_done.count({device, kernel})) return 0;
+  int optin = 0;
+  OEQB_CUDA(cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, device));
+  int static_bytes = 0;
+  cudaFuncAttributes fa{};
+  OEQB_CUDA(cudaFuncGetAttributes(&fa, kernel));
+  static_bytes = static_cast<int>(fa.sharedSizeBytes);
+  OEQB_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 optin - static_bytes));
+  g_attr_done.insert({device, kernel});
+  return 0;
+}
+
+// Launches `kernel` over `items` work items.  det = segmented kernels (range per warp).
+template <class T>
+int launch(oeqb_plan& p, const void* kernel, const Args<T>& a, bool fwd_order, bool det,
+           cudaStream_t stream) {
+  if (a.nitems <= 0) return 0;
+  const size_t smem = (fwd_order ? p.desc_f : p.desc_b) + size_t(kWarps) * p.ws_elems * sizeof(T);
+  int per_sm;
+  {
+    std::lock_guard<std::mutex> g(p.mu);
+    auto it = p.occ.find(kernel);
+    if (it == p.occ.end()) {
+      if (int rc = allow_max_smem(p.device, kernel)) return rc;
+      int n = 0;
+      OEQB_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kernel, kThreads, smem));
+      if (n <= 0) return fail(OEQB_ERR_UNSUPPORTED, "kernel does not fit on the device");
+      it = p.occ.emplace(kernel, n).first;
+    }
+    per_sm = it->second;
+  }
+  const long long rpw = 32 >> p.lgG;
+  long long blocks;
+  if (!det) {
+    const long long warps = (a.nitems + rpw - 1) / rpw;
+    blocks = (warps + kWarps - 1) / kWarps;
+  } else {
+    // Segmented kernels: at least ~64 positions per warp keeps the snapped ranges useful.
+    blocks = (a.nitems + kWarps * 64 - 1) / (kWarps * 64);
+  }
+  blocks = std::max<long long>(1, std::min<long long>(blocks, (long long)p.sm_count * per_sm));
+  void* params[] = {const_cast<Args<T>*>(&a)};
+  OEQB_CUDA(cudaLaunchKernel(kernel, dim3(static_cast<unsigned>(blocks)), dim3(kThreads), params,
+                             smem, stream));
+  return 0;
+}
+
+struct DeviceGuard {
+  int prev = -1;
+  explicit DeviceGuard(int dev) {
+    cudaGetDevice(&prev);
+    if (prev != dev) cudaSetDevice(dev);
+  }
+  ~DeviceGuard() {
+    int cur = -1;
+    cudaGetDevice(&cur);
+    if (prev >= 0 && cur != prev) cudaSetDevice(prev);
+  }
+};
+
+int check_plan(const oeqb_plan* p) {
+  if (!p) return fail(OEQB_ERR_INVALID, "null plan");
+  return 0;
+}
+
+template <class T>
+int tp_forward_t(oeqb_plan* p, int64_t B, const void* X, const void* Y, const void* W, void* Z,
+                 cudaStream_t s) {
+  Args<T> a = base_args<T>(*p, true);
+  a.nitems = B;
+  a.X = static_cast<const T*>(X);
+  a.Y = static_cast<const T*>(Y);
+  a.W = static_cast<const T*>(W);
+  a.out0 = static_cast<T*>(Z);
+  return launch(*p, batch_kernel_ptr<T>(0, p->uvw, false, kBatch), a, true, false, s);
+}
+
+template <class T>
+int tp_backward_t(oeqb_plan* p, int64_t B, const void* X, void* dX, const void* Y, void* dY,
+                  const void* W, void* dW, const void* dZ, cudaStream_t s) {
+  if (p->shared_w) OEQB_CUDA(cudaMemsetAsync(dW, 0, sizeof(T) * p->wnumel, s));
+  Args<T> a = base_args<T>(*p, false);
+  a.nitems = B;
+  a.X = static_cast<const T*>(X);
+  a.Y = static_cast<const T*>(Y);
+  a.W = static_cast<const T*>(W);
+  a.Gz = static_cast<const T*>(dZ);
+  a.out0 = static_cast<T*>(dX);
+  a.out1 = static_cast<T*>(dY);
+  a.out2 = static_cast<T*>(dW);
+  return launch(*p, batch_kernel_ptr<T>(1, p->uvw, false, kBatch), a, false, false, s);
+}
+
+template <class T>
+int tp_double_backward_t(oeqb_plan* p, int64_t B, const void* X, const void* Y, const void* W,
+                         const void* dZ, const void* ddX, const void* ddY, const void* ddW,
+                         void* gX, void* gY, void* gW, void* gZ, cudaStream_t s) {
+  Args<T> a = base_args<T>(*p, true);
+  a.nitems = B;
+  a.X = static_cast<const T*>(X);
+  a.Y = static_cast<const T*>(Y);
+  a.W = static_cast<const T*>(W);
+  a.dA = static_cast<const T*>(ddX);
+  a.dB = static_cast<const T*>(ddY);
+  a.dC = static_cast<const T*>(ddW);
+  a.out0 = static_cast<T*>(gZ);
+  if (int rc = launch(*p, batch_kernel_ptr<T>(0, p->uvw, true, kBatch), a, true, false, s)) return rc;
+  if (p->shared_w) OEQB_CUDA(cudaMemsetAsync(gW, 0, sizeof(T) * p->wnumel, s));
+  Args<T> b = base_args<T>(*p, false);
+  b.nitems = B;
+  b.X = a.X;
+  b.Y = a.Y;
+  b.W = a.W;
+  b.Gz = static_cast<const T*>(dZ);
+  b.dA = a.dA;
+  b.dB = a.dB;
+  b.dC = a.dC;
+  b.out0 = static_cast<T*>(gX);
+  b.out1 = static_cast<T*>(gY);
+  b.out2 = static_cast<T*>(gW);
+  return launch(*p, batch_kernel_ptr<T>(1, p->uvw, true, kBatch), b, false, false, s);
+}
+
+template <class T>
+int conv_fwd_t(oeqb_plan* p, bool db, const void* X, const void* Y, const void* W, const void* ddX,
+               const void* ddY, const void* ddW, void* Z, const int64_t* rows, const int64_t* cols,
+               int64_t nnz, int64_t nodes, cudaStream_t s) {
+  OEQB_CUDA(cudaMemsetAsync(Z, 0, sizeof(T) * size_t(nodes) * p->L3dim, s));
+  Args<T> a = base_args<T>(*p, true);
+  a.nitems = nnz;
+  a.nnodes = nodes;
+  a.X = static_cast<const T*>(X);
+  a.Y = static_cast<const T*>(Y);
+  a.W = static_cast<const T*>(W);
+  a.dA = static_cast<const T*>(ddX);
+  a.dB = static_cast<const T*>(ddY);
+  a.dC = static_cast<const T*>(ddW);
+  a.out0 = static_cast<T*>(Z);
+  a.rows = reinterpret_cast<const long long*>(rows);
+  a.cols = reinterpret_cast<const long long*>(cols);
+  if (p->det)
+    return launch(*p, det_kernel_ptr<T>(0, p->uvw, db, p->kahan), a, true, true, s);
+  return launch(*p, batch_kernel_ptr<T>(0, p->uvw, db, kConvAtomic), a, true, false, s);
+}
+
+template <class T>
+int conv_bwd_t(oeqb_plan* p, bool db, const void* X, const void* Y, const void* W, const void* dZ,
+               const void* ddX, const void* ddY, const void* ddW, void* gX, void* gY, void* gW,
+               const int64_t* rows, const int64_t* cols, const int64_t* perm, int64_t nnz,
+               int64_t nodes, cudaStream_t s) {
+  OEQB_CUDA(cudaMemsetAsync(gX, 0, sizeof(T) * size_t(nodes) * p->L1dim, s));
+  if (p->det) OEQB_CUDA(cudaMemsetAsync(gY, 0, sizeof(T) * size_t(nnz) * p->L2dim, s));
+  if (p->shared_w) OEQB_CUDA(cudaMemsetAsync(gW, 0, sizeof(T) * p->wnumel, s));
+  Args<T> a = base_args<T>(*p, false);
+  a.nitems = nnz;
+  a.nnodes = nodes;
+  a.X = static_cast<const T*>(X);
+  a.Y = static_cast<const T*>(Y);
+  a.W = static_cast<const T*>(W);
+  a.Gz = static_cast<const T*>(dZ);
+  a.dA = static_cast<const T*>(ddX);
+  a.dB = static_cast<const T*>(ddY);
+  a.dC = static_cast<const T*>(ddW);
+  a.out0 = static_cast<T*>(gX);
+  a.out1 = static_cast<T*>(gY);
+  a.out2 = static_cast<T*>(gW);
+  a.rows = reinterpret_cast<const long long*>(rows);
+  a.cols = reinterpret_cast<const long long*>(cols);
+  a.perm = reinterpret_cast<const long long*>(perm);
+  if (p->det) {
+    if (!perm) return fail(OEQB_ERR_INVALID, "deterministic convolution needs transpose_perm");
+    return launch(*p, det_kernel_ptr<T>(1, p->uvw, db, p->kahan), a, false, true, s);
+  }
+  return launch(*p, batch_kernel_ptr<T>(1, p->uvw, db, kConvAtomic), a, false, false, s);
+}
+
+}  // namespace
+
+// ---------------------------------------------------------------------------------------
+extern "C" {
+
+const char* oeqb_version(void) { return "oeqb200 0.1.0 (sm_100a)"; }
+
+const char* oeqb_last_error(void) { return g_last_error.c_str(); }
+
+int oeqb_plan_create(const void* descriptor, size_t nbytes, int device, oeqb_plan** out) {
+  if (!descriptor || !out) return fail(OEQB_ERR_INVALID, "null argument");
+  *out = nullptr;
+  auto* p = new oeqb_plan();
+  p->device = device;
+  if (int rc = parse_descriptor(descriptor, nbytes, *p)) {
+    delete p;
+    return rc;
+  }
+  DeviceGuard g(device);
+  int sms = 0;
+  if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device) == cudaSuccess && sms > 0)
+    p->sm_count = sms;
+  if (int rc = upload(*p)) {
+    if (p->dmem) cudaFree(p->dmem);
+    if (p->d_status) cudaFree(p->d_status);
+    delete p;
+    return rc;
+  }
+  *out = p;
+  return 0;
+}
+
+int oeqb_plan_destroy(oeqb_plan* p) {
+  if (!p) return 0;
+  {
+    DeviceGuard g(p->device);
+    if (p->dmem) cudaFree(p->dmem);
+    if (p->d_status) cudaFree(p->d_status);
+  }
+  delete p;
+  return 0;
+}
+
+size_t oeqb_conv_workspace_bytes(const oeqb_plan* p, int64_t nnz, int64_t node_count) {
+  (void)p;
+  (void)nnz;
+  (void)node_count;
+  return 0;
+}
+
+int oeqb_plan_check_status(oeqb_plan* p, int* status, void* stream) {
+  if (int rc = check_plan(p)) return rc;
+  DeviceGuard g(p->device);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int h = 0;
+  OEQB_CUDA(cudaMemcpyAsync(&h, p->d_status, sizeof(int), cudaMemcpyDeviceToHost, s));
+  OEQB_CUDA(cudaStreamSynchronize(s));
+  OEQB_CUDA(cudaMemsetAsync(p->d_status, 0, sizeof(int), s));
+  if (status) *status = h;
+  return h ? fail(OEQB_ERR_DEVICE, h == 2 ? "transpose_perm entry out of range"
+                                          : "edge index out of range")
+           : 0;
+}
+
+int oeqb_tp_forward(oeqb_plan* p, int64_t batch, const void* L1_in, const void* L2_in,
+                    const void* W, void* L3_out, void* stream) {
+  if (batch < 0) return fail(OEQB_ERR_INVALID, "negative batch");
+  if (int rc = check_plan(p)) return rc;
+  DeviceGuard g(p->device);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  return p->dtype == 1 ? tp_forward_t<float>(p, batch, L1_in, L2_in, W, L3_out, s)
+                       : tp_forward_t<double>(p, batch, L1_in, L2_in, W, L3_out, s);
+}
+
+int oeqb_tp_backward(oeqb_plan* p, int64_t batch, const void* L1_in, void* L1_grad,
+                     const void* L2_in, void* L2_grad, const void* W, void* W_grad,
+                     const void* L3_grad, void* stream) {
+  if (batch < 0) return fail(OEQB_ERR_INVALID, "negative batch");
+  if (int rc = check_plan(p)) return rc;
+  DeviceGuard g(p->device);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  return p->dtype == 1
+             ? tp_backward_t<float>(p, batch, L1_in, L1_grad, L2_in, L2_grad, W, W_grad, L3_grad, s)
+             : tp_backward_t<double>(p, batch, L1_in, L1_grad, L2_in, L2_grad, W, W_grad, L3_grad, s);
+}
+
+int oeqb_tp_double_backward(oeqb_plan* p, int64_t batch, const void* L1_in, const void* L2_in,
+                            const void* W, const void* L3_grad, const void* L1_dgrad,
+                            const void* L2_dgrad, const void* W_dgrad, void* L1_grad,
+                            void* L2_grad, void* W_grad, void* L3_dgrad, void* stream) {
+  if (batch < 0) return fail(OEQB_ERR_INVALID, "negative batch");
+  if (int rc = check_plan(p)) return rc;
+  DeviceGuard g(p->device);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  return p->dtype == 1
+             ? tp_double_backward_t<float>(p, batch, L1_in, L2_in, W, L3_grad, L1_dgrad, L2_dgrad,
+                                           W_dgrad, L1_grad, L2_grad, W_grad, L3_dgrad, s)
+             : tp_double_backward_t<double>(p, batch, L1_in, L2_in, W, L3_grad, L1_dgrad, L2_dgrad,
+                                            W_dgrad, L1_grad, L2_grad, W_grad, L3_dgrad, s);
+}
+
+int oeqb_conv_forward(oeqb_plan* p, const void* L1_in, const void* L2_in, const void* W,
+                      void* L3_out, const int64_t* rows, const int64_t* cols, int64_t nnz,
+                      int64_t node_count, void* workspace, size_t workspace_bytes, void* stream) {
+  (void)workspace;
+  (void)workspace_bytes;
+  if (nnz < 0 || node_count < 0) return fail(OEQB_ERR_INVALID, "negative size");
+  if (int rc = check_plan(p)) return rc;
+  DeviceGuard g(p->device);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  return p->dtype == 1 ? conv_fwd_t<float>(p, false, L1_in, L2_in, W, nullptr, nullptr, nullptr,
+                                           L3_out, rows, cols, nnz, node_count, s)
+                       : conv_fwd_t<double>(p, false, L1_in, L2_in, W, nullptr, nullptr, nullptr,
+                                            L3_out, rows, cols, nnz, node_count, s);
+}
+
+int oeqb_conv_backward(oeqb_plan* p, const void* L1_in, void* L1_grad, const void* L2_in,
+                       void* L2_grad, const void* W, void* W_grad, const void* L3_grad,
+                       const int64_t* rows, const int64_t* cols, int64_t nnz, int64_t node_count,
+                       void* workspace, size_t workspace_bytes, const int64_t* transpose_perm,
+                       void* stream) {
+  (void)workspace;
+  (void)workspace_bytes;
+  if (nnz < 0 || node_count < 0) return fail(OEQB_ERR_INVALID, "negative size");
+  if (int rc = check_plan(p)) return rc;
+  DeviceGuard g(p->device);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  return p->dtype == 1
+             ? conv_bwd_t<float>(p, false, L1_in, L2_in, W, L3_grad, nullptr, nullptr, nullptr,
+                                 L1_grad, L2_grad, W_grad, rows, cols, transpose_perm, nnz,
+                                 node_count, s)
+             : conv_bwd_t<double>(p, false, L1_in, L2_in, W, L3_grad, nullptr, nullptr, nullptr,
+                                  L1_grad, L2_grad, W_grad, rows, cols, transpose_perm, nnz,
+                                  node_count, s);
+}
+
+int oeqb_conv_double_backward(oeqb_plan* p, const void* L1_in, const void* L2_in, const void* W,
+                              const void* L3_grad, const void* L1_dgrad, const void* L2_dgrad,
+                              const void* W_dgrad, void* L1_grad, void* L2_grad, void* W_grad,
+                              void* L3_dgrad, const int64_t* rows, const int64_t* cols,
+                              int64_t nnz, int64_t node_count, void* workspace,
+                              size_t workspace_bytes, const int64_t* transpose_perm,
+                              void* stream) {
+  (void)workspace;
+  (void)workspace_bytes;
+  if (nnz < 0 || node_count < 0) return fail(OEQB_ERR_INVALID, "negative size");
+  if (int rc = check_plan(p)) return rc;
+  DeviceGuard g(p->device);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (p->dtype == 1) {
+    if (int rc = conv_fwd_t<float>(p, true, L1_in, L2_in, W, L1_dgrad, L2_dgrad, W_dgrad, L3_dgrad,
+                                   rows, cols, nnz, node_count, s))
+      return rc;
+    return conv_bwd_t<float>(p, true, L1_in, L2_in, W, L3_grad, L1_dgrad, L2_dgrad, W_dgrad,
+                             L1_grad, L2_grad, W_grad, rows, cols, transpose_perm, nnz, node_count,
+                             s);
+  }
+  if (int rc = conv_fwd_t<double>(p, true, L1_in, L2_in, W, L1_dgrad, L2_dgrad, W_dgrad, L3_dgrad,
+                                  rows, cols, nnz, node_count, s))
+    return rc;
+  return conv_bwd_t<double>(p, true, L1_in, L2_in, W, L3_grad, L1_dgrad, L2_dgrad, W_dgrad,
+                            L1_grad, L2_grad, W_grad, rows, cols, transpose_perm, nnz, node_count,
+                            s);
+}
+
+}  // extern "C"

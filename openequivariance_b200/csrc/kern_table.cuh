@@ -1,0 +1,40 @@
+// Kernel-pointer tables: each translation unit instantiates one dtype x family so the
+// unrolled kernels compile in parallel.  The host runtime (capi.cu) looks kernels up
+// here and launches them with cudaLaunchKernel.
+#pragma once
+#include "tp_kernels.cuh"
+
+namespace oeqb {
+
+// kind: 0 = forward (or double-backward part A), 1 = backward (or part B)
+template <class T>
+const void* batch_kernel_ptr(int kind, bool uvw, bool db, int policy);
+
+template <class T>
+const void* det_kernel_ptr(int kind, bool uvw, bool db, bool kahan);
+
+#define OEQB_PICK4(K, T, P)                                                     \
+  (uvw ? (db ? (const void*)K<T, true, true, P> : (const void*)K<T, true, false, P>) \
+       : (db ? (const void*)K<T, false, true, P> : (const void*)K<T, false, false, P>))
+
+#define OEQB_DEFINE_BATCH_TABLE(T)                                              \
+  template <>                                                                   \
+  const void* batch_kernel_ptr<T>(int kind, bool uvw, bool db, int policy) {     \
+    if (kind == 0)                                                              \
+      return policy == kBatch ? OEQB_PICK4(tp_fwd_kernel, T, kBatch)            \
+                              : OEQB_PICK4(tp_fwd_kernel, T, kConvAtomic);      \
+    return policy == kBatch ? OEQB_PICK4(tp_bwd_kernel, T, kBatch)              \
+                            : OEQB_PICK4(tp_bwd_kernel, T, kConvAtomic);        \
+  }
+
+#define OEQB_DEFINE_DET_TABLE(T, WITH_KAHAN)                                    \
+  template <>                                                                   \
+  const void* det_kernel_ptr<T>(int kind, bool uvw, bool db, bool kahan) {       \
+    if (WITH_KAHAN && kahan)                                                    \
+      return kind == 0 ? OEQB_PICK4(conv_fwd_det, T, WITH_KAHAN)                \
+                       : OEQB_PICK4(conv_bwd_det, T, WITH_KAHAN);               \
+    return kind == 0 ? OEQB_PICK4(conv_fwd_det, T, false)                       \
+                     : OEQB_PICK4(conv_bwd_det, T, false);                      \
+  }
+
+}  // namespace oeqb

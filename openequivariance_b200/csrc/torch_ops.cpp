@@ -1,0 +1,289 @@
+// Thin libtorch registration of the reference's operator schemas, forwarding to the C ABI
+// of liboeqb200.so.
+//
+// The schemas, the per-argument validation and its error texts ("Shape mismatch for tensor
+// ...", "... is not on the GPU.", "Dtype mismatch for tensor ...") and the output
+// allocation rules follow openequivariance/extension/torch_core.hpp:114-139 and 300-722,
+// so torch fakes, autograd registration, torch.compile and export keep working unchanged.
+// The `json_bytes` argument carries this package's binary problem descriptor; `hash` keys
+// the plan cache (one plan per (hash, device)), as in torch_core.hpp:185-296.
+#include <ATen/ATen.h>
+#include <ATen/Context.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <c10/cuda/CUDAStream.h>
+#include <torch/library.h>
+
+#include <map>
+#include <mutex>
+#include <sstream>
+#include <string>
+#include <tuple>
+#include <utility>
+#include <vector>
+
+#include "oeqb200.h"
+
+namespace {
+
+using at::Tensor;
+
+struct PlanInfo {
+  oeqb_plan* plan = nullptr;
+  int64_t L1_dim = 0, L2_dim = 0, L3_dim = 0, weight_numel = 0;
+  bool shared_weights = false;
+  bool deterministic = false;
+  at::ScalarType dtype = at::kFloat;
+};
+
+std::mutex g_mu;
+std::map<std::pair<int64_t, int>, PlanInfo> g_plans;
+
+std::string sizes_str(at::IntArrayRef s) {
+  std::ostringstream o;
+  o << "[";
+  for (size_t i = 0; i < s.size(); ++i) o << (i ? ", " : "") << s[i];
+  o << "]";
+  return o.str();
+}
+
+void check_tensor(const Tensor& t, std::initializer_list<int64_t> shape, at::ScalarType dtype,
+                  const char* name) {
+  bool ok = t.dim() == static_cast<int64_t>(shape.size());
+  if (ok) {
+    int64_t i = 0;
+    for (int64_t d : shape) {
+      if (t.size(i++) != d) {
+        ok = false;
+        break;
+      }
+    }
+  }
+  TORCH_CHECK(ok, "Shape mismatch for tensor '", name, "'. Expected: ",
+              sizes_str(std::vector<int64_t>(shape)), ". Got: ", sizes_str(t.sizes()));
+  TORCH_CHECK(t.is_cuda(), "Tensor '", name, "' is not on the GPU.");
+  TORCH_CHECK(t.scalar_type() == dtype, "Dtype mismatch for tensor '", name,
+              "'. Expected: ", static_cast<int>(dtype), ". Got: ",
+              static_cast<int>(t.scalar_type()));
+}
+
+const PlanInfo& get_plan(const Tensor& desc, int64_t hash, int device) {
+  std::lock_guard<std::mutex> g(g_mu);
+  auto key = std::make_pair(hash, device);
+  auto it = g_plans.find(key);
+  if (it != g_plans.end()) return it->second;
+  TORCH_CHECK(desc.device().is_cpu() && desc.scalar_type() == at::kByte,
+              "problem descriptor must be a CPU uint8 tensor");
+  Tensor d = desc.contiguous();
+  const auto* h = reinterpret_cast<const int64_t*>(d.data_ptr<uint8_t>());
+  TORCH_CHECK(d.numel() >= 128, "problem descriptor too short");
+  PlanInfo info;
+  int rc = oeqb_plan_create(d.data_ptr<uint8_t>(), static_cast<size_t>(d.numel()), device,
+                            &info.plan);
+  TORCH_CHECK(rc == 0, "oeqb_plan_create failed: ", oeqb_last_error());
+  info.dtype = h[2] == 2 ? at::kDouble : at::kFloat;
+  info.shared_weights = h[5] != 0;
+  info.L1_dim = h[10];
+  info.L2_dim = h[11];
+  info.L3_dim = h[12];
+  info.weight_numel = h[13];
+  info.deterministic = (h[15] & 1) != 0;
+  return g_plans.emplace(key, info).first->second;
+}
+
+void check_rc(int rc) { TORCH_CHECK(rc == 0, "OpenEquivariance-B200 kernel error: ", oeqb_last_error()); }
+
+void* stream_of(const Tensor& t) {
+  return reinterpret_cast<void*>(c10::cuda::getCurrentCUDAStream(t.device().index()).stream());
+}
+
+int tensor_device(const Tensor& t) { return t.is_cuda() ? t.device().index() : 0; }
+
+void check_weights(const PlanInfo& k, const Tensor& W, int64_t rows, const char* name) {
+  if (k.shared_weights)
+    check_tensor(W, {k.weight_numel}, k.dtype, name);
+  else
+    check_tensor(W, {rows, k.weight_numel}, k.dtype, name);
+}
+
+// ----------------------------- batch tensor product -----------------------------------
+
+Tensor jit_tp_forward(Tensor json_bytes, int64_t hash, Tensor L1_in, Tensor L2_in, Tensor W,
+                      int64_t L3_dim) {
+  const PlanInfo& k = get_plan(json_bytes, hash, tensor_device(L1_in));
+  const int64_t B = L1_in.size(0);
+  check_tensor(L1_in, {B, k.L1_dim}, k.dtype, "L1_in");
+  check_tensor(L2_in, {B, k.L2_dim}, k.dtype, "L2_in");
+  check_weights(k, W, B, "W");
+  (void)L3_dim;
+  c10::cuda::CUDAGuard guard(L1_in.device());
+  Tensor L3_out = at::empty({B, k.L3_dim}, L1_in.options());
+  Tensor x = L1_in.contiguous(), y = L2_in.contiguous(), w = W.contiguous();
+  check_rc(oeqb_tp_forward(k.plan, B, x.data_ptr(), y.data_ptr(), w.data_ptr(), L3_out.data_ptr(),
+                           stream_of(L1_in)));
+  return L3_out;
+}
+
+std::tuple<Tensor, Tensor, Tensor> jit_tp_backward(Tensor json_bytes, int64_t hash, Tensor L1_in,
+                                                   Tensor L2_in, Tensor W, Tensor L3_grad) {
+  const PlanInfo& k = get_plan(json_bytes, hash, tensor_device(L1_in));
+  const int64_t B = L1_in.size(0);
+  check_tensor(L1_in, {B, k.L1_dim}, k.dtype, "L1_in");
+  check_tensor(L2_in, {B, k.L2_dim}, k.dtype, "L2_in");
+  check_tensor(L3_grad, {B, k.L3_dim}, k.dtype, "L3_grad");
+  check_weights(k, W, B, "W");
+  c10::cuda::CUDAGuard guard(L1_in.device());
+  Tensor L1_grad = at::empty_like(L1_in, at::MemoryFormat::Contiguous);
+  Tensor L2_grad = at::empty_like(L2_in, at::MemoryFormat::Contiguous);
+  Tensor W_grad = at::empty_like(W, at::MemoryFormat::Contiguous);
+  Tensor x = L1_in.contiguous(), y = L2_in.contiguous(), w = W.contiguous(),
+         gz = L3_grad.contiguous();
+  check_rc(oeqb_tp_backward(k.plan, B, x.data_ptr(), L1_grad.data_ptr(), y.data_ptr(),
+                            L2_grad.data_ptr(), w.data_ptr(), W_grad.data_ptr(), gz.data_ptr(),
+                            stream_of(L1_in)));
+  return {L1_grad, L2_grad, W_grad};
+}
+
+std::tuple<Tensor, Tensor, Tensor, Tensor> jit_tp_double_backward(
+    Tensor json_bytes, int64_t hash, Tensor L1_in, Tensor L2_in, Tensor W, Tensor L3_grad,
+    Tensor L1_dgrad, Tensor L2_dgrad, Tensor W_dgrad) {
+  const PlanInfo& k = get_plan(json_bytes, hash, tensor_device(L1_in));
+  const int64_t B = L1_in.size(0);
+  check_tensor(L1_in, {B, k.L1_dim}, k.dtype, "L1_in");
+  check_tensor(L2_in, {B, k.L2_dim}, k.dtype, "L2_in");
+  check_tensor(L3_grad, {B, k.L3_dim}, k.dtype, "L3_grad");
+  check_tensor(L1_dgrad, {B, k.L1_dim}, k.dtype, "L1_dgrad");
+  check_tensor(L2_dgrad, {B, k.L2_dim}, k.dtype, "L2_dgrad");
+  check_weights(k, W, B, "W");
+  check_weights(k, W_dgrad, B, "W_dgrad");
+  c10::cuda::CUDAGuard guard(L1_in.device());
+  Tensor L1_grad = at::empty_like(L1_in, at::MemoryFormat::Contiguous);
+  Tensor L2_grad = at::empty_like(L2_in, at::MemoryFormat::Contiguous);
+  Tensor W_grad = at::empty_like(W, at::MemoryFormat::Contiguous);
+  Tensor L3_dgrad = at::empty_like(L3_grad, at::MemoryFormat::Contiguous);
+  Tensor x = L1_in.contiguous(), y = L2_in.contiguous(), w = W.contiguous(),
+         gz = L3_grad.contiguous(), dx = L1_dgrad.contiguous(), dy = L2_dgrad.contiguous(),
+         dw = W_dgrad.contiguous();
+  check_rc(oeqb_tp_double_backward(k.plan, B, x.data_ptr(), y.data_ptr(), w.data_ptr(),
+                                   gz.data_ptr(), dx.data_ptr(), dy.data_ptr(), dw.data_ptr(),
+                                   L1_grad.data_ptr(), L2_grad.data_ptr(), W_grad.data_ptr(),
+                                   L3_dgrad.data_ptr(), stream_of(L1_in)));
+  return {L1_grad, L2_grad, W_grad, L3_dgrad};
+}
+
+// ----------------------------------- convolution ---------------------------------------
+
+struct ConvIdx {
+  int64_t nnz, nodes;
+};
+
+ConvIdx check_conv_common(const PlanInfo& k, const Tensor& L1_in, const Tensor& L2_in,
+                          const Tensor& rows, const Tensor& cols, const Tensor& workspace,
+                          const Tensor& transpose_perm, const char* what) {
+  const int64_t nnz = rows.size(0);
+  const int64_t nodes = L1_in.size(0);
+  check_tensor(L1_in, {nodes, k.L1_dim}, k.dtype, "L1_in");
+  check_tensor(L2_in, {nnz, k.L2_dim}, k.dtype, "L2_in");
+  TORCH_CHECK(workspace.dim() == 1, "Shape mismatch for tensor 'workspace'. Expected a 1-D buffer.");
+  TORCH_CHECK(workspace.is_cuda(), "Tensor 'workspace' is not on the GPU.");
+  TORCH_CHECK(workspace.scalar_type() == at::kByte, "Dtype mismatch for tensor 'workspace'.");
+  check_tensor(rows, {nnz}, at::kLong, "rows");
+  check_tensor(cols, {nnz}, at::kLong, "cols");
+  if (k.deterministic)
+    check_tensor(transpose_perm, {nnz}, at::kLong, "transpose perm");
+  else
+    at::globalContext().alertNotDeterministic(what);
+  return {nnz, nodes};
+}
+
+Tensor jit_conv_forward(Tensor json_bytes, int64_t hash, Tensor L1_in, Tensor L2_in, Tensor W,
+                        int64_t L3_dim, Tensor rows, Tensor cols, Tensor workspace,
+                        Tensor transpose_perm) {
+  const PlanInfo& k = get_plan(json_bytes, hash, tensor_device(L1_in));
+  (void)L3_dim;
+  ConvIdx c = check_conv_common(k, L1_in, L2_in, rows, cols, workspace, transpose_perm,
+                                "OpenEquivariance_conv_atomic_forward");
+  check_weights(k, W, c.nnz, "W");
+  c10::cuda::CUDAGuard guard(L1_in.device());
+  Tensor L3_out = at::empty({c.nodes, k.L3_dim}, L1_in.options());
+  Tensor x = L1_in.contiguous(), y = L2_in.contiguous(), w = W.contiguous(),
+         r = rows.contiguous(), cl = cols.contiguous();
+  check_rc(oeqb_conv_forward(k.plan, x.data_ptr(), y.data_ptr(), w.data_ptr(), L3_out.data_ptr(),
+                             r.data_ptr<int64_t>(), cl.data_ptr<int64_t>(), c.nnz, c.nodes,
+                             workspace.data_ptr(), static_cast<size_t>(workspace.numel()),
+                             stream_of(L1_in)));
+  return L3_out;
+}
+
+std::tuple<Tensor, Tensor, Tensor> jit_conv_backward(Tensor json_bytes, int64_t hash,
+                                                     Tensor L1_in, Tensor L2_in, Tensor W,
+                                                     Tensor L3_grad, Tensor rows, Tensor cols,
+                                                     Tensor workspace, Tensor transpose_perm) {
+  const PlanInfo& k = get_plan(json_bytes, hash, tensor_device(L1_in));
+  ConvIdx c = check_conv_common(k, L1_in, L2_in, rows, cols, workspace, transpose_perm,
+                                "OpenEquivariance_conv_atomic_backward");
+  check_tensor(L3_grad, {c.nodes, k.L3_dim}, k.dtype, "L3_grad");
+  check_weights(k, W, c.nnz, "W");
+  c10::cuda::CUDAGuard guard(L1_in.device());
+  Tensor L1_grad = at::empty_like(L1_in, at::MemoryFormat::Contiguous);
+  Tensor L2_grad = at::empty_like(L2_in, at::MemoryFormat::Contiguous);
+  Tensor W_grad = at::empty_like(W, at::MemoryFormat::Contiguous);
+  Tensor x = L1_in.contiguous(), y = L2_in.contiguous(), w = W.contiguous(),
+         gz = L3_grad.contiguous(), r = rows.contiguous(), cl = cols.contiguous();
+  Tensor tp = k.deterministic ? transpose_perm.contiguous() : Tensor();
+  check_rc(oeqb_conv_backward(
+      k.plan, x.data_ptr(), L1_grad.data_ptr(), y.data_ptr(), L2_grad.data_ptr(), w.data_ptr(),
+      W_grad.data_ptr(), gz.data_ptr(), r.data_ptr<int64_t>(), cl.data_ptr<int64_t>(), c.nnz,
+      c.nodes, workspace.data_ptr(), static_cast<size_t>(workspace.numel()),
+      k.deterministic ? tp.data_ptr<int64_t>() : nullptr, stream_of(L1_in)));
+  return {L1_grad, L2_grad, W_grad};
+}
+
+std::tuple<Tensor, Tensor, Tensor, Tensor> jit_conv_double_backward(
+    Tensor json_bytes, int64_t hash, Tensor L1_in, Tensor L2_in, Tensor W, Tensor L3_grad,
+    Tensor L1_dgrad, Tensor L2_dgrad, Tensor W_dgrad, Tensor rows, Tensor cols, Tensor workspace,
+    Tensor transpose_perm) {
+  const PlanInfo& k = get_plan(json_bytes, hash, tensor_device(L1_in));
+  ConvIdx c = check_conv_common(k, L1_in, L2_in, rows, cols, workspace, transpose_perm,
+                                "OpenEquivariance_conv_atomic_double_backward");
+  check_tensor(L3_grad, {c.nodes, k.L3_dim}, k.dtype, "L3_grad");
+  check_tensor(L1_dgrad, {c.nodes, k.L1_dim}, k.dtype, "L1_dgrad");
+  check_tensor(L2_dgrad, {c.nnz, k.L2_dim}, k.dtype, "L2_dgrad");
+  check_weights(k, W, c.nnz, "W");
+  check_weights(k, W_dgrad, c.nnz, "W_dgrad");
+  c10::cuda::CUDAGuard guard(L1_in.device());
+  Tensor L1_grad = at::empty_like(L1_in, at::MemoryFormat::Contiguous);
+  Tensor L2_grad = at::empty_like(L2_in, at::MemoryFormat::Contiguous);
+  Tensor W_grad = at::empty_like(W, at::MemoryFormat::Contiguous);
+  Tensor L3_dgrad = at::empty_like(L3_grad, at::MemoryFormat::Contiguous);
+  Tensor x = L1_in.contiguous(), y = L2_in.contiguous(), w = W.contiguous(),
+         gz = L3_grad.contiguous(), dx = L1_dgrad.contiguous(), dy = L2_dgrad.contiguous(),
+         dw = W_dgrad.contiguous(), r = rows.contiguous(), cl = cols.contiguous();
+  Tensor tp = k.deterministic ? transpose_perm.contiguous() : Tensor();
+  check_rc(oeqb_conv_double_backward(
+      k.plan, x.data_ptr(), y.data_ptr(), w.data_ptr(), gz.data_ptr(), dx.data_ptr(),
+      dy.data_ptr(), dw.data_ptr(), L1_grad.data_ptr(), L2_grad.data_ptr(), W_grad.data_ptr(),
+      L3_dgrad.data_ptr(), r.data_ptr<int64_t>(), cl.data_ptr<int64_t>(), c.nnz, c.nodes,
+      workspace.data_ptr(), static_cast<size_t>(workspace.numel()),
+      k.deterministic ? tp.data_ptr<int64_t>() : nullptr, stream_of(L1_in)));
+  return {L1_grad, L2_grad, W_grad, L3_dgrad};
+}
+
+}  // namespace
+
+TORCH_LIBRARY(libtorch_tp_jit, m) {
+  m.def("jit_tp_forward(Tensor json_bytes, int hash, Tensor L1_in, Tensor L2_in, Tensor W, int L3_dim) -> Tensor");
+  m.def("jit_tp_backward(Tensor json_bytes, int hash, Tensor L1_in, Tensor L2_in, Tensor W, Tensor L3_grad) -> (Tensor, Tensor, Tensor)");
+  m.def("jit_tp_double_backward(Tensor json_bytes, int hash, Tensor L1_in, Tensor L2_in, Tensor W, Tensor L3_grad, Tensor L1_dgrad, Tensor L2_dgrad, Tensor W_dgrad) -> (Tensor, Tensor, Tensor, Tensor)");
+  m.def("jit_conv_forward(Tensor json_bytes, int hash, Tensor L1_in, Tensor L2_in, Tensor W, int L3_dim, Tensor rows, Tensor cols, Tensor workspace, Tensor transpose_perm) -> Tensor");
+  m.def("jit_conv_backward(Tensor json_bytes, int hash, Tensor L1_in, Tensor L2_in, Tensor W, Tensor L3_grad, Tensor rows, Tensor cols, Tensor workspace, Tensor transpose_perm) -> (Tensor, Tensor, Tensor)");
+  m.def("jit_conv_double_backward(Tensor json_bytes, int hash, Tensor L1_in, Tensor L2_in, Tensor W, Tensor L3_grad, Tensor L1_dgrad, Tensor L2_dgrad, Tensor W_dgrad, Tensor rows, Tensor cols, Tensor workspace, Tensor transpose_perm) -> (Tensor, Tensor, Tensor, Tensor)");
+}
+
+TORCH_LIBRARY_IMPL(libtorch_tp_jit, CUDA, m) {
+  m.impl("jit_tp_forward", &jit_tp_forward);
+  m.impl("jit_tp_backward", &jit_tp_backward);
+  m.impl("jit_tp_double_backward", &jit_tp_double_backward);
+  m.impl("jit_conv_forward", &jit_conv_forward);
+  m.impl("jit_conv_backward", &jit_conv_backward);
+  m.impl("jit_conv_double_backward", &jit_conv_double_backward);
+}
