@@ -1,0 +1,384 @@
+#!/usr/bin/env python
+"""Benchmark of the Clebsch-Gordan tensor-product hot path on B200.
+
+Default workload ("C2"): MACE-style batch uvu tensor product,
+X = 128x0e+128x1o+128x2e, Y = real spherical harmonics (l <= 3) of random unit vectors,
+Z = every parity-allowed output up to l = 3 (24 paths), 50,000 rows per GPU, float32,
+forward + backward per step.  A row is the tensor product of one edge, so the metric is
+edges (rows) per second.  With --gpus N every rank processes its own 50,000-row shard
+(weak scaling, no data-path collective: batch rows are independent).
+
+``--workload conv`` measures the fused convolution (config-1 irreps) on the 200,000-node
+radius graph instead (receiver-sorted, deterministic mode), one full graph per GPU.
+
+Timing: W warm-up steps, then K steps between barriers + device syncs, CUDA events on the
+launching stream, max over ranks.  Inputs are larger than L2 (126 MB) so no flush is
+needed.  ``e2e`` repeats the step through the public operator API with pinned host
+buffers, host->device copies of the inputs and device->host copies of every output inside
+the timed region.  ``--impl reference`` times the CPU port of the reference's e3nn path
+(the reference ships no CPU implementation) on the host cores.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "TP & conv fwd+bwd edges/sec at 1/2/4/8 B200; % of HBM/tensor roofline"
+UNIT = "edges/s"
+HBM_FALLBACK_GBS = 6650.0
+
+
+def _args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=["c2", "c2ml", "conv"], default="c2")
+    ap.add_argument("--rows", type=int, default=50000)
+    ap.add_argument("--e2e-steps", type=int, default=3)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def _peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            pk = json.load(f)
+        return float(pk["hbm_gbs"]), "measured"
+    except Exception:
+        return HBM_FALLBACK_GBS, "fallback"
+
+
+def _traffic(kernel_key):
+    """Per-launch DRAM bytes of a kernel from the committed ncu summary, if present."""
+    try:
+        with open(os.path.join(ROOT, "profiles", "ncu_traffic.json")) as f:
+            return json.load(f).get(kernel_key)
+    except Exception:
+        return None
+
+
+class ClockSampler:
+    """Samples nvidia-smi clocks / throttle reasons while the timed region runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index):
+        self.dev = device_index
+        self.lines = []
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100", "-i", str(self.dev)],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except Exception:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        sms, maxes, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sms.append(float(parts[1]))
+                maxes.append(float(parts[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        if not sms:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        sms.sort()
+        return {"sm_mhz": sms[len(sms) // 2], "sm_max_mhz": max(maxes),
+                "reasons": sorted(reasons), "samples": len(sms)}
+
+
+def _dist():
+    import torch
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    else:
+        if torch.cuda.is_available():
+            torch.cuda.set_device(local)
+    return world, rank, local
+
+
+def _barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+def _max_over_ranks(x, world):
+    if world == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def _sh_inputs(rows, lmax, seed, dtype, device):
+    import numpy as np
+    import torch
+
+    from openequivariance_b200.problems import real_spherical_harmonics
+
+    rng = np.random.default_rng(seed)
+    vec = rng.normal(size=(rows, 3))
+    return torch.tensor(real_spherical_harmonics(vec, lmax), dtype=dtype, device=device)
+
+
+# ------------------------------------------------------------------------------ TP workload
+
+
+def bench_tp(args, world, rank, local):
+    import numpy as np
+    import torch
+
+    import openequivariance_b200 as oeq
+    from openequivariance_b200.problems import baseline_problem
+
+    dev = torch.device("cuda", local)
+    problem = baseline_problem(args.workload)
+    tp = oeq.TensorProduct(problem)
+    B = args.rows
+    gen = torch.Generator(device=dev).manual_seed(1234 + rank)
+    X = torch.randn(B, problem.irreps_in1.dim, device=dev, generator=gen)
+    Y = _sh_inputs(B, 3, 99 + rank, torch.float32, dev)
+    W = torch.randn(B, problem.weight_numel, device=dev, generator=gen)
+    G = torch.randn(B, problem.irreps_out.dim, device=dev, generator=gen)
+    ops = torch.ops.libtorch_tp_jit
+
+    def step():
+        Z = ops.jit_tp_forward(tp.kernel, tp.hash, X, Y, W, tp.L3_dim)
+        gX, gY, gW = ops.jit_tp_backward(tp.kernel, tp.hash, X, Y, W, G)
+        return Z, gX, gY, gW
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    K = args.steps
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(K)]
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    _barrier(world)
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clk:
+        start.record()
+        for k in range(K):
+            e = ev[k]
+            e[0].record()
+            Z = ops.jit_tp_forward(tp.kernel, tp.hash, X, Y, W, tp.L3_dim)
+            e[1].record()
+            e[2].record()
+            ops.jit_tp_backward(tp.kernel, tp.hash, X, Y, W, G)
+            e[3].record()
+        end.record()
+        torch.cuda.synchronize()
+    _barrier(world)
+    elapsed_ms = _max_over_ranks(start.elapsed_time(end), world)
+    t_fwd = float(np.mean([e[0].elapsed_time(e[1]) for e in ev]))
+    t_bwd = float(np.mean([e[2].elapsed_time(e[3]) for e in ev]))
+    s = 4
+    d1, d2, d3, wn = (problem.irreps_in1.dim, problem.irreps_in2.dim, problem.irreps_out.dim,
+                      problem.weight_numel)
+    bytes_fwd = B * (d1 + d2 + d3 + wn) * s
+    bytes_bwd = B * (2 * d1 + 2 * d2 + d3 + 2 * wn) * s
+    peak, peak_src = _peaks()
+    dom = ("tp_bwd", bytes_bwd, t_bwd) if t_bwd >= t_fwd else ("tp_fwd", bytes_fwd, t_fwd)
+    achieved = dom[1] / (dom[2] * 1e-3) / 1e9
+    traffic = _traffic(f"{args.workload}:{dom[0]}")
+    rows_total = B * world * K
+    value = rows_total / (elapsed_ms * 1e-3)
+
+    # e2e: through the public module API with pinned host buffers.
+    E = max(1, args.e2e_steps)
+    hX, hY, hW, hG = (t.cpu().pin_memory() for t in (X, Y, W, G))
+    outs_h = [torch.empty(B, d3).pin_memory(), torch.empty(B, d1).pin_memory(),
+              torch.empty(B, d2).pin_memory(), torch.empty(B, wn).pin_memory()]
+
+    def e2e_step():
+        x = hX.to(dev, non_blocking=True).requires_grad_()
+        y = hY.to(dev, non_blocking=True).requires_grad_()
+        w = hW.to(dev, non_blocking=True).requires_grad_()
+        g = hG.to(dev, non_blocking=True)
+        z = tp(x, y, w)
+        z.backward(g)
+        for h, d in zip(outs_h, (z.detach(), x.grad, y.grad, w.grad)):
+            h.copy_(d, non_blocking=True)
+
+    e2e_step()
+    torch.cuda.synchronize()
+    _barrier(world)
+    t0 = time.perf_counter()
+    for _ in range(E):
+        e2e_step()
+    torch.cuda.synchronize()
+    e2e_s = _max_over_ranks(time.perf_counter() - t0, world)
+    h2d = (hX.numel() + hY.numel() + hW.numel() + hG.numel()) * s
+    d2h = sum(h.numel() for h in outs_h) * s
+    e2e = {"value": B * world * E / e2e_s, "unit": UNIT, "h2d_bytes_per_step": h2d,
+           "d2h_bytes_per_step": d2h, "steps": E,
+           "path": "oeq.TensorProduct forward+backward (torch op API), pinned host buffers"}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline_tp(problem, budget_s=15.0)
+
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": K,
+        "warmup": args.warmup, "ms_per_step": elapsed_ms / K, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": f"{args.workload}: batch uvu CG tensor product fwd+bwd "
+                               f"({len(problem.instructions)} paths, X={problem.irreps_in1}, "
+                               f"Y=SH l<=3, L3_dim={d3})",
+                   "rows_per_gpu": B, "global_rows": B * world,
+                   "l2": "inputs larger than L2 (no flush needed)",
+                   "parallelism": f"dp{world} (independent row shards)"},
+        "kernels_ms": {"tp_fwd": t_fwd, "tp_bwd": t_bwd},
+        "roofline": {"bound": "hbm", "kernel": dom[0], "achieved": achieved, "peak": peak,
+                     "peak_source": peak_src, "unit": "GB/s", "frac": achieved / peak,
+                     "traffic": traffic, "algorithmic_bytes_per_launch": dom[1],
+                     "fwd_frac": bytes_fwd / (t_fwd * 1e-3) / 1e9 / peak,
+                     "bwd_frac": bytes_bwd / (t_bwd * 1e-3) / 1e9 / peak},
+        "e2e": e2e,
+        "gpu_launches": 2 * K,
+        "clocks": clk.summary(),
+    }
+    if cpu is not None:
+        line["cpu_baseline"] = cpu
+    return line
+
+
+def cpu_baseline_tp(problem, budget_s=15.0, rows=None):
+    """Times the CPU port on a bounded sample of the same workload."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import cpu_baseline as CB
+    import tp_oracle as O
+
+    p = O.Problem(
+        [(m.mul, m.ir.l, m.ir.p) for m in problem.irreps_in1],
+        [(m.mul, m.ir.l, m.ir.p) for m in problem.irreps_in2],
+        [(m.mul, m.ir.l, m.ir.p) for m in problem.irreps_out],
+        [(i.i_in1, i.i_in2, i.i_out, i.connection_mode, True) for i in problem.instructions],
+        shared_weights=problem.shared_weights)
+    n = rows or 256
+    t, threads = CB.time_tp_fwd_bwd(p, n)
+    while rows is None and t < budget_s / 8 and n < 50000:
+        n *= 2
+        t, threads = CB.time_tp_fwd_bwd(p, n)
+    return {"value": n / t, "unit": UNIT, "cores": threads, "kind": "port",
+            "sample": f"{n} rows of the same workload, forward+backward, float32 torch-CPU "
+                      f"einsums ({t:.2f} s)"}
+
+
+# ----------------------------------------------------------------------------- reference
+
+
+def bench_reference(args, world, rank):
+    if rank != 0:
+        return None
+    from openequivariance_b200.problems import baseline_problem
+
+    problem = baseline_problem(args.workload if args.workload != "conv" else "c1")
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import cpu_baseline as CB
+    import tp_oracle as O
+
+    p = O.Problem(
+        [(m.mul, m.ir.l, m.ir.p) for m in problem.irreps_in1],
+        [(m.mul, m.ir.l, m.ir.p) for m in problem.irreps_in2],
+        [(m.mul, m.ir.l, m.ir.p) for m in problem.irreps_out],
+        [(i.i_in1, i.i_in2, i.i_out, i.connection_mode, True) for i in problem.instructions],
+        shared_weights=problem.shared_weights)
+    rows = 2048
+    for _ in range(args.warmup):
+        CB.time_tp_fwd_bwd(p, 128)
+    times = []
+    threads = None
+    for _ in range(args.steps):
+        t, threads = CB.time_tp_fwd_bwd(p, rows)
+        times.append(t)
+    total = sum(times)
+    value = rows * args.steps / total
+    return {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": 1e3 * total / args.steps, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "impl": "reference",
+        "config": {"workload": f"{args.workload}: batch uvu CG tensor product fwd+bwd "
+                               "(CPU port of the reference's e3nn path)",
+                   "rows_per_step": rows},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
+                         "sample": f"{rows} rows per step, forward+backward, float32"},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+
+
+def main():
+    args = _args()
+    world, rank, local = _dist()
+    if args.impl == "reference":
+        line = bench_reference(args, world, rank)
+    elif args.workload == "conv":
+        from bench_conv import bench_conv  # noqa: F401  (conv workload module)
+
+        line = bench_conv(args, world, rank, local)
+    else:
+        line = bench_tp(args, world, rank, local)
+    if rank == 0 and line is not None:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()
