@@ -20,12 +20,15 @@
 
 #include "oeqb200.h"
 #include "tp_core.cuh"
+#include "tp_kernels_row.cuh"
 
 namespace oeqb {
 template <class T>
 const void* batch_kernel_ptr(int kind, bool uvw, bool db, int policy);
 template <class T>
 const void* det_kernel_ptr(int kind, bool uvw, bool db, bool kahan);
+template <class T>
+const void* row_kernel_ptr(int kind, int nwarps);
 }  // namespace oeqb
 
 using namespace oeqb;
@@ -78,6 +81,14 @@ struct oeqb_plan {
   std::vector<GroupD> grp_f, grp_b;
   std::vector<int> zb_f, zb_b;
   std::vector<CGEntry> cg;
+  // Row-staged wide-uvu batch kernels (tp_kernels_row.cuh): items, per-warp lists.
+  struct RowTable {
+    std::vector<RowItem> items;
+    std::vector<int> witems, wofs;
+    int nwarps = 8;
+    size_t off_items = 0, off_witems = 0, off_wofs = 0;
+  } rowf, rowb;
+  bool row_ok = false;
   DevArrays off{};
   unsigned char* dmem = nullptr;
   int* d_status = nullptr;
@@ -121,6 +132,90 @@ void make_groups(const std::vector<InstrD>& ins, bool by_out, int nirreps,
   zero_blocks.clear();
   for (int r = 0; r < nirreps; ++r)
     if (!used[r] && irreps[r].mul > 0) zero_blocks.push_back(r);
+}
+
+// Lockstep assignment: every item is one 32-lane chunk, items keep their instruction order
+// and are dealt round-robin, so at any moment the warps of a CTA execute the code of the
+// same one or two degree triples (the unrolled kernels are large; warps running different
+// triples at once thrash the instruction cache).
+void schedule_items(oeqb_plan::RowTable& t, const std::vector<double>& /*cost*/) {
+  std::vector<RowItem> single;
+  for (const RowItem& it : t.items)
+    for (int c = it.c0; c < it.c0 + it.nc; ++c) single.push_back(RowItem{it.key, c, 1, 0});
+  t.items = single;
+  const int nw = t.nwarps;
+  t.witems.clear();
+  t.wofs.assign(1, 0);
+  for (int w = 0; w < nw; ++w) {
+    for (size_t i = w; i < t.items.size(); i += nw) t.witems.push_back(static_cast<int>(i));
+    t.wofs.push_back(static_cast<int>(t.witems.size()));
+  }
+}
+
+size_t round_elems(size_t n, size_t elem) {
+  const size_t q = 16 / elem;
+  return (n + q - 1) / q * q;
+}
+
+// Shared-memory bytes of a row kernel launch (must match stage_desc_row / the kernels).
+size_t row_smem(const oeqb_plan& p, int kind, int nwarps, size_t elem, int* row_elems,
+                int* offY, int* offW, int* offG, int* ws_elems) {
+  const auto& t = kind == 0 ? p.rowf : p.rowb;
+  const size_t desc = p.desc_f;  // both row kernels stage the forward-order tables
+  const size_t tabs = align16(sizeof(RowItem) * t.items.size() + sizeof(int) * t.witems.size() +
+                              sizeof(int) * (nwarps + 1));
+  *offY = static_cast<int>(round_elems(p.L1dim, elem));
+  *offW = *offY + static_cast<int>(round_elems(p.L2dim, elem));
+  *offG = *offW + static_cast<int>(p.shared_w ? 0 : round_elems(p.wnumel, elem));
+  *row_elems = *offG + static_cast<int>(kind == 1 ? round_elems(p.L3dim, elem) : 0);
+  if (kind == 0)
+    *ws_elems = 2 * 32 * kDMax;
+  else
+    *ws_elems = static_cast<int>(round_elems(p.L1dim, elem) + round_elems(p.L2dim, elem));
+  return desc + tabs + 16 + 2 * elem * size_t(*row_elems) + size_t(nwarps) * (*ws_elems) * elem;
+}
+
+// The row kernels cover uvu problems with a 32-lane group whose degrees are all in the
+// unrolled range and whose rows fit in shared memory; everything else runs on the v1
+// kernels.
+void build_row(oeqb_plan& p) {
+  p.row_ok = false;
+  if (p.uvw || p.lgG != 5) return;
+  for (const InstrD& in : p.ins_f)
+    if (in.code < 0) return;
+  for (const IrrepD& r : p.ir3)
+    if (r.l > kLMaxUnrolled) return;
+  auto nnz = [&](const InstrD& in) { return static_cast<double>(in.cg_nnz); };
+  p.rowf = {};
+  p.rowb = {};
+  std::vector<double> cf, cb;
+  for (size_t g = 0; g < p.grp_f.size(); ++g) {
+    const GroupD& gd = p.grp_f[g];
+    const IrrepD& r3 = p.ir3[gd.irrep];
+    double c = 2.0 * r3.dim;
+    for (int i = gd.first; i < gd.first + gd.count; ++i)
+      c += p.ins_f[i].m2 * (2.0 * nnz(p.ins_f[i]) + p.ir2[p.ins_f[i].i2].dim) + p.ir1[p.ins_f[i].i1].dim;
+    p.rowf.items.push_back(RowItem{static_cast<int>(g), 0, (r3.mul + 31) / 32, 0});
+    cf.push_back(c);
+  }
+  for (size_t i = 0; i < p.ins_f.size(); ++i) {
+    const InstrD& in = p.ins_f[i];
+    const double c = in.m2 * (4.0 * nnz(in) + 3.0 * p.ir1[in.i1].dim + p.ir2[in.i2].dim) +
+                     p.ir3[in.i3].dim;
+    p.rowb.items.push_back(RowItem{static_cast<int>(i), 0, (in.m1 + 31) / 32, 0});
+    cb.push_back(c);
+  }
+  const size_t elem = p.dtype == 2 ? 8 : 4;
+  const size_t budget = 220 * 1024;
+  int re, oy, ow, og, we;
+  p.rowf.nwarps = 8;
+  schedule_items(p.rowf, cf);
+  if (row_smem(p, 0, 8, elem, &re, &oy, &ow, &og, &we) > budget) return;
+  p.rowb.nwarps = 16;
+  if (row_smem(p, 1, 16, elem, &re, &oy, &ow, &og, &we) > budget) p.rowb.nwarps = 8;
+  schedule_items(p.rowb, cb);
+  if (row_smem(p, 1, p.rowb.nwarps, elem, &re, &oy, &ow, &og, &we) > budget) return;
+  p.row_ok = true;
 }
 
 int parse_descriptor(const void* data, size_t n, oeqb_plan& p) {
@@ -259,6 +354,7 @@ int parse_descriptor(const void* data, size_t n, oeqb_plan& p) {
   p.ws_elems = (off + 3) & ~3;
   p.desc_f = desc_bytes(p, p.grp_f.size(), p.zb_f.size());
   p.desc_b = desc_bytes(p, p.grp_b.size(), p.zb_b.size());
+  build_row(p);
   return 0;
 }
 
@@ -282,6 +378,11 @@ int upload(oeqb_plan& p) {
   p.off.grp_b = put(buf, p.grp_b);
   p.off.zb_b = put(buf, p.zb_b);
   p.off.cg = put(buf, p.cg);
+  for (auto* t : {&p.rowf, &p.rowb}) {
+    t->off_items = put(buf, t->items);
+    t->off_witems = put(buf, t->witems);
+    t->off_wofs = put(buf, t->wofs);
+  }
   p.off.total = align16(buf.size());
   buf.resize(p.off.total);
   OEQB_CUDA(cudaMalloc(&p.dmem, p.off.total));
@@ -377,6 +478,61 @@ int launch(oeqb_plan& p, const void* kernel, const Args<T>& a, bool fwd_order, b
   return 0;
 }
 
+bool aligned16(const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15) == 0; }
+
+template <class T>
+int launch_row(oeqb_plan& p, int kind, const Args<T>& a, cudaStream_t stream) {
+  if (a.nitems <= 0) return 0;
+  const auto& t = kind == 0 ? p.rowf : p.rowb;
+  ArgsRow<T> v;
+  v.a = a;
+  // Row items index the forward-order instruction table (and the forward groups).
+  v.a.ins = reinterpret_cast<const InstrD*>(p.dmem + p.off.ins_f);
+  v.a.grp = reinterpret_cast<const GroupD*>(p.dmem + p.off.grp_f);
+  v.a.zero_blocks = reinterpret_cast<const int*>(p.dmem + p.off.zb_f);
+  v.a.ngrp = static_cast<int>(p.grp_f.size());
+  v.a.nzero = static_cast<int>(p.zb_f.size());
+  v.items = reinterpret_cast<const RowItem*>(p.dmem + t.off_items);
+  v.witems = reinterpret_cast<const int*>(p.dmem + t.off_witems);
+  v.wofs = reinterpret_cast<const int*>(p.dmem + t.off_wofs);
+  v.nitems = static_cast<int>(t.items.size());
+  v.nwitems = static_cast<int>(t.witems.size());
+  v.nwarps = t.nwarps;
+  const size_t elem = sizeof(T);
+  const size_t smem = row_smem(p, kind, t.nwarps, elem, &v.row_elems, &v.offY, &v.offW, &v.offG,
+                               &v.ws_elems);
+  v.off_stage = 0;
+  v.off_dxp = 0;
+  v.off_dyp = static_cast<int>(round_elems(p.L1dim, elem));
+  // Bulk (TMA) copies need 16-byte aligned rows: every base pointer and row length.
+  bool tma = aligned16(a.X) && aligned16(a.Y) && (p.L1dim * elem) % 16 == 0 &&
+             (p.L2dim * elem) % 16 == 0;
+  if (!p.shared_w) tma = tma && aligned16(a.W) && (p.wnumel * elem) % 16 == 0;
+  if (kind == 1) tma = tma && aligned16(a.Gz) && (p.L3dim * elem) % 16 == 0;
+  v.use_tma = tma ? 1 : 0;
+  const void* kernel = row_kernel_ptr<T>(kind, t.nwarps);
+  const int threads = 32 * t.nwarps;
+  int per_sm;
+  {
+    std::lock_guard<std::mutex> g(p.mu);
+    auto it = p.occ.find(kernel);
+    if (it == p.occ.end()) {
+      if (int rc = allow_max_smem(p.device, kernel)) return rc;
+      int n = 0;
+      OEQB_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kernel, threads, smem));
+      if (n <= 0) return fail(OEQB_ERR_UNSUPPORTED, "row kernel does not fit on the device");
+      it = p.occ.emplace(kernel, n).first;
+    }
+    per_sm = it->second;
+  }
+  long long blocks = std::min<long long>(a.nitems, (long long)p.sm_count * per_sm);
+  blocks = std::max<long long>(1, blocks);
+  void* params[] = {&v};
+  OEQB_CUDA(cudaLaunchKernel(kernel, dim3(static_cast<unsigned>(blocks)), dim3(threads), params,
+                             smem, stream));
+  return 0;
+}
+
 struct DeviceGuard {
   int prev = -1;
   explicit DeviceGuard(int dev) {
@@ -404,6 +560,7 @@ int tp_forward_t(oeqb_plan* p, int64_t B, const void* X, const void* Y, const vo
   a.Y = static_cast<const T*>(Y);
   a.W = static_cast<const T*>(W);
   a.out0 = static_cast<T*>(Z);
+  if (p->row_ok) return launch_row(*p, 0, a, s);
   return launch(*p, batch_kernel_ptr<T>(0, p->uvw, false, kBatch), a, true, false, s);
 }
 
@@ -420,6 +577,7 @@ int tp_backward_t(oeqb_plan* p, int64_t B, const void* X, void* dX, const void* 
   a.out0 = static_cast<T*>(dX);
   a.out1 = static_cast<T*>(dY);
   a.out2 = static_cast<T*>(dW);
+  if (p->row_ok) return launch_row(*p, 1, a, s);
   return launch(*p, batch_kernel_ptr<T>(1, p->uvw, false, kBatch), a, false, false, s);
 }
 

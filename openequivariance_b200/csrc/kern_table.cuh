@@ -3,6 +3,7 @@
 // here and launches them with cudaLaunchKernel.
 #pragma once
 #include "tp_kernels.cuh"
+#include "tp_kernels_row.cuh"
 
 namespace oeqb {
 
@@ -12,6 +13,10 @@ const void* batch_kernel_ptr(int kind, bool uvw, bool db, int policy);
 
 template <class T>
 const void* det_kernel_ptr(int kind, bool uvw, bool db, bool kahan);
+
+// Row-staged wide-uvu batch kernels (tp_kernels_row.cuh); kind 0 = forward, 1 = backward.
+template <class T>
+const void* row_kernel_ptr(int kind, int nwarps);
 
 #define OEQB_PICK4(K, T, P)                                                     \
   (uvw ? (db ? (const void*)K<T, true, true, P> : (const void*)K<T, true, false, P>) \
@@ -25,6 +30,13 @@ const void* det_kernel_ptr(int kind, bool uvw, bool db, bool kahan);
                               : OEQB_PICK4(tp_fwd_kernel, T, kConvAtomic);      \
     return policy == kBatch ? OEQB_PICK4(tp_bwd_kernel, T, kBatch)              \
                             : OEQB_PICK4(tp_bwd_kernel, T, kConvAtomic);        \
+  }
+
+#define OEQB_DEFINE_ROW_TABLE(T)                                                \
+  template <>                                                                   \
+  const void* row_kernel_ptr<T>(int kind, int nwarps) {                          \
+    if (kind == 0) return (const void*)tp_fwd_row<T, 8>;                          \
+    return nwarps == 16 ? (const void*)tp_bwd_row<T, 16> : (const void*)tp_bwd_row<T, 8>; \
   }
 
 #define OEQB_DEFINE_DET_TABLE(T, WITH_KAHAN)                                    \

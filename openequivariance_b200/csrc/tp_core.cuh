@@ -196,18 +196,20 @@ struct RowPtrs {
 // ---------------------------------------------------------------------------
 // uvu, forward (and double-backward part A): z[D3] accumulates output index u.
 
+// wblk: this chunk's weight block, indexed v*ul + (u - u0) (ul = chunk width, u0 = start).
 template <class T, int A, int B, int C, bool DB>
 __device__ __forceinline__ void uvu_fwd(const InstrD& in, const IrrepD& r1, const IrrepD& r2,
-                                        const RowPtrs<T>& rp, int u, T* z) {
+                                        const RowPtrs<T>& rp, const T* wblk, int u, T* z) {
   constexpr int D1 = 2 * A + 1, D2 = 2 * B + 1;
   T x[D1];
   ldv(x, rp.x, r1, u);
   T xa[DB ? D1 : 1];
   if constexpr (DB) ldv(xa, rp.a, r1, u);
   const T pw = T(in.pw);
+  const int u0 = u & ~31, ul = min(32, in.m1 - u0);
   for (int v = 0; v < in.m2; ++v) {
     const int wi = in.woff + widx_uvu(in.m1, in.m2, u, v);
-    const T wp = rp.w[wi] * pw;
+    const T wp = wblk[v * ul + (u - u0)] * pw;
     T y[D2];
     ldv(y, rp.y, r2, v);
     if constexpr (!DB) {
@@ -271,12 +273,14 @@ struct BwdOut {
   T* dy_row;   // per-warp smem staging for this item's dY (length L2dim)
   T* dw;       // dW row (global)
   bool shared_w;
+  int dy_shift = 0;  // real irrep offset minus the offset of the (staged) view used to read Y
 };
 
 template <class T, int A, int B, int C, bool DB>
 __device__ __forceinline__ void uvu_bwd(const InstrD& in, const IrrepD& r1, const IrrepD& r2,
-                                        const IrrepD& r3, const RowPtrs<T>& rp, int u, bool act,
-                                        const Lane<T>& L, T* gx, const BwdOut<T>& bo) {
+                                        const IrrepD& r3, const RowPtrs<T>& rp, const T* wblk,
+                                        int u, bool act, const Lane<T>& L, T* gx,
+                                        const BwdOut<T>& bo) {
   constexpr int D1 = 2 * A + 1, D2 = 2 * B + 1, D3 = 2 * C + 1;
   T x[D1], gz[D3];
   T xa[DB ? D1 : 1];
@@ -286,32 +290,46 @@ __device__ __forceinline__ void uvu_bwd(const InstrD& in, const IrrepD& r1, cons
     if constexpr (DB) ldv(xa, rp.a, r1, u);
   }
   const T pw = T(in.pw);
+  const int u0 = u & ~31, ul = min(32, in.m1 - u0);
   for (int v = 0; v < in.m2; ++v) {
     T gy[D2];
     zero(gy);
     if (act) {
       const int wi = in.woff + widx_uvu(in.m1, in.m2, u, v);
-      const T wp = rp.w[wi] * pw;
+      const T wp = wblk[v * ul + (u - u0)] * pw;
       T y[D2];
       ldv(y, rp.y, r2, v);
-      T s;
+      T s = T(0);
       if constexpr (!DB) {
-        T p[D1], q[D2];
+        // h_i = sum c gz_k y_j:  dX_i += w h_i,  dW = sum_i x_i h_i;  e_j = sum c gz_k x_i.
+        T h[D1];
+        CG<A, B, C>::hvec(gz, y, h);
 #pragma unroll
-        for (int i = 0; i < D1; ++i) p[i] = wp * x[i];
+        for (int i = 0; i < D1; ++i) {
+          gx[i] += wp * h[i];
+          s += x[i] * h[i];
+        }
+        T e[D2];
+        CG<A, B, C>::evec(gz, x, e);
 #pragma unroll
-        for (int j = 0; j < D2; ++j) q[j] = wp * y[j];
-        s = CG<A, B, C>::template bwd1<T>(p, q, gz, gx, gy, x, y);
+        for (int j = 0; j < D2; ++j) gy[j] = wp * e[j];
       } else {
         T yb[D2];
         ldv(yb, rp.b, r2, v);
         const T cp = rp.c[wi] * pw;
-        T p[D1], q[D2];
+        T hy[D1], hb[D1];
+        CG<A, B, C>::hvec(gz, y, hy);
+        CG<A, B, C>::hvec(gz, yb, hb);
 #pragma unroll
-        for (int i = 0; i < D1; ++i) p[i] = wp * xa[i] + cp * x[i];
+        for (int i = 0; i < D1; ++i) {
+          gx[i] += wp * hb[i] + cp * hy[i];
+          s += xa[i] * hy[i] + x[i] * hb[i];
+        }
+        T ea[D2], ex[D2];
+        CG<A, B, C>::evec(gz, xa, ea);
+        CG<A, B, C>::evec(gz, x, ex);
 #pragma unroll
-        for (int j = 0; j < D2; ++j) q[j] = wp * yb[j] + cp * y[j];
-        s = CG<A, B, C>::template bwd2<T>(p, q, gz, gx, gy, xa, y, x, yb);
+        for (int j = 0; j < D2; ++j) gy[j] = wp * ea[j] + cp * ex[j];
       }
       if (bo.shared_w)
         atomic_add(bo.dw + wi, s * pw);
@@ -321,7 +339,7 @@ __device__ __forceinline__ void uvu_bwd(const InstrD& in, const IrrepD& r1, cons
 #pragma unroll
     for (int j = 0; j < D2; ++j) {
       const T t = group_sum(gy[j], L.lgG);
-      if (L.gl == 0 && bo.dy_row) bo.dy_row[r2.off + v * r2.su + j * r2.si] += t;
+      if (L.gl == 0 && bo.dy_row) bo.dy_row[r2.off + bo.dy_shift + v * r2.su + j * r2.si] += t;
     }
   }
 }
@@ -543,14 +561,30 @@ __device__ __forceinline__ void uvw_bwd(const InstrD& in, const IrrepD& r1, cons
       }
       T y[D2];
       ldv(y, rp.y, r2, v);
+      T h[D1], e[D2];
       if constexpr (!DB) {
-        CG<A, B, C>::template bwd1<T>(x, y, dtw, gx, gy, x, y);
+        CG<A, B, C>::hvec(dtw, y, h);
+        CG<A, B, C>::evec(dtw, x, e);
+#pragma unroll
+        for (int i = 0; i < D1; ++i) gx[i] += h[i];
+#pragma unroll
+        for (int j = 0; j < D2; ++j) gy[j] += e[j];
         CG<A, B, C>::fwd(x, y, t);
       } else {
         T yb[D2];
         ldv(yb, rp.b, r2, v);
-        CG<A, B, C>::template bwd1<T>(xa, yb, dtw, gx, gy, x, y);
-        CG<A, B, C>::template bwd1<T>(x, y, dtc, gx, gy, x, y);
+        CG<A, B, C>::hvec(dtw, yb, h);
+        CG<A, B, C>::evec(dtw, xa, e);
+#pragma unroll
+        for (int i = 0; i < D1; ++i) gx[i] += h[i];
+#pragma unroll
+        for (int j = 0; j < D2; ++j) gy[j] += e[j];
+        CG<A, B, C>::hvec(dtc, y, h);
+        CG<A, B, C>::evec(dtc, x, e);
+#pragma unroll
+        for (int i = 0; i < D1; ++i) gx[i] += h[i];
+#pragma unroll
+        for (int j = 0; j < D2; ++j) gy[j] += e[j];
         CG<A, B, C>::fwd(xa, y, t);
         CG<A, B, C>::fwd(x, yb, t);
       }

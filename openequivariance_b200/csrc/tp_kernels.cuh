@@ -65,7 +65,8 @@ __device__ __forceinline__ void fwd_chunk(const Args<T>& a, const SmemDesc& d, c
       if (act) {
         if constexpr (L3 >= 0)
           done = dispatch_triple(in.code, [&]<int A, int B, int C>() {
-            if constexpr (C == L3) uvu_fwd<T, A, B, C, DB>(in, r1, r2, rp, wu, z);
+            if constexpr (C == L3)
+              uvu_fwd<T, A, B, C, DB>(in, r1, r2, rp, rp.w + in.woff + (wu & ~31) * in.m2, wu, z);
           });
         if (!done) {
           if (!generic_used) {
@@ -128,7 +129,8 @@ __device__ __forceinline__ void bwd_chunk(const Args<T>& a, const SmemDesc& d, c
       done = dispatch_triple(in.code, [&]<int A, int B, int C>() {
         if constexpr (A == L1) {
           if constexpr (!UVW)
-            uvu_bwd<T, A, B, C, DB>(in, r1, r2, r3, rp, u, act, L, gx, bo);
+            uvu_bwd<T, A, B, C, DB>(in, r1, r2, r3, rp, rp.w + in.woff + (u & ~31) * in.m2, u,
+                                    act, L, gx, bo);
           else
             uvw_bwd<T, A, B, C, DB>(in, r1, r2, r3, rp, rv, cidx, L, ws_t, ws_gz, gx, bo);
         }
