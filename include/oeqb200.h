@@ -116,6 +116,22 @@ int oeqb_conv_double_backward(oeqb_plan* plan, const void* L1_in, const void* L2
                               void* workspace, size_t workspace_bytes,
                               const int64_t* transpose_perm, void* stream);
 
+/* ---- allocation-free batch forward (no counterpart in the reference) ----
+ * Same result as oeqb_plan_create + oeqb_tp_forward, for callers that must not allocate
+ * device memory: code running inside another runtime's memory manager (an XLA/JAX custom
+ * call, an inference server with a fixed arena) or a real-time loop where cudaMalloc's
+ * implicit synchronisation and fragmentation are not acceptable.  The problem tables live
+ * in a static device array of the library (OEQB_NOALLOC_BYTES, loaded on every device
+ * the library is used on and kept until process exit); problems whose tables exceed it are
+ * rejected with OEQB_ERR_UNSUPPORTED.  The first call on a device resolves the array's
+ * address (make that first call outside any stream capture).  All calls on a device share
+ * the array, so calls whose GPU work overlaps race; serialise them (one stream).  Inputs
+ * and outputs are as for oeqb_tp_forward; the descriptor is parsed on every call. */
+#define OEQB_NOALLOC_BYTES 65536
+int oeqb_tp_forward_noalloc(const void* descriptor, size_t nbytes, int device, int64_t batch,
+                            const void* L1_in, const void* L2_in, const void* W, void* L3_out,
+                            void* stream);
+
 #ifdef __cplusplus
 }
 #endif

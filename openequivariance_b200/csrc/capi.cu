@@ -366,8 +366,9 @@ size_t put(std::vector<unsigned char>& buf, const std::vector<V>& v) {
   return at;
 }
 
-int upload(oeqb_plan& p) {
-  std::vector<unsigned char> buf;
+// Lays out every device table of a plan in one host image (offsets recorded in the plan).
+void layout_tables(oeqb_plan& p, std::vector<unsigned char>& buf) {
+  buf.clear();
   p.off.ir1 = put(buf, p.ir1);
   p.off.ir2 = put(buf, p.ir2);
   p.off.ir3 = put(buf, p.ir3);
@@ -385,6 +386,11 @@ int upload(oeqb_plan& p) {
   }
   p.off.total = align16(buf.size());
   buf.resize(p.off.total);
+}
+
+int upload(oeqb_plan& p) {
+  std::vector<unsigned char> buf;
+  layout_tables(p, buf);
   OEQB_CUDA(cudaMalloc(&p.dmem, p.off.total));
   OEQB_CUDA(cudaMemcpy(p.dmem, buf.data(), p.off.total, cudaMemcpyHostToDevice));
   OEQB_CUDA(cudaMalloc(&p.d_status, sizeof(int)));
@@ -667,6 +673,34 @@ int conv_bwd_t(oeqb_plan* p, bool db, const void* X, const void* Y, const void* 
 }  // namespace
 
 // ---------------------------------------------------------------------------------------
+// Allocation-free forward (oeqb_tp_forward_noalloc).  The problem tables and the status
+// flag live in this file-scope device array instead of plan memory, so the call needs no
+// device allocation.  Every call on a device shares the array and leaves its contents
+// behind; calls whose GPU work overlaps (e.g. on two streams) race on it.
+constexpr size_t kNoAllocBytes = 64 * 1024;
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocBytes];
+
+namespace {
+std::mutex g_noalloc_mu;
+constexpr int kMaxDevices = 64;
+unsigned char* g_noalloc_addr[kMaxDevices] = {};
+
+// Device address of the array on `device` (which must be current); resolved once per device.
+int noalloc_base(int device, unsigned char** out) {
+  std::lock_guard<std::mutex> g(g_noalloc_mu);
+  if (device < 0 || device >= kMaxDevices) return fail(OEQB_ERR_INVALID, "device index out of range");
+  if (!g_noalloc_addr[device]) {
+    void* ptr = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+    if (e != cudaSuccess || !ptr)
+      return fail(OEQB_ERR_CUDA, std::string("cudaGetSymbolAddress failed: ") + cudaGetErrorString(e));
+    g_noalloc_addr[device] = static_cast<unsigned char*>(ptr);
+  }
+  *out = g_noalloc_addr[device];
+  return 0;
+}
+}  // namespace
+
 extern "C" {
 
 const char* oeqb_version(void) { return "oeqb200 0.1.0 (sm_100a)"; }
@@ -827,6 +861,42 @@ int oeqb_conv_double_backward(oeqb_plan* p, const void* L1_in, const void* L2_in
   return conv_bwd_t<double>(p, true, L1_in, L2_in, W, L3_grad, L1_dgrad, L2_dgrad, W_dgrad,
                             L1_grad, L2_grad, W_grad, rows, cols, transpose_perm, nnz, node_count,
                             s);
+}
+
+int oeqb_tp_forward_noalloc(const void* descriptor, size_t nbytes, int device, int64_t batch,
+                            const void* L1_in, const void* L2_in, const void* W, void* L3_out,
+                            void* stream) {
+  if (!descriptor) return fail(OEQB_ERR_INVALID, "null descriptor");
+  if (batch < 0) return fail(OEQB_ERR_INVALID, "negative batch");
+  oeqb_plan p;
+  p.device = device;
+  if (int rc = parse_descriptor(descriptor, nbytes, p)) return rc;
+  p.row_ok = false;  // this entry point runs the table-driven forward kernel
+  std::vector<unsigned char> img;
+  layout_tables(p, img);
+  const size_t status_off = align16(img.size());
+  const size_t need = status_off + 16;
+  if (need > kNoAllocBytes)
+    return fail(OEQB_ERR_UNSUPPORTED,
+                "problem tables need " + std::to_string(need) +
+                    " bytes; the allocation-free entry point holds at most " +
+                    std::to_string(kNoAllocBytes) + " bytes (use a plan instead)");
+  DeviceGuard g(device);
+  unsigned char* base = nullptr;
+  if (int rc = noalloc_base(device, &base)) return rc;
+  int sms = 0;
+  if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device) == cudaSuccess && sms > 0)
+    p.sm_count = sms;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  p.dmem = base;
+  p.d_status = reinterpret_cast<int*>(base + status_off);
+  OEQB_CUDA(cudaMemcpyAsync(base, img.data(), img.size(), cudaMemcpyHostToDevice, s));
+  OEQB_CUDA(cudaMemsetAsync(p.d_status, 0, sizeof(int), s));
+  const int rc = p.dtype == 1 ? tp_forward_t<float>(&p, batch, L1_in, L2_in, W, L3_out, s)
+                              : tp_forward_t<double>(&p, batch, L1_in, L2_in, W, L3_out, s);
+  p.dmem = nullptr;  // not owned
+  p.d_status = nullptr;
+  return rc;
 }
 
 }  // extern "C"
