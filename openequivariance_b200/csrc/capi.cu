@@ -20,7 +20,7 @@
 
 #include "oeqb200.h"
 #include "tp_core.cuh"
-#include "tp_kernels_row.cuh"
+#include "tp_kernels_cw.cuh"
 
 namespace oeqb {
 template <class T>
@@ -29,6 +29,8 @@ template <class T>
 const void* det_kernel_ptr(int kind, bool uvw, bool db, bool kahan);
 template <class T>
 const void* row_kernel_ptr(int kind, int nwarps);
+template <class T>
+const void* cw_kernel_ptr(int kind);
 }  // namespace oeqb
 
 using namespace oeqb;
@@ -89,6 +91,10 @@ struct oeqb_plan {
     size_t off_items = 0, off_witems = 0, off_wofs = 0;
   } rowf, rowb;
   bool row_ok = false;
+  // Channelwise-uvu kernels (tp_kernels_cw.cuh): one item per (instruction, 32-lane chunk).
+  std::vector<CwItem> cw_items;
+  size_t off_cw = 0;
+  bool cw_ok = false;
   DevArrays off{};
   unsigned char* dmem = nullptr;
   int* d_status = nullptr;
@@ -216,6 +222,50 @@ void build_row(oeqb_plan& p) {
   schedule_items(p.rowb, cb);
   if (row_smem(p, 1, p.rowb.nwarps, elem, &re, &oy, &ow, &og, &we) > budget) return;
   p.row_ok = true;
+}
+
+size_t cw_smem(const oeqb_plan& p, int kind, size_t elem, int* row_elems, int* offY, int* offW,
+               int* offG, int* ws_elems, int* rows_per_buf) {
+  *offY = static_cast<int>(round_elems(p.L1dim, elem));
+  *offW = *offY + static_cast<int>(round_elems(p.L2dim, elem));
+  *offG = *offW + static_cast<int>(p.shared_w ? 0 : round_elems(p.wnumel, elem));
+  *row_elems = *offG + static_cast<int>(kind == 1 ? round_elems(p.L3dim, elem) : 0);
+  *rows_per_buf = kind == 0 ? 2 : 1;
+  *ws_elems = kind == 0 ? 2 * 32 * kDMax
+                        : static_cast<int>(((p.L1dim + 3) & ~3) + size_t(p.L2dim) * 32);
+  return align16(sizeof(CwItem) * p.cw_items.size()) + 16 +
+         2 * elem * size_t(*row_elems) * (*rows_per_buf) + 8 * elem * size_t(*ws_elems);
+}
+
+// Channelwise uvu (MACE / NequIP interaction shape): mul_ir, one Y copy per instruction,
+// multiplicities in whole 32-lane chunks, one instruction per output irrep.
+void build_cw(oeqb_plan& p) {
+  p.cw_ok = false;
+  p.cw_items.clear();
+  if (p.uvw || p.layout != 0 || !p.zb_f.empty()) return;
+  for (const GroupD& g : p.grp_f)
+    if (g.count != 1) return;
+  for (const InstrD& in : p.ins_f) {
+    if (in.code < 0 || in.m2 != 1 || in.m1 % 32 != 0 || in.m1 == 0) return;
+    const IrrepD& r1 = p.ir1[in.i1];
+    const IrrepD& r2 = p.ir2[in.i2];
+    const IrrepD& r3 = p.ir3[in.i3];
+    for (int c0 = 0; c0 < in.m1; c0 += 32) {
+      CwItem it{};
+      it.code = in.code;
+      it.x_off = r1.off + c0 * r1.dim;
+      it.y_off = r2.off;
+      it.w_off = in.woff + c0;
+      it.z_off = r3.off + c0 * r3.dim;
+      it.pw = in.pw;
+      p.cw_items.push_back(it);
+    }
+  }
+  const size_t elem = p.dtype == 2 ? 8 : 4;
+  int re, oy, ow, og, we, rpb;
+  if (cw_smem(p, 0, elem, &re, &oy, &ow, &og, &we, &rpb) > 110 * 1024) return;
+  if (cw_smem(p, 1, elem, &re, &oy, &ow, &og, &we, &rpb) > 220 * 1024) return;
+  p.cw_ok = !p.cw_items.empty();
 }
 
 int parse_descriptor(const void* data, size_t n, oeqb_plan& p) {
@@ -355,6 +405,7 @@ int parse_descriptor(const void* data, size_t n, oeqb_plan& p) {
   p.desc_f = desc_bytes(p, p.grp_f.size(), p.zb_f.size());
   p.desc_b = desc_bytes(p, p.grp_b.size(), p.zb_b.size());
   build_row(p);
+  build_cw(p);
   return 0;
 }
 
@@ -384,6 +435,7 @@ void layout_tables(oeqb_plan& p, std::vector<unsigned char>& buf) {
     t->off_witems = put(buf, t->witems);
     t->off_wofs = put(buf, t->wofs);
   }
+  p.off_cw = put(buf, p.cw_items);
   p.off.total = align16(buf.size());
   buf.resize(p.off.total);
 }
@@ -539,6 +591,45 @@ int launch_row(oeqb_plan& p, int kind, const Args<T>& a, cudaStream_t stream) {
   return 0;
 }
 
+template <class T>
+int launch_cw(oeqb_plan& p, int kind, const Args<T>& a, cudaStream_t stream) {
+  if (a.nitems <= 0) return 0;
+  ArgsCw<T> v;
+  v.a = a;
+  v.items = reinterpret_cast<const CwItem*>(p.dmem + p.off_cw);
+  v.nitems = static_cast<int>(p.cw_items.size());
+  v.nwarps = 8;
+  const size_t elem = sizeof(T);
+  const size_t smem = cw_smem(p, kind, elem, &v.row_elems, &v.offY, &v.offW, &v.offG, &v.ws_elems,
+                              &v.rows_per_buf);
+  bool tma = aligned16(a.X) && aligned16(a.Y) && (p.L1dim * elem) % 16 == 0 &&
+             (p.L2dim * elem) % 16 == 0;
+  if (!p.shared_w) tma = tma && aligned16(a.W) && (p.wnumel * elem) % 16 == 0;
+  if (kind == 1) tma = tma && aligned16(a.Gz) && (p.L3dim * elem) % 16 == 0;
+  v.use_tma = tma ? 1 : 0;
+  const void* kernel = cw_kernel_ptr<T>(kind);
+  int per_sm;
+  {
+    std::lock_guard<std::mutex> g(p.mu);
+    auto it = p.occ.find(kernel);
+    if (it == p.occ.end()) {
+      if (int rc = allow_max_smem(p.device, kernel)) return rc;
+      int n = 0;
+      OEQB_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kernel, 256, smem));
+      if (n <= 0) return fail(OEQB_ERR_UNSUPPORTED, "channelwise kernel does not fit on the device");
+      it = p.occ.emplace(kernel, n).first;
+    }
+    per_sm = it->second;
+  }
+  const long long units = (a.nitems + v.rows_per_buf - 1) / v.rows_per_buf;
+  long long blocks = std::min<long long>(units, (long long)p.sm_count * per_sm);
+  blocks = std::max<long long>(1, blocks);
+  void* params[] = {&v};
+  OEQB_CUDA(cudaLaunchKernel(kernel, dim3(static_cast<unsigned>(blocks)), dim3(256), params, smem,
+                             stream));
+  return 0;
+}
+
 struct DeviceGuard {
   int prev = -1;
   explicit DeviceGuard(int dev) {
@@ -566,6 +657,7 @@ int tp_forward_t(oeqb_plan* p, int64_t B, const void* X, const void* Y, const vo
   a.Y = static_cast<const T*>(Y);
   a.W = static_cast<const T*>(W);
   a.out0 = static_cast<T*>(Z);
+  if (p->cw_ok) return launch_cw(*p, 0, a, s);
   if (p->row_ok) return launch_row(*p, 0, a, s);
   return launch(*p, batch_kernel_ptr<T>(0, p->uvw, false, kBatch), a, true, false, s);
 }
@@ -583,6 +675,7 @@ int tp_backward_t(oeqb_plan* p, int64_t B, const void* X, void* dX, const void* 
   a.out0 = static_cast<T*>(dX);
   a.out1 = static_cast<T*>(dY);
   a.out2 = static_cast<T*>(dW);
+  if (p->cw_ok) return launch_cw(*p, 1, a, s);
   if (p->row_ok) return launch_row(*p, 1, a, s);
   return launch(*p, batch_kernel_ptr<T>(1, p->uvw, false, kBatch), a, false, false, s);
 }
@@ -872,6 +965,7 @@ int oeqb_tp_forward_noalloc(const void* descriptor, size_t nbytes, int device, i
   p.device = device;
   if (int rc = parse_descriptor(descriptor, nbytes, p)) return rc;
   p.row_ok = false;  // this entry point runs the table-driven forward kernel
+  p.cw_ok = false;
   std::vector<unsigned char> img;
   layout_tables(p, img);
   const size_t status_off = align16(img.size());

@@ -3,7 +3,7 @@
 // here and launches them with cudaLaunchKernel.
 #pragma once
 #include "tp_kernels.cuh"
-#include "tp_kernels_row.cuh"
+#include "tp_kernels_cw.cuh"
 
 namespace oeqb {
 
@@ -17,6 +17,10 @@ const void* det_kernel_ptr(int kind, bool uvw, bool db, bool kahan);
 // Row-staged wide-uvu batch kernels (tp_kernels_row.cuh); kind 0 = forward, 1 = backward.
 template <class T>
 const void* row_kernel_ptr(int kind, int nwarps);
+
+// Channelwise-uvu kernels (tp_kernels_cw.cuh); kind 0 = forward, 1 = backward.
+template <class T>
+const void* cw_kernel_ptr(int kind);
 
 #define OEQB_PICK4(K, T, P)                                                     \
   (uvw ? (db ? (const void*)K<T, true, true, P> : (const void*)K<T, true, false, P>) \
@@ -37,6 +41,12 @@ const void* row_kernel_ptr(int kind, int nwarps);
   const void* row_kernel_ptr<T>(int kind, int nwarps) {                          \
     if (kind == 0) return (const void*)tp_fwd_row<T, 8>;                          \
     return nwarps == 16 ? (const void*)tp_bwd_row<T, 16> : (const void*)tp_bwd_row<T, 8>; \
+  }
+
+#define OEQB_DEFINE_CW_TABLE(T)                                                 \
+  template <>                                                                   \
+  const void* cw_kernel_ptr<T>(int kind) {                                      \
+    return kind == 0 ? (const void*)tp_fwd_cw<T> : (const void*)tp_bwd_cw<T>;     \
   }
 
 #define OEQB_DEFINE_DET_TABLE(T, WITH_KAHAN)                                    \
