@@ -8,9 +8,6 @@ forward + backward per step.  A row is the tensor product of one edge, so the me
 edges (rows) per second.  With --gpus N every rank processes its own 50,000-row shard
 (weak scaling, no data-path collective: batch rows are independent).
 
-``--workload conv`` measures the fused convolution (config-1 irreps) on the 200,000-node
-radius graph instead (receiver-sorted, deterministic mode), one full graph per GPU.
-
 Timing: W warm-up steps, then K steps between barriers + device syncs, CUDA events on the
 launching stream, max over ranks.  Inputs are larger than L2 (126 MB) so no flush is
 needed.  ``e2e`` repeats the step through the public operator API with pinned host
@@ -43,7 +40,7 @@ def _args():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["c2", "c2ml", "conv"], default="c2")
+    ap.add_argument("--workload", choices=["c2", "c2ml"], default="c2")
     ap.add_argument("--rows", type=int, default=50000)
     ap.add_argument("--e2e-steps", type=int, default=3)
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -326,7 +323,7 @@ def bench_reference(args, world, rank):
         return None
     from openequivariance_b200.problems import baseline_problem
 
-    problem = baseline_problem(args.workload if args.workload != "conv" else "c1")
+    problem = baseline_problem(args.workload)
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import cpu_baseline as CB
     import tp_oracle as O
@@ -366,10 +363,6 @@ def main():
     world, rank, local = _dist()
     if args.impl == "reference":
         line = bench_reference(args, world, rank)
-    elif args.workload == "conv":
-        from bench_conv import bench_conv  # noqa: F401  (conv workload module)
-
-        line = bench_conv(args, world, rank, local)
     else:
         line = bench_tp(args, world, rank, local)
     if rank == 0 and line is not None:

@@ -30,7 +30,7 @@ const void* det_kernel_ptr(int kind, bool uvw, bool db, bool kahan);
 template <class T>
 const void* row_kernel_ptr(int kind, int nwarps);
 template <class T>
-const void* cw_kernel_ptr(int kind);
+const void* cw_kernel_ptr(int kind, int nwarps);
 }  // namespace oeqb
 
 using namespace oeqb;
@@ -93,8 +93,10 @@ struct oeqb_plan {
   bool row_ok = false;
   // Channelwise-uvu kernels (tp_kernels_cw.cuh): one item per (instruction, 32-lane chunk).
   std::vector<CwItem> cw_items;
-  size_t off_cw = 0;
+  std::vector<CwXIrrep> cw_xirr;
+  size_t off_cw = 0, off_cwx = 0;
   bool cw_ok = false;
+  int cw_chunk_mode = 0, cw_nch = 0, cw_bwd_warps = 8;
   DevArrays off{};
   unsigned char* dmem = nullptr;
   int* d_status = nullptr;
@@ -224,6 +226,14 @@ void build_row(oeqb_plan& p) {
   p.row_ok = true;
 }
 
+// Elements of one warp's dX partial: one chunk of every X irrep in chunk mode, else a row.
+int cw_dxn(const oeqb_plan& p) {
+  if (!p.cw_chunk_mode) return p.L1dim;
+  int n = 0;
+  for (const IrrepD& r : p.ir1) n += 32 * r.dim;
+  return n;
+}
+
 size_t cw_smem(const oeqb_plan& p, int kind, size_t elem, int* row_elems, int* offY, int* offW,
                int* offG, int* ws_elems, int* rows_per_buf) {
   *offY = static_cast<int>(round_elems(p.L1dim, elem));
@@ -231,10 +241,11 @@ size_t cw_smem(const oeqb_plan& p, int kind, size_t elem, int* row_elems, int* o
   *offG = *offW + static_cast<int>(p.shared_w ? 0 : round_elems(p.wnumel, elem));
   *row_elems = *offG + static_cast<int>(kind == 1 ? round_elems(p.L3dim, elem) : 0);
   *rows_per_buf = kind == 0 ? 2 : 1;
+  const int nw = kind == 0 ? 8 : p.cw_bwd_warps;
   *ws_elems = kind == 0 ? 2 * 32 * kDMax
-                        : static_cast<int>(((p.L1dim + 3) & ~3) + size_t(p.L2dim) * 32);
-  return align16(sizeof(CwItem) * p.cw_items.size()) + 16 +
-         2 * elem * size_t(*row_elems) * (*rows_per_buf) + 8 * elem * size_t(*ws_elems);
+                        : static_cast<int>(((cw_dxn(p) + 3) & ~3) + size_t(p.L2dim) * 32);
+  return align16(sizeof(CwItem) * p.cw_items.size() + sizeof(CwXIrrep) * p.cw_xirr.size()) + 16 +
+         2 * elem * size_t(*row_elems) * (*rows_per_buf) + size_t(nw) * elem * size_t(*ws_elems);
 }
 
 // Channelwise uvu (MACE / NequIP interaction shape): mul_ir, one Y copy per instruction,
@@ -257,13 +268,54 @@ void build_cw(oeqb_plan& p) {
       it.y_off = r2.off;
       it.w_off = in.woff + c0;
       it.z_off = r3.off + c0 * r3.dim;
+      it.xp_off = r1.off + c0 * r1.dim;  // full-row partial; chunk mode rewrites below
       it.pw = in.pw;
       p.cw_items.push_back(it);
     }
   }
+  // Chunk mode: every instruction spans the same number of chunks and 16 warps split
+  // evenly, so item i (instruction-major, chunk-minor) lands on warp i % 16, whose chunk
+  // is always (warp % nch).  Its dX partial then holds only that chunk of each X irrep.
+  int nch = -1;
+  bool uniform = true;
+  for (const InstrD& in : p.ins_f) {
+    const int c = in.m1 / 32;
+    if (nch < 0) nch = c;
+    uniform = uniform && c == nch;
+  }
+  for (const IrrepD& r : p.ir1) uniform = uniform && (r.mul == 0 || r.mul == 32 * nch);
+  p.cw_xirr.clear();
+  int poff = 0;
+  for (const IrrepD& r : p.ir1) {
+    p.cw_xirr.push_back(CwXIrrep{r.off, r.dim, (r.mul + 31) / 32, poff});
+    poff += 32 * r.dim;
+  }
   const size_t elem = p.dtype == 2 ? 8 : 4;
   int re, oy, ow, og, we, rpb;
   if (cw_smem(p, 0, elem, &re, &oy, &ow, &og, &we, &rpb) > 110 * 1024) return;
+  p.cw_chunk_mode = 0;
+  p.cw_bwd_warps = 8;
+  if (uniform && nch > 0 && 16 % nch == 0) {
+    p.cw_chunk_mode = 1;
+    p.cw_nch = nch;
+    p.cw_bwd_warps = 16;
+    if (cw_smem(p, 1, elem, &re, &oy, &ow, &og, &we, &rpb) > 220 * 1024) {
+      p.cw_chunk_mode = 0;
+      p.cw_bwd_warps = 8;
+    }
+  }
+  if (p.cw_chunk_mode) {
+    for (CwItem& it : p.cw_items) {
+      // Locate this item's X irrep by offset and point at the warp's chunk slice.
+      for (size_t r = 0; r < p.ir1.size(); ++r) {
+        const IrrepD& ir = p.ir1[r];
+        if (it.x_off >= ir.off && it.x_off < ir.off + ir.mul * ir.dim) {
+          it.xp_off = p.cw_xirr[r].poff;
+          break;
+        }
+      }
+    }
+  }
   if (cw_smem(p, 1, elem, &re, &oy, &ow, &og, &we, &rpb) > 220 * 1024) return;
   p.cw_ok = !p.cw_items.empty();
 }
@@ -436,6 +488,7 @@ void layout_tables(oeqb_plan& p, std::vector<unsigned char>& buf) {
     t->off_wofs = put(buf, t->wofs);
   }
   p.off_cw = put(buf, p.cw_items);
+  p.off_cwx = put(buf, p.cw_xirr);
   p.off.total = align16(buf.size());
   buf.resize(p.off.total);
 }
@@ -597,8 +650,13 @@ int launch_cw(oeqb_plan& p, int kind, const Args<T>& a, cudaStream_t stream) {
   ArgsCw<T> v;
   v.a = a;
   v.items = reinterpret_cast<const CwItem*>(p.dmem + p.off_cw);
+  v.xirr = reinterpret_cast<const CwXIrrep*>(p.dmem + p.off_cwx);
   v.nitems = static_cast<int>(p.cw_items.size());
-  v.nwarps = 8;
+  v.nxirr = static_cast<int>(p.cw_xirr.size());
+  v.nwarps = kind == 0 ? 8 : p.cw_bwd_warps;
+  v.chunk_mode = kind == 1 ? p.cw_chunk_mode : 0;
+  v.nch_all = p.cw_nch;
+  v.dxn = (cw_dxn(p) + 3) & ~3;
   const size_t elem = sizeof(T);
   const size_t smem = cw_smem(p, kind, elem, &v.row_elems, &v.offY, &v.offW, &v.offG, &v.ws_elems,
                               &v.rows_per_buf);
@@ -607,7 +665,8 @@ int launch_cw(oeqb_plan& p, int kind, const Args<T>& a, cudaStream_t stream) {
   if (!p.shared_w) tma = tma && aligned16(a.W) && (p.wnumel * elem) % 16 == 0;
   if (kind == 1) tma = tma && aligned16(a.Gz) && (p.L3dim * elem) % 16 == 0;
   v.use_tma = tma ? 1 : 0;
-  const void* kernel = cw_kernel_ptr<T>(kind);
+  const void* kernel = cw_kernel_ptr<T>(kind, v.nwarps);
+  const int threads = 32 * v.nwarps;
   int per_sm;
   {
     std::lock_guard<std::mutex> g(p.mu);
@@ -615,7 +674,7 @@ int launch_cw(oeqb_plan& p, int kind, const Args<T>& a, cudaStream_t stream) {
     if (it == p.occ.end()) {
       if (int rc = allow_max_smem(p.device, kernel)) return rc;
       int n = 0;
-      OEQB_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kernel, 256, smem));
+      OEQB_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kernel, threads, smem));
       if (n <= 0) return fail(OEQB_ERR_UNSUPPORTED, "channelwise kernel does not fit on the device");
       it = p.occ.emplace(kernel, n).first;
     }
@@ -625,8 +684,8 @@ int launch_cw(oeqb_plan& p, int kind, const Args<T>& a, cudaStream_t stream) {
   long long blocks = std::min<long long>(units, (long long)p.sm_count * per_sm);
   blocks = std::max<long long>(1, blocks);
   void* params[] = {&v};
-  OEQB_CUDA(cudaLaunchKernel(kernel, dim3(static_cast<unsigned>(blocks)), dim3(256), params, smem,
-                             stream));
+  OEQB_CUDA(cudaLaunchKernel(kernel, dim3(static_cast<unsigned>(blocks)), dim3(threads), params,
+                             smem, stream));
   return 0;
 }
 

@@ -20,7 +20,7 @@ const void* row_kernel_ptr(int kind, int nwarps);
 
 // Channelwise-uvu kernels (tp_kernels_cw.cuh); kind 0 = forward, 1 = backward.
 template <class T>
-const void* cw_kernel_ptr(int kind);
+const void* cw_kernel_ptr(int kind, int nwarps);
 
 #define OEQB_PICK4(K, T, P)                                                     \
   (uvw ? (db ? (const void*)K<T, true, true, P> : (const void*)K<T, true, false, P>) \
@@ -45,8 +45,9 @@ const void* cw_kernel_ptr(int kind);
 
 #define OEQB_DEFINE_CW_TABLE(T)                                                 \
   template <>                                                                   \
-  const void* cw_kernel_ptr<T>(int kind) {                                      \
-    return kind == 0 ? (const void*)tp_fwd_cw<T> : (const void*)tp_bwd_cw<T>;     \
+  const void* cw_kernel_ptr<T>(int kind, int nwarps) {                          \
+    if (kind == 0) return (const void*)tp_fwd_cw<T>;                              \
+    return nwarps == 16 ? (const void*)tp_bwd_cw<T, 16> : (const void*)tp_bwd_cw<T, 8>; \
   }
 
 #define OEQB_DEFINE_DET_TABLE(T, WITH_KAHAN)                                    \

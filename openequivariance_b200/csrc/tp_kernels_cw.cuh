@@ -26,16 +26,26 @@ struct CwItem {
   int y_off;   // Y row offset of the Y irrep
   int w_off;   // W row offset of this chunk (instruction offset + c0)
   int z_off;   // output row offset of this chunk (irrep offset + c0 * d3)
-  int pad0, pad1, pad2;
+  int xp_off;  // offset of this chunk in the warp's dX partial (backward)
+  int pad0, pad1;
   double pw;
+};
+
+// Backward dX reduction plan: per X irrep, where its chunks live in the warp partials.
+struct CwXIrrep {
+  int off, dim, nch, poff;  // row offset, irrep dim, chunks, offset of chunk slice in partials
 };
 
 template <class T>
 struct ArgsCw {
   Args<T> a;
   const CwItem* items;
-  int nitems;
+  const CwXIrrep* xirr;
+  int nitems, nxirr;
   int nwarps;
+  int chunk_mode;   // backward: 1 = warp w owns chunk w % nch_all; partials hold one chunk
+  int nch_all;      // chunks per instruction (chunk mode)
+  int dxn;          // elements of the per-warp dX partial
   int offY, offW, offG, row_elems;  // one row's layout in the row buffer
   int rows_per_buf;                 // forward: rows staged per buffer (consecutive rows)
   int use_tma;
@@ -44,6 +54,7 @@ struct ArgsCw {
 
 struct SmemCw {
   CwItem* items;
+  CwXIrrep* xirr;
   unsigned long long* bars;
   unsigned char* rowbuf;
   unsigned char* warps;
@@ -55,6 +66,8 @@ __device__ __forceinline__ SmemCw stage_cw(const ArgsCw<T>& v, unsigned char* sm
   unsigned char* p = sm;
   s.items = reinterpret_cast<CwItem*>(p);
   p += sizeof(CwItem) * v.nitems;
+  s.xirr = reinterpret_cast<CwXIrrep*>(p);
+  p += sizeof(CwXIrrep) * v.nxirr;
   p = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(p) + 15) & ~uintptr_t(15));
   s.bars = reinterpret_cast<unsigned long long*>(p);
   p += 16;
@@ -65,6 +78,9 @@ __device__ __forceinline__ SmemCw stage_cw(const ArgsCw<T>& v, unsigned char* sm
   int* dst = reinterpret_cast<int*>(s.items);
   for (int i = threadIdx.x; i < static_cast<int>(sizeof(CwItem) / 4) * v.nitems; i += blockDim.x)
     dst[i] = src[i];
+  const int* xs = reinterpret_cast<const int*>(v.xirr);
+  int* xd = reinterpret_cast<int*>(s.xirr);
+  for (int i = threadIdx.x; i < 4 * v.nxirr; i += blockDim.x) xd[i] = xs[i];
   if (threadIdx.x == 0) {
     mbar_init(&s.bars[0], 1);
     mbar_init(&s.bars[1], 1);
@@ -190,16 +206,15 @@ __global__ void __launch_bounds__(256, 2) tp_fwd_cw(const ArgsCw<T> v) {
   if (lane == 0) bulk_wait_all<0>();
 }
 
-template <class T>
-__global__ void __launch_bounds__(256, 1) tp_bwd_cw(const ArgsCw<T> v) {
+template <class T, int NW>
+__global__ void __launch_bounds__(NW * 32, 1) tp_bwd_cw(const ArgsCw<T> v) {
   extern __shared__ __align__(16) unsigned char smem[];
   const SmemCw s = stage_cw(v, smem);
   const Args<T>& a = v.a;
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
-  // Per-warp scratch: dX partial row (L1dim, rounded) then dY lane columns [L2dim][32].
-  const int dxn = (a.L1dim + 3) & ~3;
+  // Per-warp scratch: dX partial (v.dxn elements) then dY lane columns [L2dim][32].
   T* dxp = reinterpret_cast<T*>(s.warps) + static_cast<size_t>(wid) * v.ws_elems;
-  T* gyc = dxp + dxn;
+  T* gyc = dxp + v.dxn;
   const long long B = a.nitems;
   if (blockIdx.x < B) cw_load<T, true>(v, s, 0, blockIdx.x, 1);
   if (blockIdx.x + gridDim.x < B) cw_load<T, true>(v, s, 1, blockIdx.x + gridDim.x, 1);
@@ -207,12 +222,12 @@ __global__ void __launch_bounds__(256, 1) tp_bwd_cw(const ArgsCw<T> v) {
   int it = 0;
   for (long long row = blockIdx.x; row < B; row += gridDim.x, ++it) {
     const int b = it & 1;
-    for (int e = lane; e < dxn + a.L2dim * 32; e += 32) dxp[e] = T(0);
+    for (int e = lane; e < v.dxn + a.L2dim * 32; e += 32) dxp[e] = T(0);
     if (v.use_tma) mbar_wait(&s.bars[b], (it >> 1) & 1, a.status);
     __syncwarp();
     const T* rb = reinterpret_cast<const T*>(s.rowbuf) + static_cast<size_t>(b) * v.row_elems;
     T* dwrow = a.shared_w ? a.out2 : a.out2 + row * a.wnumel;
-    for (int ii = wid; ii < v.nitems; ii += v.nwarps) {
+    for (int ii = wid; ii < v.nitems; ii += NW) {
       const CwItem it_ = s.items[ii];
       dispatch_triple(it_.code, [&]<int A, int Bd, int C>() {
         constexpr int D1 = 2 * A + 1, D2 = 2 * Bd + 1, D3 = 2 * C + 1;
@@ -233,7 +248,7 @@ __global__ void __launch_bounds__(256, 1) tp_bwd_cw(const ArgsCw<T> v) {
         const T wp = wraw * pw;
         // h_i = sum_k P[i][k] gz_k: dX_i += w pw h_i, dW = pw sum_i x_i h_i.
         T sdot = T(0);
-        T* gxr = dxp + it_.x_off + lane * D1;
+        T* gxr = dxp + it_.xp_off + lane * D1;
 #pragma unroll
         for (int i = 0; i < D1; ++i) {
           T h = T(0);
@@ -259,15 +274,32 @@ __global__ void __launch_bounds__(256, 1) tp_bwd_cw(const ArgsCw<T> v) {
     // Fixed-order reductions over warps (and lanes for dY).
     const T* wbase = reinterpret_cast<const T*>(s.warps);
     T* gxrow = a.out0 + row * a.L1dim;
-    for (int e = threadIdx.x; e < a.L1dim; e += blockDim.x) {
-      T acc = T(0);
-      for (int w = 0; w < v.nwarps; ++w) acc += wbase[static_cast<size_t>(w) * v.ws_elems + e];
-      gxrow[e] = acc;
+    if (v.chunk_mode) {
+      // Warp w holds chunk (w % nch) of every X irrep at xirr.poff + (u % 32) * dim + i.
+      const int nch = v.nch_all;
+      for (int r = 0; r < v.nxirr; ++r) {
+        const CwXIrrep xr = s.xirr[r];
+        const int n = xr.nch * 32 * xr.dim;
+        for (int e = threadIdx.x; e < n; e += blockDim.x) {
+          const int c = e / (32 * xr.dim), q = e - c * 32 * xr.dim;
+          T acc = T(0);
+          for (int w = c; w < NW; w += nch)
+            acc += wbase[static_cast<size_t>(w) * v.ws_elems + xr.poff + q];
+          gxrow[xr.off + e] = acc;
+        }
+      }
+    } else {
+      for (int e = threadIdx.x; e < a.L1dim; e += blockDim.x) {
+        T acc = T(0);
+        for (int w = 0; w < NW; ++w) acc += wbase[static_cast<size_t>(w) * v.ws_elems + e];
+        gxrow[e] = acc;
+      }
     }
     T* gyrow = a.out1 + row * a.L2dim;
-    for (int j = wid; j < a.L2dim; j += v.nwarps) {
+    for (int j = wid; j < a.L2dim; j += NW) {
       T acc = T(0);
-      for (int w = 0; w < v.nwarps; ++w) acc += wbase[static_cast<size_t>(w) * v.ws_elems + dxn + j * 32 + lane];
+      for (int w = 0; w < NW; ++w)
+        acc += wbase[static_cast<size_t>(w) * v.ws_elems + v.dxn + j * 32 + lane];
       acc = group_sum(acc, 5);
       if (lane == 0) gyrow[j] = acc;
     }
