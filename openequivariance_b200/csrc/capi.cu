@@ -20,7 +20,7 @@
 
 #include "oeqb200.h"
 #include "tp_core.cuh"
-#include "tp_kernels_cw.cuh"
+#include "tp_kernels_seg.cuh"
 
 namespace oeqb {
 template <class T>
@@ -30,7 +30,7 @@ const void* det_kernel_ptr(int kind, bool uvw, bool db, bool kahan);
 template <class T>
 const void* row_kernel_ptr(int kind, int nwarps);
 template <class T>
-const void* cw_kernel_ptr(int kind, int nwarps);
+const void* seg_kernel_ptr(int kind);
 }  // namespace oeqb
 
 using namespace oeqb;
@@ -91,12 +91,17 @@ struct oeqb_plan {
     size_t off_items = 0, off_witems = 0, off_wofs = 0;
   } rowf, rowb;
   bool row_ok = false;
-  // Channelwise-uvu kernels (tp_kernels_cw.cuh): one item per (instruction, 32-lane chunk).
-  std::vector<CwItem> cw_items;
-  std::vector<CwXIrrep> cw_xirr;
-  size_t off_cw = 0, off_cwx = 0;
-  bool cw_ok = false;
-  int cw_chunk_mode = 0, cw_nch = 0, cw_bwd_warps = 8;
+  // Channelwise-uvu segment kernels (tp_kernels_seg.cuh): one table image per pass.
+  struct SegTable {
+    bool ok = false;
+    std::vector<unsigned char> blob;  // SegInstr | SegRun | grp | SegX | SegPEnt | SegTerm
+    int off_run = 0, off_grp = 0, off_x = 0, off_pent = 0, off_term = 0;
+    int ngroups = 1, nsplit = 1, cbs = 1, nx = 0, npent = 0, psize = 0, rows_per_buf = 1;
+    int scratch_off = 0, gyc_off = 0;
+    int offY = 0, offW = 0, offG = 0, row_elems = 0;
+    size_t smem = 0, dev_off = 0;
+  } segf, segb;
+
   DevArrays off{};
   unsigned char* dmem = nullptr;
   int* d_status = nullptr;
@@ -226,98 +231,183 @@ void build_row(oeqb_plan& p) {
   p.row_ok = true;
 }
 
-// Elements of one warp's dX partial: one chunk of every X irrep in chunk mode, else a row.
-int cw_dxn(const oeqb_plan& p) {
-  if (!p.cw_chunk_mode) return p.L1dim;
-  int n = 0;
-  for (const IrrepD& r : p.ir1) n += 32 * r.dim;
-  return n;
+constexpr int kSegBwdWarps = 16;
+
+template <class V>
+int blob_put(std::vector<unsigned char>& blob, const std::vector<V>& v) {
+  const size_t at = align16(blob.size());
+  blob.resize(at + sizeof(V) * v.size());
+  if (!v.empty()) std::memcpy(blob.data() + at, v.data(), sizeof(V) * v.size());
+  return static_cast<int>(at);
 }
 
-size_t cw_smem(const oeqb_plan& p, int kind, size_t elem, int* row_elems, int* offY, int* offW,
-               int* offG, int* ws_elems, int* rows_per_buf) {
-  *offY = static_cast<int>(round_elems(p.L1dim, elem));
-  *offW = *offY + static_cast<int>(round_elems(p.L2dim, elem));
-  *offG = *offW + static_cast<int>(p.shared_w ? 0 : round_elems(p.wnumel, elem));
-  *row_elems = *offG + static_cast<int>(kind == 1 ? round_elems(p.L3dim, elem) : 0);
-  *rows_per_buf = kind == 0 ? 2 : 1;
-  const int nw = kind == 0 ? 8 : p.cw_bwd_warps;
-  *ws_elems = kind == 0 ? 2 * 32 * kDMax
-                        : static_cast<int>(((cw_dxn(p) + 3) & ~3) + size_t(p.L2dim) * 32);
-  return align16(sizeof(CwItem) * p.cw_items.size() + sizeof(CwXIrrep) * p.cw_xirr.size()) + 16 +
-         2 * elem * size_t(*row_elems) * (*rows_per_buf) + size_t(nw) * elem * size_t(*ws_elems);
-}
-
-// Channelwise uvu (MACE / NequIP interaction shape): mul_ir, one Y copy per instruction,
-// multiplicities in whole 32-lane chunks, one instruction per output irrep.
-void build_cw(oeqb_plan& p) {
-  p.cw_ok = false;
-  p.cw_items.clear();
-  if (p.uvw || p.layout != 0 || !p.zb_f.empty()) return;
-  for (const GroupD& g : p.grp_f)
-    if (g.count != 1) return;
-  for (const InstrD& in : p.ins_f) {
-    if (in.code < 0 || in.m2 != 1 || in.m1 % 32 != 0 || in.m1 == 0) return;
-    const IrrepD& r1 = p.ir1[in.i1];
-    const IrrepD& r2 = p.ir2[in.i2];
-    const IrrepD& r3 = p.ir3[in.i3];
-    for (int c0 = 0; c0 < in.m1; c0 += 32) {
-      CwItem it{};
-      it.code = in.code;
-      it.x_off = r1.off + c0 * r1.dim;
-      it.y_off = r2.off;
-      it.w_off = in.woff + c0;
-      it.z_off = r3.off + c0 * r3.dim;
-      it.xp_off = r1.off + c0 * r1.dim;  // full-row partial; chunk mode rewrites below
-      it.pw = in.pw;
-      p.cw_items.push_back(it);
-    }
-  }
-  // Chunk mode: every instruction spans the same number of chunks and 16 warps split
-  // evenly, so item i (instruction-major, chunk-minor) lands on warp i % 16, whose chunk
-  // is always (warp % nch).  Its dX partial then holds only that chunk of each X irrep.
-  int nch = -1;
-  bool uniform = true;
-  for (const InstrD& in : p.ins_f) {
-    const int c = in.m1 / 32;
-    if (nch < 0) nch = c;
-    uniform = uniform && c == nch;
-  }
-  for (const IrrepD& r : p.ir1) uniform = uniform && (r.mul == 0 || r.mul == 32 * nch);
-  p.cw_xirr.clear();
+// Builds the table image of one segment-kernel pass.  `order` lists the instructions sorted
+// by X irrep; `bounds` splits it into contiguous groups (backward units; one group forward).
+template <class T>
+void seg_tables(const oeqb_plan& p, const std::vector<int>& order, const std::vector<int>& bounds,
+                oeqb_plan::SegTable& t) {
+  std::vector<SegInstr> ins;
+  std::vector<SegRun> runs;
+  std::vector<int> grp;
+  std::vector<SegX> xs;
+  std::vector<SegPEnt> pent;
+  std::vector<SegTerm<T>> term;
   int poff = 0;
-  for (const IrrepD& r : p.ir1) {
-    p.cw_xirr.push_back(CwXIrrep{r.off, r.dim, (r.mul + 31) / 32, poff});
-    poff += 32 * r.dim;
-  }
-  const size_t elem = p.dtype == 2 ? 8 : 4;
-  int re, oy, ow, og, we, rpb;
-  if (cw_smem(p, 0, elem, &re, &oy, &ow, &og, &we, &rpb) > 110 * 1024) return;
-  p.cw_chunk_mode = 0;
-  p.cw_bwd_warps = 8;
-  if (uniform && nch > 0 && 16 % nch == 0) {
-    p.cw_chunk_mode = 1;
-    p.cw_nch = nch;
-    p.cw_bwd_warps = 16;
-    if (cw_smem(p, 1, elem, &re, &oy, &ow, &og, &we, &rpb) > 220 * 1024) {
-      p.cw_chunk_mode = 0;
-      p.cw_bwd_warps = 8;
+  for (int idx : order) {
+    const InstrD& in = p.ins_f[idx];
+    const IrrepD& r1 = p.ir1[in.i1];
+    const IrrepD& r3 = p.ir3[in.i3];
+    SegInstr si{};
+    si.l1 = in.l1;
+    si.l3 = in.l3;
+    si.bc = pair_code(in.l2, in.l3);
+    si.y_off = p.ir2[in.i2].off;
+    si.w_off = in.woff;
+    si.z_off = r3.off;
+    si.p_off = poff;
+    si.pw = in.pw;
+    ins.push_back(si);
+    // Non-zero P entries: P[i][k] = sum_j (pw c_ijk) y_j, terms grouped by (i, k).
+    std::vector<std::vector<std::pair<int, double>>> cell(size_t(r1.dim) * r3.dim);
+    for (int e = in.cg_off; e < in.cg_off + in.cg_nnz; ++e) {
+      const CGEntry& c = p.cg[e];
+      cell[size_t(c.i) * r3.dim + c.k].push_back({si.y_off + c.j, in.pw * c.c});
     }
+    for (size_t q = 0; q < cell.size(); ++q) {
+      if (cell[q].empty()) continue;
+      pent.push_back(SegPEnt{poff + static_cast<int>(q),
+                             (static_cast<int>(term.size()) << 8) | static_cast<int>(cell[q].size())});
+      for (auto& tj : cell[q]) term.push_back(SegTerm<T>{T(tj.second), tj.first});
+    }
+    poff += (r1.dim * r3.dim + 3) / 4 * 4;
   }
-  if (p.cw_chunk_mode) {
-    for (CwItem& it : p.cw_items) {
-      // Locate this item's X irrep by offset and point at the warp's chunk slice.
-      for (size_t r = 0; r < p.ir1.size(); ++r) {
-        const IrrepD& ir = p.ir1[r];
-        if (it.x_off >= ir.off && it.x_off < ir.off + ir.mul * ir.dim) {
-          it.xp_off = p.cw_xirr[r].poff;
-          break;
-        }
+  // Runs: maximal pieces of a group with one X irrep.  Groups are contiguous pieces of the
+  // X-sorted list, so the runs of one X irrep are consecutive in the run table.
+  std::vector<int> run_irrep;
+  int pslot = 0;
+  for (size_t g = 0; g + 1 < bounds.size(); ++g) {
+    grp.push_back(static_cast<int>(runs.size()));
+    for (int n = bounds[g]; n < bounds[g + 1]; ++n) {
+      const InstrD& in = p.ins_f[order[n]];
+      if (static_cast<int>(runs.size()) == grp.back() || run_irrep.back() != in.i1) {
+        const IrrepD& r1 = p.ir1[in.i1];
+        runs.push_back(SegRun{r1.off, r1.l, r1.mul / 32, n, n + 1, pslot, 0, 0});
+        run_irrep.push_back(in.i1);
+        pslot += (r1.mul * r1.dim + 3) / 4 * 4;
+      } else {
+        runs.back().n1 = n + 1;
       }
     }
   }
-  if (cw_smem(p, 1, elem, &re, &oy, &ow, &og, &we, &rpb) > 220 * 1024) return;
-  p.cw_ok = !p.cw_items.empty();
+  grp.push_back(static_cast<int>(runs.size()));
+  for (size_t r = 0; r < p.ir1.size(); ++r) {
+    int r0 = 0, r1 = 0;
+    for (size_t q = 0; q < runs.size(); ++q)
+      if (run_irrep[q] == static_cast<int>(r)) {
+        if (r1 == 0) r0 = static_cast<int>(q);
+        r1 = static_cast<int>(q) + 1;
+      }
+    xs.push_back(SegX{p.ir1[r].off, p.ir1[r].mul * p.ir1[r].dim, r0, r1});
+  }
+  t.gyc_off = pslot;
+  t.blob.clear();
+  blob_put(t.blob, ins);
+  t.off_run = blob_put(t.blob, runs);
+  t.off_grp = blob_put(t.blob, grp);
+  t.off_x = blob_put(t.blob, xs);
+  t.off_pent = blob_put(t.blob, pent);
+  t.off_term = blob_put(t.blob, term);
+  t.blob.resize(align16(t.blob.size()));
+  t.ngroups = static_cast<int>(bounds.size()) - 1;
+  t.nx = static_cast<int>(xs.size());
+  t.npent = static_cast<int>(pent.size());
+  t.psize = poff;
+}
+
+// Row layout and shared-memory bytes of a segment pass (must match stage_seg).
+void seg_layout(const oeqb_plan& p, int kind, size_t elem, oeqb_plan::SegTable& t) {
+  t.offY = static_cast<int>(round_elems(p.L1dim, elem));
+  t.offW = t.offY + static_cast<int>(round_elems(p.L2dim, elem));
+  t.offG = t.offW + static_cast<int>(p.shared_w ? 0 : round_elems(p.wnumel, elem));
+  t.row_elems = t.offG + static_cast<int>(kind == 1 ? round_elems(p.L3dim, elem) : 0);
+  t.scratch_off = static_cast<int>(round_elems(size_t(t.rows_per_buf) * t.psize, elem));
+  size_t scratch;
+  if (kind == 0)
+    scratch = size_t(8) * kSegStages * seg_fwd_cpl(static_cast<int>(elem)) * 32 * kSegD;
+  else
+    scratch = size_t(t.gyc_off) + size_t(kSegBwdWarps) * p.L2dim * 32;
+  t.smem = t.blob.size() + 16 + 2 * elem * size_t(t.row_elems) * t.rows_per_buf +
+           elem * (size_t(t.scratch_off) + scratch);
+}
+
+// Channelwise uvu (MACE / NequIP interaction shape): mul_ir, one Y copy per instruction,
+// multiplicities in whole 32-lane chunks, one instruction per output irrep, unrolled degrees.
+void build_seg(oeqb_plan& p) {
+  p.segf = {};
+  p.segb = {};
+  if (p.uvw || p.layout != 0 || !p.zb_f.empty() || p.ins_f.empty()) return;
+  for (const GroupD& g : p.grp_f)
+    if (g.count != 1) return;
+  int nchmax = 0;
+  for (const InstrD& in : p.ins_f) {
+    if (in.code < 0 || in.m2 != 1 || in.m1 % 32 != 0 || in.m1 == 0) return;
+    if (in.l1 > kLMaxUnrolled || in.l2 > kLMaxUnrolled || in.l3 > kLMaxUnrolled) return;
+    nchmax = std::max(nchmax, in.m1 / 32);
+  }
+  std::vector<int> order(p.ins_f.size());
+  for (size_t i = 0; i < order.size(); ++i) order[i] = static_cast<int>(i);
+  std::stable_sort(order.begin(), order.end(), [&](int x, int y) {
+    const InstrD &a = p.ins_f[x], &b = p.ins_f[y];
+    return a.i1 != b.i1 ? a.i1 < b.i1 : a.i2 < b.i2;
+  });
+  const int n = static_cast<int>(order.size());
+  const size_t elem = p.dtype == 2 ? 8 : 4;
+  // Splits the X-sorted list into G contiguous groups of similar cost.
+  auto split = [&](int G, bool bwd) {
+    std::vector<double> cost(n);
+    double total = 0;
+    for (int q = 0; q < n; ++q) {
+      const InstrD& in = p.ins_f[order[q]];
+      const int d1 = 2 * in.l1 + 1, d2 = 2 * in.l2 + 1, d3 = 2 * in.l3 + 1;
+      cost[q] = bwd ? 2.0 * d1 * d3 + 2.0 * in.cg_nnz + 2.0 * d2 + d3 + 12.0 : d1 * d3 + 2.0 * d3 + 10.0;
+      total += cost[q];
+    }
+    std::vector<int> bounds{0};
+    double acc = 0;
+    for (int q = 0; q < n; ++q) {
+      acc += cost[q];
+      const int g = static_cast<int>(bounds.size());
+      if (g < G && q + 1 < n && acc >= total * g / G) bounds.push_back(q + 1);
+    }
+    bounds.push_back(n);
+    return bounds;
+  };
+  auto tables = [&](const std::vector<int>& bounds, oeqb_plan::SegTable& t) {
+    if (p.dtype == 2)
+      seg_tables<double>(p, order, bounds, t);
+    else
+      seg_tables<float>(p, order, bounds, t);
+  };
+  // Forward: 8 warps = groups x chunk blocks of up to seg_fwd_cpl chunks, one row per buffer.
+  {
+    oeqb_plan::SegTable& t = p.segf;
+    t.cbs = std::min(seg_fwd_cpl(static_cast<int>(elem)), nchmax);
+    t.nsplit = (nchmax + t.cbs - 1) / t.cbs;
+    tables(split(std::max(1, std::min(n, 8 / std::min(8, t.nsplit))), false), t);
+    t.rows_per_buf = 1;
+    seg_layout(p, 0, elem, t);
+    t.ok = t.smem <= 220 * 1024;
+  }
+  // Backward: 16 warps = groups x chunk blocks of up to seg_bwd_cpl chunks.
+  {
+    oeqb_plan::SegTable& t = p.segb;
+    t.cbs = std::min(seg_bwd_cpl(static_cast<int>(elem)), nchmax);
+    t.nsplit = (nchmax + t.cbs - 1) / t.cbs;
+    tables(split(std::max(1, std::min(n, kSegBwdWarps / std::min(kSegBwdWarps, t.nsplit))), true), t);
+    t.rows_per_buf = 1;
+    seg_layout(p, 1, elem, t);
+    t.ok = t.smem <= 220 * 1024;
+  }
 }
 
 int parse_descriptor(const void* data, size_t n, oeqb_plan& p) {
@@ -457,7 +547,7 @@ int parse_descriptor(const void* data, size_t n, oeqb_plan& p) {
   p.desc_f = desc_bytes(p, p.grp_f.size(), p.zb_f.size());
   p.desc_b = desc_bytes(p, p.grp_b.size(), p.zb_b.size());
   build_row(p);
-  build_cw(p);
+  build_seg(p);
   return 0;
 }
 
@@ -487,8 +577,7 @@ void layout_tables(oeqb_plan& p, std::vector<unsigned char>& buf) {
     t->off_witems = put(buf, t->witems);
     t->off_wofs = put(buf, t->wofs);
   }
-  p.off_cw = put(buf, p.cw_items);
-  p.off_cwx = put(buf, p.cw_xirr);
+  for (auto* t : {&p.segf, &p.segb}) t->dev_off = put(buf, t->blob);
   p.off.total = align16(buf.size());
   buf.resize(p.off.total);
 }
@@ -645,28 +734,39 @@ int launch_row(oeqb_plan& p, int kind, const Args<T>& a, cudaStream_t stream) {
 }
 
 template <class T>
-int launch_cw(oeqb_plan& p, int kind, const Args<T>& a, cudaStream_t stream) {
+int launch_seg(oeqb_plan& p, int kind, const Args<T>& a, cudaStream_t stream) {
   if (a.nitems <= 0) return 0;
-  ArgsCw<T> v;
+  const oeqb_plan::SegTable& t = kind == 0 ? p.segf : p.segb;
+  ArgsSeg<T> v;
   v.a = a;
-  v.items = reinterpret_cast<const CwItem*>(p.dmem + p.off_cw);
-  v.xirr = reinterpret_cast<const CwXIrrep*>(p.dmem + p.off_cwx);
-  v.nitems = static_cast<int>(p.cw_items.size());
-  v.nxirr = static_cast<int>(p.cw_xirr.size());
-  v.nwarps = kind == 0 ? 8 : p.cw_bwd_warps;
-  v.chunk_mode = kind == 1 ? p.cw_chunk_mode : 0;
-  v.nch_all = p.cw_nch;
-  v.dxn = (cw_dxn(p) + 3) & ~3;
+  v.tables = p.dmem + t.dev_off;
+  v.table_bytes = static_cast<int>(t.blob.size());
+  v.off_run = t.off_run;
+  v.off_grp = t.off_grp;
+  v.off_x = t.off_x;
+  v.off_pent = t.off_pent;
+  v.off_term = t.off_term;
+  v.ngroups = t.ngroups;
+  v.nsplit = t.nsplit;
+  v.cbs = t.cbs;
+  v.gyc_off = t.gyc_off;
+  v.nx = t.nx;
+  v.npent = t.npent;
+  v.psize = t.psize;
+  v.offY = t.offY;
+  v.offW = t.offW;
+  v.offG = t.offG;
+  v.row_elems = t.row_elems;
+  v.rows_per_buf = t.rows_per_buf;
+  v.scratch_off = t.scratch_off;
   const size_t elem = sizeof(T);
-  const size_t smem = cw_smem(p, kind, elem, &v.row_elems, &v.offY, &v.offW, &v.offG, &v.ws_elems,
-                              &v.rows_per_buf);
   bool tma = aligned16(a.X) && aligned16(a.Y) && (p.L1dim * elem) % 16 == 0 &&
              (p.L2dim * elem) % 16 == 0;
   if (!p.shared_w) tma = tma && aligned16(a.W) && (p.wnumel * elem) % 16 == 0;
   if (kind == 1) tma = tma && aligned16(a.Gz) && (p.L3dim * elem) % 16 == 0;
   v.use_tma = tma ? 1 : 0;
-  const void* kernel = cw_kernel_ptr<T>(kind, v.nwarps);
-  const int threads = 32 * v.nwarps;
+  const void* kernel = seg_kernel_ptr<T>(kind);
+  const int threads = kind == 0 ? 256 : 32 * kSegBwdWarps;
   int per_sm;
   {
     std::lock_guard<std::mutex> g(p.mu);
@@ -674,18 +774,18 @@ int launch_cw(oeqb_plan& p, int kind, const Args<T>& a, cudaStream_t stream) {
     if (it == p.occ.end()) {
       if (int rc = allow_max_smem(p.device, kernel)) return rc;
       int n = 0;
-      OEQB_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kernel, threads, smem));
+      OEQB_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kernel, threads, t.smem));
       if (n <= 0) return fail(OEQB_ERR_UNSUPPORTED, "channelwise kernel does not fit on the device");
       it = p.occ.emplace(kernel, n).first;
     }
     per_sm = it->second;
   }
-  const long long units = (a.nitems + v.rows_per_buf - 1) / v.rows_per_buf;
+  const long long units = (a.nitems + t.rows_per_buf - 1) / t.rows_per_buf;
   long long blocks = std::min<long long>(units, (long long)p.sm_count * per_sm);
   blocks = std::max<long long>(1, blocks);
   void* params[] = {&v};
   OEQB_CUDA(cudaLaunchKernel(kernel, dim3(static_cast<unsigned>(blocks)), dim3(threads), params,
-                             smem, stream));
+                             t.smem, stream));
   return 0;
 }
 
@@ -716,7 +816,7 @@ int tp_forward_t(oeqb_plan* p, int64_t B, const void* X, const void* Y, const vo
   a.Y = static_cast<const T*>(Y);
   a.W = static_cast<const T*>(W);
   a.out0 = static_cast<T*>(Z);
-  if (p->cw_ok) return launch_cw(*p, 0, a, s);
+  if (p->segf.ok) return launch_seg(*p, 0, a, s);
   if (p->row_ok) return launch_row(*p, 0, a, s);
   return launch(*p, batch_kernel_ptr<T>(0, p->uvw, false, kBatch), a, true, false, s);
 }
@@ -734,7 +834,7 @@ int tp_backward_t(oeqb_plan* p, int64_t B, const void* X, void* dX, const void* 
   a.out0 = static_cast<T*>(dX);
   a.out1 = static_cast<T*>(dY);
   a.out2 = static_cast<T*>(dW);
-  if (p->cw_ok) return launch_cw(*p, 1, a, s);
+  if (p->segb.ok) return launch_seg(*p, 1, a, s);
   if (p->row_ok) return launch_row(*p, 1, a, s);
   return launch(*p, batch_kernel_ptr<T>(1, p->uvw, false, kBatch), a, false, false, s);
 }
@@ -1024,7 +1124,8 @@ int oeqb_tp_forward_noalloc(const void* descriptor, size_t nbytes, int device, i
   p.device = device;
   if (int rc = parse_descriptor(descriptor, nbytes, p)) return rc;
   p.row_ok = false;  // this entry point runs the table-driven forward kernel
-  p.cw_ok = false;
+  p.segf = {};
+  p.segb = {};
   std::vector<unsigned char> img;
   layout_tables(p, img);
   const size_t status_off = align16(img.size());

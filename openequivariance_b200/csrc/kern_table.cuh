@@ -3,7 +3,7 @@
 // here and launches them with cudaLaunchKernel.
 #pragma once
 #include "tp_kernels.cuh"
-#include "tp_kernels_cw.cuh"
+#include "tp_kernels_seg.cuh"
 
 namespace oeqb {
 
@@ -18,9 +18,9 @@ const void* det_kernel_ptr(int kind, bool uvw, bool db, bool kahan);
 template <class T>
 const void* row_kernel_ptr(int kind, int nwarps);
 
-// Channelwise-uvu kernels (tp_kernels_cw.cuh); kind 0 = forward, 1 = backward.
+// Channelwise-uvu segment kernels (tp_kernels_seg.cuh); kind 0 = forward, 1 = backward.
 template <class T>
-const void* cw_kernel_ptr(int kind, int nwarps);
+const void* seg_kernel_ptr(int kind);
 
 #define OEQB_PICK4(K, T, P)                                                     \
   (uvw ? (db ? (const void*)K<T, true, true, P> : (const void*)K<T, true, false, P>) \
@@ -45,9 +45,8 @@ const void* cw_kernel_ptr(int kind, int nwarps);
 
 #define OEQB_DEFINE_CW_TABLE(T)                                                 \
   template <>                                                                   \
-  const void* cw_kernel_ptr<T>(int kind, int nwarps) {                          \
-    if (kind == 0) return (const void*)tp_fwd_cw<T>;                              \
-    return nwarps == 16 ? (const void*)tp_bwd_cw<T, 16> : (const void*)tp_bwd_cw<T, 8>; \
+  const void* seg_kernel_ptr<T>(int kind) {                                     \
+    return kind == 0 ? (const void*)tp_fwd_seg<T> : (const void*)tp_bwd_seg<T, 16>; \
   }
 
 #define OEQB_DEFINE_DET_TABLE(T, WITH_KAHAN)                                    \
