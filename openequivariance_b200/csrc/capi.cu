@@ -20,7 +20,7 @@
 
 #include "oeqb200.h"
 #include "tp_core.cuh"
-#include "tp_kernels_seg.cuh"
+#include "tp_kernels_lk.cuh"
 
 namespace oeqb {
 template <class T>
@@ -31,6 +31,8 @@ template <class T>
 const void* row_kernel_ptr(int kind, int nwarps);
 template <class T>
 const void* seg_kernel_ptr(int kind);
+template <class T>
+const void* lk_kernel_ptr();
 }  // namespace oeqb
 
 using namespace oeqb;
@@ -96,11 +98,17 @@ struct oeqb_plan {
     bool ok = false;
     std::vector<unsigned char> blob;  // SegInstr | SegRun | grp | SegX | SegPEnt | SegTerm
     int off_run = 0, off_grp = 0, off_x = 0, off_pent = 0, off_term = 0;
-    int ngroups = 1, nsplit = 1, cbs = 1, nx = 0, npent = 0, psize = 0, rows_per_buf = 1;
+    int ngroups = 1, nsplit = 1, cbs = 1, nx = 0, npent = 0, psize = 0, rows_per_buf = 1, nrun = 0;
     int scratch_off = 0, gyc_off = 0;
     int offY = 0, offW = 0, offG = 0, row_elems = 0;
     size_t smem = 0, dev_off = 0;
-  } segf, segb;
+  } segf, segb, segl;
+  // Lockstep backward (tp_kernels_lk.cuh) over the tables of segl.
+  struct LkCfg {
+    bool ok = false;
+    int nch = 0, rb = 0, nslots = 0, offY = 0, xy_elems = 0, slot_elems = 0, slot_w_off = 0;
+    size_t smem = 0;
+  } lk;
 
   DevArrays off{};
   unsigned char* dmem = nullptr;
@@ -319,6 +327,7 @@ void seg_tables(const oeqb_plan& p, const std::vector<int>& order, const std::ve
   t.off_term = blob_put(t.blob, term);
   t.blob.resize(align16(t.blob.size()));
   t.ngroups = static_cast<int>(bounds.size()) - 1;
+  t.nrun = static_cast<int>(runs.size());
   t.nx = static_cast<int>(xs.size());
   t.npent = static_cast<int>(pent.size());
   t.psize = poff;
@@ -408,6 +417,56 @@ void build_seg(oeqb_plan& p) {
     seg_layout(p, 1, elem, t);
     t.ok = t.smem <= 220 * 1024;
   }
+}
+
+// Lockstep backward: segment-eligible problems whose instructions all span the same number
+// of 32-channel chunks (dividing 16), that use every X irrep, and whose Y is the spherical-
+// harmonic layout (one irrep of each degree 0..L in order).
+void build_lk(oeqb_plan& p) {
+  p.lk = {};
+  p.segl = {};
+  if (!p.segb.ok || p.dtype != 1) return;  // fp64 operands do not fit the register budget
+  if (p.ir2.size() > static_cast<size_t>(kLMaxUnrolled) + 1) return;
+  for (size_t i = 0; i < p.ir2.size(); ++i)
+    if (p.ir2[i].mul != 1 || p.ir2[i].l != static_cast<int>(i)) return;
+  int nch = -1;
+  std::vector<char> used(p.ir1.size(), 0);
+  for (const InstrD& in : p.ins_f) {
+    const int c = in.m1 / 32;
+    if (nch >= 0 && c != nch) return;
+    nch = c;
+    used[in.i1] = 1;
+  }
+  if (nch <= 0 || kLkWarps % nch != 0) return;
+  for (size_t r = 0; r < p.ir1.size(); ++r)
+    if (!used[r] || p.ir1[r].mul != nch * 32) return;
+  std::vector<int> order(p.ins_f.size());
+  for (size_t i = 0; i < order.size(); ++i) order[i] = static_cast<int>(i);
+  std::stable_sort(order.begin(), order.end(), [&](int x, int y) {
+    const InstrD &a = p.ins_f[x], &b = p.ins_f[y];
+    return a.i1 != b.i1 ? a.i1 < b.i1 : a.i2 < b.i2;
+  });
+  const int n = static_cast<int>(order.size());
+  if (p.dtype == 2)
+    seg_tables<double>(p, order, {0, n}, p.segl);
+  else
+    seg_tables<float>(p, order, {0, n}, p.segl);
+  const size_t elem = p.dtype == 2 ? 8 : 4;
+  oeqb_plan::LkCfg& c = p.lk;
+  c.nch = nch;
+  c.rb = kLkWarps / nch;
+  c.offY = static_cast<int>(round_elems(p.L1dim, elem));
+  c.xy_elems = c.offY + static_cast<int>(round_elems(p.L2dim, elem));
+  c.slot_w_off = c.rb * nch * 32 * kSegD;
+  c.slot_elems = c.slot_w_off + (p.shared_w ? 0 : c.rb * nch * 32);
+  const size_t fixed = p.segl.blob.size() + 8 * (4 + 2 * kLkMaxSlots) +
+                       elem * (size_t(2) * c.rb * c.xy_elems + size_t(c.rb) * p.segl.psize +
+                               size_t(kLkWarps) * kLkGy);
+  for (c.nslots = kLkMaxSlots; c.nslots >= 3; --c.nslots) {
+    c.smem = fixed + elem * size_t(c.nslots) * c.slot_elems;
+    if (c.smem <= 220 * 1024) break;
+  }
+  c.ok = c.nslots >= 3;
 }
 
 int parse_descriptor(const void* data, size_t n, oeqb_plan& p) {
@@ -548,6 +607,7 @@ int parse_descriptor(const void* data, size_t n, oeqb_plan& p) {
   p.desc_b = desc_bytes(p, p.grp_b.size(), p.zb_b.size());
   build_row(p);
   build_seg(p);
+  build_lk(p);
   return 0;
 }
 
@@ -577,7 +637,7 @@ void layout_tables(oeqb_plan& p, std::vector<unsigned char>& buf) {
     t->off_witems = put(buf, t->witems);
     t->off_wofs = put(buf, t->wofs);
   }
-  for (auto* t : {&p.segf, &p.segb}) t->dev_off = put(buf, t->blob);
+  for (auto* t : {&p.segf, &p.segb, &p.segl}) t->dev_off = put(buf, t->blob);
   p.off.total = align16(buf.size());
   buf.resize(p.off.total);
 }
@@ -789,6 +849,62 @@ int launch_seg(oeqb_plan& p, int kind, const Args<T>& a, cudaStream_t stream) {
   return 0;
 }
 
+template <class T>
+int launch_lk(oeqb_plan& p, const Args<T>& a, cudaStream_t stream) {
+  const oeqb_plan::SegTable& t = p.segl;
+  const oeqb_plan::LkCfg& c = p.lk;
+  ArgsLk<T> v;
+  v.a = a;
+  v.tables = p.dmem + t.dev_off;
+  v.table_bytes = static_cast<int>(t.blob.size());
+  v.off_run = t.off_run;
+  v.off_grp = t.off_grp;
+  v.off_x = t.off_x;
+  v.off_pent = t.off_pent;
+  v.off_term = t.off_term;
+  v.ninstr = static_cast<int>(p.ins_f.size());
+  v.nrun = t.nrun;
+  v.npent = t.npent;
+  v.psize = t.psize;
+  v.nch = c.nch;
+  v.rb = c.rb;
+  v.nslots = c.nslots;
+  v.offY = c.offY;
+  v.xy_elems = c.xy_elems;
+  v.slot_elems = c.slot_elems;
+  v.slot_w_off = c.slot_w_off;
+  const void* kernel = lk_kernel_ptr<T>();
+  {
+    std::lock_guard<std::mutex> g(p.mu);
+    auto it = p.occ.find(kernel);
+    if (it == p.occ.end()) {
+      if (int rc = allow_max_smem(p.device, kernel)) return rc;
+      int n = 0;
+      OEQB_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kernel, 32 * (kLkWarps + 1),
+                                                              c.smem));
+      if (n <= 0) return fail(OEQB_ERR_UNSUPPORTED, "lockstep kernel does not fit on the device");
+      p.occ.emplace(kernel, n);
+    }
+  }
+  const long long nblk = (a.nitems + c.rb - 1) / c.rb;
+  const long long blocks = std::max<long long>(1, std::min<long long>(nblk, p.sm_count));
+  void* params[] = {&v};
+  OEQB_CUDA(cudaLaunchKernel(kernel, dim3(static_cast<unsigned>(blocks)), dim3(32 * (kLkWarps + 1)),
+                             params, c.smem, stream));
+  return 0;
+}
+
+// Every bulk copy of the lockstep backward is row-granular: rows and base pointers must be
+// 16-byte aligned.
+template <class T>
+bool lk_aligned(const oeqb_plan& p, const Args<T>& a) {
+  const size_t e = sizeof(T);
+  bool ok = aligned16(a.X) && aligned16(a.Y) && aligned16(a.Gz) && aligned16(a.out0) &&
+            (p.L1dim * e) % 16 == 0 && (p.L2dim * e) % 16 == 0 && (p.L3dim * e) % 16 == 0;
+  if (!p.shared_w) ok = ok && aligned16(a.W) && (p.wnumel * e) % 16 == 0;
+  return ok;
+}
+
 struct DeviceGuard {
   int prev = -1;
   explicit DeviceGuard(int dev) {
@@ -834,6 +950,7 @@ int tp_backward_t(oeqb_plan* p, int64_t B, const void* X, void* dX, const void* 
   a.out0 = static_cast<T*>(dX);
   a.out1 = static_cast<T*>(dY);
   a.out2 = static_cast<T*>(dW);
+  if (p->lk.ok && lk_aligned(*p, a)) return launch_lk(*p, a, s);
   if (p->segb.ok) return launch_seg(*p, 1, a, s);
   if (p->row_ok) return launch_row(*p, 1, a, s);
   return launch(*p, batch_kernel_ptr<T>(1, p->uvw, false, kBatch), a, false, false, s);
@@ -1126,6 +1243,8 @@ int oeqb_tp_forward_noalloc(const void* descriptor, size_t nbytes, int device, i
   p.row_ok = false;  // this entry point runs the table-driven forward kernel
   p.segf = {};
   p.segb = {};
+  p.segl = {};
+  p.lk = {};
   std::vector<unsigned char> img;
   layout_tables(p, img);
   const size_t status_off = align16(img.size());

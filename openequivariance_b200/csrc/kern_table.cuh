@@ -3,7 +3,7 @@
 // here and launches them with cudaLaunchKernel.
 #pragma once
 #include "tp_kernels.cuh"
-#include "tp_kernels_seg.cuh"
+#include "tp_kernels_lk.cuh"
 
 namespace oeqb {
 
@@ -21,6 +21,8 @@ const void* row_kernel_ptr(int kind, int nwarps);
 // Channelwise-uvu segment kernels (tp_kernels_seg.cuh); kind 0 = forward, 1 = backward.
 template <class T>
 const void* seg_kernel_ptr(int kind);
+template <class T>
+const void* lk_kernel_ptr();
 
 #define OEQB_PICK4(K, T, P)                                                     \
   (uvw ? (db ? (const void*)K<T, true, true, P> : (const void*)K<T, true, false, P>) \
@@ -47,7 +49,9 @@ const void* seg_kernel_ptr(int kind);
   template <>                                                                   \
   const void* seg_kernel_ptr<T>(int kind) {                                     \
     return kind == 0 ? (const void*)tp_fwd_seg<T> : (const void*)tp_bwd_seg<T, 16>; \
-  }
+  }                                                                               \
+  template <>                                                                     \
+  const void* lk_kernel_ptr<T>() { return (const void*)tp_bwd_lk<T>; }
 
 #define OEQB_DEFINE_DET_TABLE(T, WITH_KAHAN)                                    \
   template <>                                                                   \

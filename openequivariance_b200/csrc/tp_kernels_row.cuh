@@ -44,7 +44,11 @@ struct ArgsRow {
   int off_stage, off_dxp, off_dyp, ws_elems;  // per-warp scratch layout
 };
 
-constexpr long long kWaitLimit = 1LL << 28;  // ~seconds of polling; never reached normally
+// Bounded barrier waits: a wait gives up after kWaitNs of device time (never reached in
+// normal operation, where a wait lasts microseconds) and raises status flag 3.  Once the flag
+// is 3, later waits give up at once, so a kernel whose pipeline lost a phase runs to its end
+// in milliseconds instead of timing out wait by wait.
+constexpr unsigned long long kWaitNs = 2000000000ull;
 
 __device__ __forceinline__ unsigned smem_u32(const void* p) {
   return static_cast<unsigned>(__cvta_generic_to_shared(p));
@@ -80,12 +84,25 @@ __device__ __forceinline__ bool mbar_try_wait(unsigned long long* bar, unsigned 
   return ok != 0;
 }
 
+__device__ __forceinline__ unsigned long long global_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;\n" : "=l"(t));
+  return t;
+}
+
 // Bounded wait: returns false (and raises the status flag) if the phase never completes.
 __device__ __forceinline__ bool mbar_wait(unsigned long long* bar, unsigned parity, int* status) {
-  for (long long i = 0; i < kWaitLimit; ++i)
-    if (mbar_try_wait(bar, parity)) return true;
-  if (status) atomicCAS(status, 0, 3);
-  return false;
+  if (mbar_try_wait(bar, parity)) return true;
+  const unsigned long long t0 = global_ns();
+  for (;;) {
+    for (int i = 0; i < 32; ++i)
+      if (mbar_try_wait(bar, parity)) return true;
+    if (status && *reinterpret_cast<volatile int*>(status) == 3) return false;
+    if (global_ns() - t0 > kWaitNs) {
+      if (status) atomicCAS(status, 0, 3);
+      return false;
+    }
+  }
 }
 
 __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, unsigned bytes,
