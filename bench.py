@@ -37,7 +37,7 @@ HBM_FALLBACK_GBS = 6650.0
 def _args():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=["c2", "c2ml"], default="c2")
@@ -66,61 +66,108 @@ def _traffic(kernel_key):
 
 
 class ClockSampler:
-    """Samples nvidia-smi clocks / throttle reasons while the timed region runs."""
+    """Samples SM clocks and clock-event (throttle) reasons while the timed region runs.
 
+    NVML is polled every 10 ms from a thread (nvidia-smi's own data source, without its
+    start-up delay); if NVML is unavailable, an ``nvidia-smi -lms 100`` loop is read instead.
+    """
+
+    REASON_BITS = {"sw_power_cap": 0x4, "hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20,
+                   "hw_thermal_slowdown": 0x40}
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
     def __init__(self, device_index):
         self.dev = device_index
-        self.lines = []
+        self.samples = []  # (sm_mhz, max_mhz, reasons set)
         self.proc = None
+        self.stop = threading.Event()
+        self.thread = None
+
+    def _nvml_handle(self):
+        import pynvml
+        import torch
+
+        pynvml.nvmlInit()
+        want = str(torch.cuda.get_device_properties(self.dev).uuid).lower()
+        for i in range(pynvml.nvmlDeviceGetCount()):
+            h = pynvml.nvmlDeviceGetHandleByIndex(i)
+            u = pynvml.nvmlDeviceGetUUID(h)
+            u = (u.decode() if isinstance(u, bytes) else u).lower()
+            if u.endswith(want):
+                return pynvml, h
+        return pynvml, pynvml.nvmlDeviceGetHandleByIndex(self.dev)
+
+    def _poll_nvml(self, nv, h):
+        get_reasons = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+            nv.nvmlDeviceGetCurrentClocksThrottleReasons
+        mx = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
+        while not self.stop.is_set():
+            try:
+                sm = nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)
+                bits = get_reasons(h)
+                rs = {n for n, b in self.REASON_BITS.items() if bits & b}
+                self.samples.append((float(sm), float(mx), rs))
+            except Exception:
+                pass
+            self.stop.wait(0.01)
+
+    def _read_smi(self):
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.proc.stdout:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                rs = {n for n, v in zip(names, parts[5:9]) if v.lower() == "active"}
+                self.samples.append((float(parts[1]), float(parts[2]), rs))
+            except ValueError:
+                continue
 
     def __enter__(self):
+        try:
+            nv, h = self._nvml_handle()
+            self.thread = threading.Thread(target=self._poll_nvml, args=(nv, h), daemon=True)
+            self.thread.start()
+            while not self.samples and self.thread.is_alive():
+                time.sleep(0.005)
+            return self
+        except Exception:
+            pass
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
                  "-lms", "100", "-i", str(self.dev)],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread = threading.Thread(target=self._read_smi, daemon=True)
             self.thread.start()
+            t0 = time.time()
+            while not self.samples and time.time() - t0 < 5:
+                time.sleep(0.01)
         except Exception:
             self.proc = None
         return self
 
-    def _read(self):
-        for line in self.proc.stdout:
-            self.lines.append(line.strip())
-
     def __exit__(self, *exc):
+        self.stop.set()
         if self.proc is not None:
             self.proc.terminate()
             try:
                 self.proc.wait(timeout=5)
             except Exception:
                 self.proc.kill()
+        if self.thread is not None:
+            self.thread.join(timeout=2)
 
     def summary(self):
-        sms, maxes, reasons = [], [], set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
-            parts = [p.strip() for p in ln.split(",")]
-            if len(parts) < 9:
-                continue
-            try:
-                sms.append(float(parts[1]))
-                maxes.append(float(parts[2]))
-            except ValueError:
-                continue
-            for n, v in zip(names, parts[5:9]):
-                if v.lower() == "active":
-                    reasons.add(n)
-        if not sms:
+        if not self.samples:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
-        sms.sort()
-        return {"sm_mhz": sms[len(sms) // 2], "sm_max_mhz": max(maxes),
-                "reasons": sorted(reasons), "samples": len(sms)}
+        sms = sorted(s[0] for s in self.samples)
+        reasons = set().union(*(s[2] for s in self.samples))
+        return {"sm_mhz": sms[len(sms) // 2], "sm_max_mhz": max(s[1] for s in self.samples),
+                "reasons": sorted(reasons), "samples": len(sms),
+                "source": "nvml" if self.proc is None else "nvidia-smi"}
 
 
 def _dist():
@@ -173,6 +220,11 @@ def _sh_inputs(rows, lmax, seed, dtype, device):
 
 
 # ------------------------------------------------------------------------------ TP workload
+
+
+def _workload_desc(name, problem):
+    return (f"{name}: batch uvu CG tensor product fwd+bwd ({len(problem.instructions)} paths, "
+            f"X={problem.irreps_in1}, Y=SH l<=3, L3_dim={problem.irreps_out.dim})")
 
 
 def bench_tp(args, world, rank, local):
@@ -266,15 +318,13 @@ def bench_tp(args, world, rank, local):
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        cpu = cpu_baseline_tp(problem, budget_s=15.0)
+        cpu = cpu_baseline_tp(problem, budget_s=10.0)
 
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": K,
         "warmup": args.warmup, "ms_per_step": elapsed_ms / K, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": f"{args.workload}: batch uvu CG tensor product fwd+bwd "
-                               f"({len(problem.instructions)} paths, X={problem.irreps_in1}, "
-                               f"Y=SH l<=3, L3_dim={d3})",
+        "config": {"workload": _workload_desc(args.workload, problem),
                    "rows_per_gpu": B, "global_rows": B * world,
                    "l2": "inputs larger than L2 (no flush needed)",
                    "parallelism": f"dp{world} (independent row shards)"},
@@ -293,7 +343,7 @@ def bench_tp(args, world, rank, local):
     return line
 
 
-def cpu_baseline_tp(problem, budget_s=15.0, rows=None):
+def cpu_baseline_tp(problem, budget_s=10.0, rows=None):
     """Times the CPU port on a bounded sample of the same workload."""
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import cpu_baseline as CB
@@ -305,14 +355,21 @@ def cpu_baseline_tp(problem, budget_s=15.0, rows=None):
         [(m.mul, m.ir.l, m.ir.p) for m in problem.irreps_out],
         [(i.i_in1, i.i_in2, i.i_out, i.connection_mode, True) for i in problem.instructions],
         shared_weights=problem.shared_weights)
+    # Grow the batch until one call takes about a second, then repeat it until the sample
+    # holds about budget_s seconds of CPU work.
     n = rows or 256
     t, threads = CB.time_tp_fwd_bwd(p, n)
-    while rows is None and t < budget_s / 8 and n < 50000:
+    while rows is None and t < 1.0 and n < 50000:
         n *= 2
         t, threads = CB.time_tp_fwd_bwd(p, n)
-    return {"value": n / t, "unit": UNIT, "cores": threads, "kind": "port",
-            "sample": f"{n} rows of the same workload, forward+backward, float32 torch-CPU "
-                      f"einsums ({t:.2f} s)"}
+    total_t, total_n = t, n
+    while total_t < budget_s:
+        t, threads = CB.time_tp_fwd_bwd(p, n)
+        total_t += t
+        total_n += n
+    return {"value": total_n / total_t, "unit": UNIT, "cores": threads, "kind": "port",
+            "sample": f"{total_n} rows of the same workload ({n}-row batches), forward+backward, "
+                      f"float32 torch-CPU einsums, {total_t:.1f} s"}
 
 
 # ----------------------------------------------------------------------------- reference
@@ -349,9 +406,9 @@ def bench_reference(args, world, rank):
         "warmup": args.warmup, "ms_per_step": 1e3 * total / args.steps, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "impl": "reference",
-        "config": {"workload": f"{args.workload}: batch uvu CG tensor product fwd+bwd "
-                               "(CPU port of the reference's e3nn path)",
-                   "rows_per_step": rows},
+        "config": {"workload": _workload_desc(args.workload, problem),
+                   "rows_per_step": rows,
+                   "implementation": "CPU port of the reference's e3nn path (torch-CPU einsums)"},
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
                          "sample": f"{rows} rows per step, forward+backward, float32"},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
