@@ -17,6 +17,7 @@ __version__ = "0.1.0"
 if os.environ.get("OEQ_NOTORCH", "0") != "1":
     import torch
 
+    from .symmetric_contraction import SymmetricContraction
     from .tensor_product import TensorProduct
     from .tensor_product_conv import TensorProductConv
     from .utils import torch_to_oeq_dtype, transpose_irreps
@@ -51,6 +52,7 @@ __all__ = [
     "Irreps",
     "TensorProduct",
     "TensorProductConv",
+    "SymmetricContraction",
     "torch_to_oeq_dtype",
     "torch_ext_so_path",
     "jax",

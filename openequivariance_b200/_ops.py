@@ -166,6 +166,43 @@ def _register_conv():
                                     setup_context=setup_dbl)
 
 
+def _register_sc():
+    """group_gemm (reference schema, ``SymmetricContraction.py:339-414`` formulas) and the
+    fused contraction ops' fake kernels."""
+    lib = "libtorch_tp_jit"
+    op = torch.ops.libtorch_tp_jit.group_gemm
+
+    @torch.library.register_fake(f"{lib}::group_gemm")
+    def _fake_gg(A, B, ragged_counts, num_W, batch_size, m, k, ragged_inner):
+        if ragged_inner == 0:
+            return A.new_empty(B.shape[0], batch_size, m)
+        return A.new_empty(num_W, batch_size, m, k)
+
+    def setup_gg(ctx, inputs, output):
+        ctx.A, ctx.B, ctx.counts, ctx.num_W, ctx.batch, ctx.m, ctx.k, ctx.inner = inputs
+
+    def grad_gg(ctx, g):
+        # ragged_inner == 0: C = A B  -> dA = sum_r g (x) B (inner form), dB = A^T g.
+        # ragged_inner == 1: C = sum_r A (x) B -> dA = C-shaped g applied to B, dB = g^T A.
+        if ctx.inner == 0:
+            gA = op(g, ctx.B, ctx.counts, ctx.num_W, ctx.batch, ctx.m, ctx.k, 1)
+            gB = op(ctx.A.transpose(2, 3), g, ctx.counts, ctx.num_W, ctx.batch, ctx.k, ctx.m, 0)
+        else:
+            gA = op(g, ctx.B, ctx.counts, ctx.num_W, ctx.batch, ctx.m, ctx.k, 0)
+            gB = op(g.transpose(2, 3), ctx.A, ctx.counts, ctx.num_W, ctx.batch, ctx.k, ctx.m, 0)
+        return gA, gB, None, None, None, None, None, None
+
+    torch.library.register_autograd(f"{lib}::group_gemm", grad_gg, setup_context=setup_gg)
+
+    @torch.library.register_fake("oeqb200::sc_forward")
+    def _fake_scf(x, perm, elem_sorted, coef, out_col, out_step, out_dim, degree):
+        return x.new_empty(x.shape[0], out_dim)
+
+    @torch.library.register_fake("oeqb200::sc_backward")
+    def _fake_scb(x, perm, elem_sorted, elem_offsets, coef, grad_out, out_col, out_step, degree):
+        return torch.empty_like(x), torch.empty_like(coef)
+
+
 def _register_autocast():
     for name in ("jit_tp_forward", "jit_tp_backward", "jit_tp_double_backward",
                  "jit_conv_forward", "jit_conv_backward", "jit_conv_double_backward"):
@@ -182,5 +219,6 @@ def ensure_registered() -> None:
     _ext.load_torch_ops()
     _register_tp()
     _register_conv()
+    _register_sc()
     _register_autocast()
     _registered = True

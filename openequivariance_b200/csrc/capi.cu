@@ -33,6 +33,7 @@ template <class T>
 const void* seg_kernel_ptr(int kind);
 template <class T>
 const void* lk_kernel_ptr();
+int set_error(int code, const std::string& msg);
 }  // namespace oeqb
 
 using namespace oeqb;
@@ -49,6 +50,13 @@ int fail(int code, const std::string& msg) {
   g_last_error = msg;
   return code;
 }
+
+}  // namespace
+
+// Error reporting shared with the other translation units of the library (kern_sc.cu).
+int oeqb::set_error(int code, const std::string& msg) { return fail(code, msg); }
+
+namespace {
 
 #define OEQB_CUDA(expr)                                                                  \
   do {                                                                                   \

@@ -268,7 +268,94 @@ std::tuple<Tensor, Tensor, Tensor, Tensor> jit_conv_double_backward(
   return {L1_grad, L2_grad, W_grad, L3_dgrad};
 }
 
+// ----------------------------- symmetric contraction ----------------------------------
+
+int dtype_code(const Tensor& t) {
+  TORCH_CHECK(t.scalar_type() == at::kFloat || t.scalar_type() == at::kDouble,
+              "expected float32 or float64, got ", t.scalar_type());
+  return t.scalar_type() == at::kDouble ? 2 : 1;
+}
+
+// group_gemm (torch_core.hpp:653-684): same checks and output shapes; ragged_counts may live
+// on the host (as the reference's bincount does) or on the device.
+Tensor group_gemm(Tensor A, Tensor B, Tensor ragged_counts, int64_t num_W, int64_t batch_size,
+                  int64_t m, int64_t k, int64_t ragged_inner) {
+  TORCH_CHECK(A.scalar_type() == B.scalar_type(), "group_gemm: A and B must have the same dtype");
+  TORCH_CHECK(ragged_counts.scalar_type() == at::kLong, "group_gemm: ragged_counts must be int64");
+  TORCH_CHECK(A.is_cuda() && B.is_cuda(), "group_gemm: A and B must be on the GPU");
+  const c10::cuda::CUDAGuard guard(A.device());
+  Tensor Ac = A.contiguous(), Bc = B.contiguous();
+  Tensor counts = ragged_counts.to(A.device(), /*non_blocking=*/false).contiguous();
+  Tensor offsets = at::zeros({num_W + 1}, counts.options());
+  if (num_W > 0) offsets.narrow(0, 1, num_W).copy_(at::cumsum(counts.narrow(0, 0, num_W), 0));
+  Tensor C;
+  int64_t rows;
+  if (ragged_inner == 0) {
+    rows = B.size(0);
+    C = at::empty({rows, batch_size, m}, A.options());
+  } else {
+    rows = A.size(0);
+    C = at::empty({num_W, batch_size, m, k}, A.options());
+  }
+  check_rc(oeqb_group_gemm(dtype_code(A), Ac.data_ptr(), Bc.data_ptr(),
+                           offsets.data_ptr<int64_t>(), static_cast<int>(num_W), rows,
+                           static_cast<int>(batch_size), static_cast<int>(m), static_cast<int>(k),
+                           static_cast<int>(ragged_inner), C.data_ptr(), stream_of(A)));
+  return C;
+}
+
+std::vector<int> int_list(at::IntArrayRef v) { return std::vector<int>(v.begin(), v.end()); }
+
+// Fused symmetric contraction (this package's op; no reference schema).
+Tensor sc_forward(Tensor x, Tensor perm, Tensor elem_sorted, Tensor coef, at::IntArrayRef out_col,
+                  at::IntArrayRef out_step, int64_t out_dim, int64_t degree) {
+  TORCH_CHECK(x.is_cuda() && x.dim() == 3, "sc_forward: x must be a [N, C, K] GPU tensor");
+  TORCH_CHECK(coef.dim() == 4 && coef.scalar_type() == x.scalar_type(), "sc_forward: coef must be [E, C, M, DT] of x's dtype");
+  const c10::cuda::CUDAGuard guard(x.device());
+  Tensor xc = x.contiguous(), cc = coef.contiguous();
+  Tensor out = at::empty({x.size(0), out_dim}, x.options());
+  const auto col = int_list(out_col), step = int_list(out_step);
+  TORCH_CHECK(col.size() == step.size(), "sc_forward: out_col / out_step length mismatch");
+  check_rc(oeqb_sc_forward(dtype_code(x), x.size(0), static_cast<int>(x.size(1)),
+                           static_cast<int>(x.size(2)), static_cast<int>(degree),
+                           static_cast<int>(coef.size(3)), static_cast<int>(col.size()), col.data(),
+                           step.data(), out_dim, xc.data_ptr(), perm.data_ptr<int64_t>(),
+                           elem_sorted.data_ptr<int64_t>(), cc.data_ptr(), out.data_ptr(),
+                           stream_of(x)));
+  return out;
+}
+
+std::tuple<Tensor, Tensor> sc_backward(Tensor x, Tensor perm, Tensor elem_sorted,
+                                       Tensor elem_offsets, Tensor coef, Tensor grad_out,
+                                       at::IntArrayRef out_col, at::IntArrayRef out_step,
+                                       int64_t degree) {
+  TORCH_CHECK(x.is_cuda() && x.dim() == 3, "sc_backward: x must be a [N, C, K] GPU tensor");
+  const c10::cuda::CUDAGuard guard(x.device());
+  Tensor xc = x.contiguous(), cc = coef.contiguous(), gc = grad_out.contiguous();
+  Tensor gx = at::empty_like(xc);
+  Tensor gcoef = at::empty_like(cc);
+  const auto col = int_list(out_col), step = int_list(out_step);
+  check_rc(oeqb_sc_backward(dtype_code(x), x.size(0), static_cast<int>(x.size(1)),
+                            static_cast<int>(x.size(2)), static_cast<int>(degree),
+                            static_cast<int>(coef.size(3)), static_cast<int>(col.size()),
+                            col.data(), step.data(), gc.size(1), static_cast<int>(coef.size(0)),
+                            xc.data_ptr(), perm.data_ptr<int64_t>(), elem_sorted.data_ptr<int64_t>(),
+                            elem_offsets.data_ptr<int64_t>(), cc.data_ptr(), gc.data_ptr(),
+                            gx.data_ptr(), gcoef.data_ptr(), stream_of(x)));
+  return {gx, gcoef};
+}
+
 }  // namespace
+
+TORCH_LIBRARY(oeqb200, m) {
+  m.def("sc_forward(Tensor x, Tensor perm, Tensor elem_sorted, Tensor coef, int[] out_col, int[] out_step, int out_dim, int degree) -> Tensor");
+  m.def("sc_backward(Tensor x, Tensor perm, Tensor elem_sorted, Tensor elem_offsets, Tensor coef, Tensor grad_out, int[] out_col, int[] out_step, int degree) -> (Tensor, Tensor)");
+}
+
+TORCH_LIBRARY_IMPL(oeqb200, CUDA, m) {
+  m.impl("sc_forward", &sc_forward);
+  m.impl("sc_backward", &sc_backward);
+}
 
 TORCH_LIBRARY(libtorch_tp_jit, m) {
   m.def("jit_tp_forward(Tensor json_bytes, int hash, Tensor L1_in, Tensor L2_in, Tensor W, int L3_dim) -> Tensor");
@@ -277,6 +364,7 @@ TORCH_LIBRARY(libtorch_tp_jit, m) {
   m.def("jit_conv_forward(Tensor json_bytes, int hash, Tensor L1_in, Tensor L2_in, Tensor W, int L3_dim, Tensor rows, Tensor cols, Tensor workspace, Tensor transpose_perm) -> Tensor");
   m.def("jit_conv_backward(Tensor json_bytes, int hash, Tensor L1_in, Tensor L2_in, Tensor W, Tensor L3_grad, Tensor rows, Tensor cols, Tensor workspace, Tensor transpose_perm) -> (Tensor, Tensor, Tensor)");
   m.def("jit_conv_double_backward(Tensor json_bytes, int hash, Tensor L1_in, Tensor L2_in, Tensor W, Tensor L3_grad, Tensor L1_dgrad, Tensor L2_dgrad, Tensor W_dgrad, Tensor rows, Tensor cols, Tensor workspace, Tensor transpose_perm) -> (Tensor, Tensor, Tensor, Tensor)");
+  m.def("group_gemm(Tensor A, Tensor B, Tensor ragged_counts, int num_W, int batch_size, int m, int k, int ragged_inner) -> Tensor");
 }
 
 TORCH_LIBRARY_IMPL(libtorch_tp_jit, CUDA, m) {
@@ -286,4 +374,5 @@ TORCH_LIBRARY_IMPL(libtorch_tp_jit, CUDA, m) {
   m.impl("jit_conv_forward", &jit_conv_forward);
   m.impl("jit_conv_backward", &jit_conv_backward);
   m.impl("jit_conv_double_backward", &jit_conv_double_backward);
+  m.impl("group_gemm", &group_gemm);
 }
