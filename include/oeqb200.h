@@ -122,27 +122,26 @@ int oeqb_conv_double_backward(oeqb_plan* plan, const void* L1_in, const void* L2
  * each (node, channel) feature vector.  The caller passes its coefficients on the distinct
  * monomials: coef [num_elements, channels, m, dt] with m = k + k(k+1)/2 [+ k(k+1)(k+2)/6 for
  * degree 3], monomials ordered by degree, then lexicographically by (a <= b <= c), and dt
- * padded output components per (node, channel) (4 or 16; the first nout are used).  Nodes are
- * visited in the order perm [nodes] (sorted by element); elem_sorted[i] is the element of
- * node perm[i].  x is [nodes, channels, k]; output component o of channel c of node n is
+ * padded output components per (node, channel) (4 or 16; the first nout are used).  perm
+ * [nodes] lists the nodes sorted by element and elem_offsets [num_elements + 1] gives each
+ * element's range in it.  x is [nodes, channels, k]; output component o of channel c of node n is
  * written to out[n * out_dim + out_col[o] + c * out_step[o]].  Supported: k in {4, 9},
  * degree 1..3, float32 / float64 (dtype 1 / 2); dt = 16 for float32 only.  No host
  * synchronisation. */
 int oeqb_sc_forward(int dtype, int64_t nodes, int channels, int k, int degree, int dt, int nout,
-                    const int* out_col, const int* out_step, int64_t out_dim, const void* x,
-                    const int64_t* perm, const int64_t* elem_sorted, const void* coef, void* out,
-                    void* stream);
+                    const int* out_col, const int* out_step, int64_t out_dim, int num_elements,
+                    const void* x, const int64_t* perm, const int64_t* elem_offsets,
+                    const void* coef, void* out, void* stream);
 
 /* Gradients of oeqb_sc_forward for the upstream gradient grad_out (laid out like out):
  * grad_x [nodes, channels, k] (skipped if NULL) and grad_coef [num_elements, channels, m, dt]
- * (skipped if NULL; padding columns are written as zero-weighted sums).  elem_offsets
- * [num_elements + 1] gives each element's range in the sorted order.  Sums are taken in a
- * fixed order: results are bitwise reproducible. */
+ * (skipped if NULL; padding columns are written as zero-weighted sums).  Sums are taken in
+ * a fixed order: results are bitwise reproducible. */
 int oeqb_sc_backward(int dtype, int64_t nodes, int channels, int k, int degree, int dt, int nout,
                      const int* out_col, const int* out_step, int64_t out_dim, int num_elements,
-                     const void* x, const int64_t* perm, const int64_t* elem_sorted,
-                     const int64_t* elem_offsets, const void* coef, const void* grad_out,
-                     void* grad_x, void* grad_coef, void* stream);
+                     const void* x, const int64_t* perm, const int64_t* elem_offsets,
+                     const void* coef, const void* grad_out, void* grad_x, void* grad_coef,
+                     void* stream);
 
 /* Ragged grouped GEMM of the reference's group_gemm op (extension/group_mm.hpp:38-141),
  * row-major.  Rows are grouped contiguously: group g owns rows [offsets[g], offsets[g+1])

@@ -195,11 +195,11 @@ def _register_sc():
     torch.library.register_autograd(f"{lib}::group_gemm", grad_gg, setup_context=setup_gg)
 
     @torch.library.register_fake("oeqb200::sc_forward")
-    def _fake_scf(x, perm, elem_sorted, coef, out_col, out_step, out_dim, degree):
+    def _fake_scf(x, perm, elem_offsets, coef, out_col, out_step, out_dim, degree):
         return x.new_empty(x.shape[0], out_dim)
 
     @torch.library.register_fake("oeqb200::sc_backward")
-    def _fake_scb(x, perm, elem_sorted, elem_offsets, coef, grad_out, out_col, out_step, degree):
+    def _fake_scb(x, perm, elem_offsets, coef, grad_out, out_col, out_step, degree):
         return torch.empty_like(x), torch.empty_like(coef)
 
 

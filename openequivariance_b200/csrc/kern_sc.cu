@@ -43,14 +43,31 @@ int sc_launch(int kind, const ArgsSc<T>& a, cudaStream_t s) {
     return 0;
   }
   if (ntiles == 0) return 0;
-  // Two resident CTAs per SM across the channel blocks.
-  const long long want = std::max<long long>(1, 2LL * sm_count() / cblocks);
-  const dim3 grid(static_cast<unsigned>(std::min(ntiles, want)), cblocks);
-  if (kind == 0)
-    sc_fwd_kernel<T, K, DT><<<grid, kScWarps * 32, 0, s>>>(a);
-  else
-    sc_bwd_dx_kernel<T, K, DT><<<grid, kScWarps * 32, 0, s>>>(a);
-  SC_CUDA(cudaGetLastError());
+  const void* fn = kind == 0 ? reinterpret_cast<const void*>(sc_fwd_kernel<T, K, DT>)
+                             : reinterpret_cast<const void*>(sc_bwd_dx_kernel<T, K, DT>);
+  const size_t smem = sc_smem_bytes<T, K, DT>(a.m, a.num_elements);
+  int per_sm = 0;
+  {
+    static std::mutex mu;
+    static std::set<std::pair<int, const void*>> done;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    std::lock_guard<std::mutex> g(mu);
+    if (!done.count({dev, fn})) {
+      SC_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+      done.insert({dev, fn});
+    }
+  }
+  if (smem > 200 * 1024) return set_error(OEQB_ERR_UNSUPPORTED, "symmetric contraction: shapes exceed shared memory");
+  SC_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, kScWarps * 32, smem));
+  if (per_sm <= 0) return set_error(OEQB_ERR_UNSUPPORTED, "symmetric contraction kernel does not fit");
+  // Persistent over node tiles: resident CTAs per SM, spread across the channel blocks.
+  const long long tiles = (a.nodes + 32 * sc_npl(sizeof(T)) - 1) / (32 * sc_npl(sizeof(T))) +
+                          a.num_elements;
+  const long long want = std::max<long long>(1, static_cast<long long>(per_sm) * sm_count() / cblocks);
+  const dim3 grid(static_cast<unsigned>(std::min(tiles, want)), cblocks);
+  void* params[] = {const_cast<ArgsSc<T>*>(&a)};
+  SC_CUDA(cudaLaunchKernel(fn, grid, dim3(kScWarps * 32), params, smem, s));
   return 0;
 }
 
@@ -69,7 +86,7 @@ int sc_dispatch(int kind, const ArgsSc<T>& a, int dt, cudaStream_t s) {
 
 template <class T>
 int sc_common(ArgsSc<T>& a, int dt, int nout, const int* out_col, const int* out_step) {
-  if (a.nodes < 0 || a.channels <= 0 || a.degree < 1 || a.degree > 3)
+  if (a.nodes < 0 || a.channels <= 0 || a.degree < 1 || a.degree > 3 || a.num_elements <= 0)
     return set_error(OEQB_ERR_INVALID, "symmetric contraction: bad sizes or degree (1..3)");
   if (dt != 4 && dt != 16) return set_error(OEQB_ERR_UNSUPPORTED, "symmetric contraction: dt must be 4 or 16");
   if (nout < 1 || nout > dt) return set_error(OEQB_ERR_INVALID, "symmetric contraction: nout must be in [1, dt]");
@@ -87,15 +104,16 @@ int sc_common(ArgsSc<T>& a, int dt, int nout, const int* out_col, const int* out
 extern "C" {
 
 int oeqb_sc_forward(int dtype, int64_t nodes, int channels, int k, int degree, int dt, int nout,
-                    const int* out_col, const int* out_step, int64_t out_dim, const void* x,
-                    const int64_t* perm, const int64_t* elem_sorted, const void* coef, void* out,
-                    void* stream) {
+                    const int* out_col, const int* out_step, int64_t out_dim, int num_elements,
+                    const void* x, const int64_t* perm, const int64_t* elem_offsets,
+                    const void* coef, void* out, void* stream) {
   auto run = [&](auto tag) -> int {
     using T = decltype(tag);
     ArgsSc<T> a{};
     a.x = static_cast<const T*>(x);
     a.perm = perm;
-    a.elem = elem_sorted;
+    a.eoff = elem_offsets;
+    a.num_elements = num_elements;
     a.coef = static_cast<const T*>(coef);
     a.out = static_cast<T*>(out);
     a.nodes = nodes;
@@ -113,16 +131,15 @@ int oeqb_sc_forward(int dtype, int64_t nodes, int channels, int k, int degree, i
 
 int oeqb_sc_backward(int dtype, int64_t nodes, int channels, int k, int degree, int dt, int nout,
                      const int* out_col, const int* out_step, int64_t out_dim, int num_elements,
-                     const void* x, const int64_t* perm, const int64_t* elem_sorted,
-                     const int64_t* elem_offsets, const void* coef, const void* grad_out,
-                     void* grad_x, void* grad_coef, void* stream) {
+                     const void* x, const int64_t* perm, const int64_t* elem_offsets,
+                     const void* coef, const void* grad_out, void* grad_x, void* grad_coef,
+                     void* stream) {
   auto run = [&](auto tag) -> int {
     using T = decltype(tag);
     ArgsSc<T> a{};
     a.x = static_cast<const T*>(x);
     a.gout = static_cast<const T*>(grad_out);
     a.perm = perm;
-    a.elem = elem_sorted;
     a.eoff = elem_offsets;
     a.coef = static_cast<const T*>(coef);
     a.out = static_cast<T*>(grad_x);

@@ -12,16 +12,19 @@
 // K(K+1)(K+2)/6 rows (219 for K = 9).  Monomials are enumerated by degree, then in
 // lexicographic order of (a, b, c); the kernels walk the same nested loops.
 //
-// Work mapping (forward, dX): nodes are processed in element-sorted order (perm), a warp is
-// one channel and its lanes are 32 consecutive sorted nodes, so the coefficients of (e, c)
-// are warp-uniform broadcast loads; a tile that straddles two elements loops over them.
-// x (and dZ) rows are staged through shared memory so global accesses are row-contiguous.
+// Work mapping (forward, dX): nodes are processed in element-sorted order (perm) in tiles of
+// 32 (float64) or 64 (float32) nodes of one element; a warp is one channel, its lanes the
+// tile's nodes, and the warp's coefficients of (element, channel) sit in a shared-memory
+// cache read by broadcast loads.  x (and dZ) rows are staged through shared memory so global
+// accesses are row-contiguous.
 // Coefficient gradient: one CTA per (element, channel), each thread owns monomials and
 // accumulates over the element's nodes in sorted order (deterministic).
 #pragma once
 
 #include <cuda_runtime.h>
 #include <stdint.h>
+
+#include <type_traits>
 
 namespace oeqb {
 
@@ -38,8 +41,7 @@ struct ArgsSc {
   const T* x;              // [N, C, K]
   const T* gout;           // [N, out_dim] (backward)
   const int64_t* perm;     // sorted position -> node
-  const int64_t* elem;     // sorted position -> element
-  const int64_t* eoff;     // [E + 1] sorted offsets of each element (coefficient gradient)
+  const int64_t* eoff;     // [E + 1] offsets of each element's range in the sorted order
   const T* coef;           // [E, C, M, DT]
   T* out;                  // forward: [N, out_dim]; backward: dX [N, C, K]
   T* dcoef;                // [E, C, M, DT]
@@ -66,13 +68,39 @@ __host__ __device__ constexpr int sc_idx3(int p, int q, int r) {
   return n + (r - q);
 }
 
-// Broadcast load of the DT coefficients of one monomial (16-byte vector loads).
+// Stages rows [pos0, pos0 + R) of the sorted order, channels [c0, c0 + kScWarps), into
+// xs[R][kScWarps * K + 1] (the pad keeps lane-strided reads conflict-free).
+template <class T, int K, int R>
+__device__ __forceinline__ void sc_stage_x(const ArgsSc<T>& a, T* xs, long long pos0, int nrows,
+                                           int c0) {
+  constexpr int ROW = kScWarps * K;
+  const int nc = min(kScWarps, a.channels - c0);
+  for (int e = threadIdx.x; e < R * ROW; e += blockDim.x) {
+    const int r = e / ROW, q = e - r * ROW;
+    T v = T(0);
+    if (r < nrows && q < nc * K) v = a.x[(a.perm[pos0 + r] * a.channels + c0) * K + q];
+    xs[r * (ROW + 1) + q] = v;
+  }
+}
+
+// Copies the coefficients of (element e, channel c) into this warp's cache.
 template <class T, int DT>
-__device__ __forceinline__ void sc_ldcoef(T (&d)[DT], const T* p) {
+__device__ __forceinline__ void sc_load_coef(const ArgsSc<T>& a, T* cache, int e, int c, int lane) {
+  const T* src = a.coef + (static_cast<size_t>(e) * a.channels + c) * a.m * DT;
+  constexpr int V = 16 / sizeof(T);
+  const int nvec = a.m * DT / V;
+  for (int i = lane; i < nvec; i += 32)
+    reinterpret_cast<uint4*>(cache)[i] = __ldg(reinterpret_cast<const uint4*>(src) + i);
+  __syncwarp();
+}
+
+// Broadcast load of the DT coefficients of one monomial from the warp's cache.
+template <class T, int DT>
+__device__ __forceinline__ void sc_ldcache(T (&d)[DT], const T* p) {
   if constexpr (sizeof(T) == 4) {
 #pragma unroll
     for (int q = 0; q < DT / 4; ++q) {
-      const float4 t = __ldg(reinterpret_cast<const float4*>(p) + q);
+      const float4 t = reinterpret_cast<const float4*>(p)[q];
       d[4 * q] = t.x;
       d[4 * q + 1] = t.y;
       d[4 * q + 2] = t.z;
@@ -81,185 +109,276 @@ __device__ __forceinline__ void sc_ldcoef(T (&d)[DT], const T* p) {
   } else {
 #pragma unroll
     for (int q = 0; q < DT / 2; ++q) {
-      const double2 t = __ldg(reinterpret_cast<const double2*>(p) + q);
+      const double2 t = reinterpret_cast<const double2*>(p)[q];
       d[2 * q] = t.x;
       d[2 * q + 1] = t.y;
     }
   }
 }
 
-// Stages rows [pos0, pos0 + 32) of the sorted order, channels [c0, c0 + kScWarps), into
-// xs[32][kScWarps * K + 1] (the pad keeps lane-strided reads conflict-free).
-template <class T, int K>
-__device__ __forceinline__ void sc_stage_x(const ArgsSc<T>& a, T* xs, long long pos0, int c0) {
-  constexpr int ROW = kScWarps * K;
-  const int nc = min(kScWarps, a.channels - c0);
-  for (int e = threadIdx.x; e < 32 * ROW; e += blockDim.x) {
-    const int r = e / ROW, q = e - r * ROW;
-    const long long pos = pos0 + r;
-    T v = T(0);
-    if (pos < a.nodes && q < nc * K) v = a.x[(a.perm[pos] * a.channels + c0) * K + q];
-    xs[r * (ROW + 1) + q] = v;
+__host__ __device__ constexpr int sc_npl(int elem) { return elem == 4 ? 2 : 1; }
+
+// Staging area of the forward / dX kernels: R rows of x ([R][8K+1]) or of outputs / dZ
+// ([R][8][DT]), whichever is larger; the per-warp coefficient caches follow it.
+template <class T, int K, int DT>
+__host__ __device__ constexpr int sc_stage_elems() {
+  return 32 * sc_npl(sizeof(T)) *
+         (kScWarps * K + 1 > kScWarps * DT ? kScWarps * K + 1 : kScWarps * DT);
+}
+
+// Layout: tile prefix (num_elements + 1 int64, padded to 16 bytes) | staging | caches.
+__host__ __device__ constexpr size_t sc_prefix_bytes(int num_elements) {
+  return (static_cast<size_t>(num_elements + 1) * 8 + 15) / 16 * 16;
+}
+
+template <class T, int K, int DT>
+__host__ __device__ constexpr size_t sc_smem_bytes(int m, int num_elements) {
+  return sc_prefix_bytes(num_elements) +
+         sizeof(T) * (static_cast<size_t>(sc_stage_elems<T, K, DT>()) +
+                      static_cast<size_t>(kScWarps) * m * DT);
+}
+
+// Compile-time loop: f(std::integral_constant<int, I>) for I in [B, E).  The monomial loops
+// are triangular nests of up to 165 iterations; writing them this way keeps every register
+// array index a constant (an unroll pragma alone is not applied that deep).
+template <int B, int E, class F>
+__device__ __forceinline__ void static_for(F&& f) {
+  if constexpr (B < E) {
+    f(std::integral_constant<int, B>{});
+    static_for<B + 1, E>(f);
   }
 }
 
+// acc[j] += sum_m coef_m phi_m(x[j]) for the NPL nodes of this lane (one element).
+template <class T, int K, int DT, int NPL>
+__device__ __forceinline__ void sc_fwd_pass(const T (&x)[NPL][K], T (&acc)[NPL][DT], const T* cw,
+                                            int degree) {
+  static_for<0, K>([&](auto P) {
+    constexpr int p = decltype(P)::value;
+    T cv[DT];
+    sc_ldcache<T, DT>(cv, cw + p * DT);
+#pragma unroll
+    for (int j = 0; j < NPL; ++j)
+#pragma unroll
+      for (int o = 0; o < DT; ++o) acc[j][o] += cv[o] * x[j][p];
+    if (degree >= 2) {
+      static_for<p, K>([&](auto Q) {
+        constexpr int q = decltype(Q)::value;
+        T xpq[NPL];
+#pragma unroll
+        for (int j = 0; j < NPL; ++j) xpq[j] = x[j][p] * x[j][q];
+        T cq[DT];
+        sc_ldcache<T, DT>(cq, cw + sc_idx2<K>(p, q) * DT);
+#pragma unroll
+        for (int j = 0; j < NPL; ++j)
+#pragma unroll
+          for (int o = 0; o < DT; ++o) acc[j][o] += cq[o] * xpq[j];
+        if (degree >= 3) {
+          static_for<q, K>([&](auto Rr) {
+            constexpr int r = decltype(Rr)::value;
+            T cr[DT];
+            sc_ldcache<T, DT>(cr, cw + sc_idx3<K>(p, q, r) * DT);
+#pragma unroll
+            for (int j = 0; j < NPL; ++j) {
+              const T xpqr = xpq[j] * x[j][r];
+#pragma unroll
+              for (int o = 0; o < DT; ++o) acc[j][o] += cr[o] * xpqr;
+            }
+          });
+        }
+      });
+    }
+  });
+}
+
+// dx[j] += d/dx sum_o g[j][o] sum_m coef_m,o phi_m(x[j]).
+template <class T, int K, int DT, int NPL>
+__device__ __forceinline__ void sc_dx_pass(const T (&x)[NPL][K], const T (&g)[NPL][DT],
+                                           T (&dx)[NPL][K], const T* cw, int degree) {
+  static_for<0, K>([&](auto P) {
+    constexpr int p = decltype(P)::value;
+    T cv[DT];
+    sc_ldcache<T, DT>(cv, cw + p * DT);
+#pragma unroll
+    for (int j = 0; j < NPL; ++j) {
+      T G = T(0);
+#pragma unroll
+      for (int o = 0; o < DT; ++o) G += cv[o] * g[j][o];
+      dx[j][p] += G;
+    }
+    if (degree >= 2) {
+      static_for<p, K>([&](auto Q) {
+        constexpr int q = decltype(Q)::value;
+        T cq[DT];
+        sc_ldcache<T, DT>(cq, cw + sc_idx2<K>(p, q) * DT);
+#pragma unroll
+        for (int j = 0; j < NPL; ++j) {
+          T G2 = T(0);
+#pragma unroll
+          for (int o = 0; o < DT; ++o) G2 += cq[o] * g[j][o];
+          dx[j][p] += G2 * x[j][q];
+          dx[j][q] += G2 * x[j][p];
+        }
+        if (degree >= 3) {
+          static_for<q, K>([&](auto Rr) {
+            constexpr int r = decltype(Rr)::value;
+            T cr[DT];
+            sc_ldcache<T, DT>(cr, cw + sc_idx3<K>(p, q, r) * DT);
+#pragma unroll
+            for (int j = 0; j < NPL; ++j) {
+              T G3 = T(0);
+#pragma unroll
+              for (int o = 0; o < DT; ++o) G3 += cr[o] * g[j][o];
+              const T G3r = G3 * x[j][r];
+              dx[j][p] += G3r * x[j][q];
+              dx[j][q] += G3r * x[j][p];
+              dx[j][r] += G3 * (x[j][p] * x[j][q]);
+            }
+          });
+        }
+      });
+    }
+  });
+}
+
+// Tiles never span two elements: element e's sorted range [eoff[e], eoff[e+1]) is cut into
+// ceil(count / R) tiles of its own.  Every CTA builds the per-element tile prefix in shared
+// memory and maps a tile index to (element, first position, rows) by binary search.
+__device__ __forceinline__ void sc_tile_prefix(const int64_t* eoff, int num_elements, int R,
+                                               long long* tp) {
+  if (threadIdx.x == 0) {
+    long long t = 0;
+    tp[0] = 0;
+    for (int e = 0; e < num_elements; ++e) {
+      t += (eoff[e + 1] - eoff[e] + R - 1) / R;
+      tp[e + 1] = t;
+    }
+  }
+  __syncthreads();
+}
+
+__device__ __forceinline__ int sc_tile_element(const long long* tp, int num_elements, long long t) {
+  int lo = 0, hi = num_elements;  // tp[lo] <= t < tp[hi]
+  while (hi - lo > 1) {
+    const int mid = (lo + hi) >> 1;
+    if (tp[mid] <= t) lo = mid; else hi = mid;
+  }
+  return lo;
+}
+
+// Forward.  Lane l of warp w handles rows l + 32 j (j < NPL) of a tile, channel c0 + w,
+// with the warp's coefficients of (element, channel) cached in shared memory.
 template <class T, int K, int DT>
 __global__ void __launch_bounds__(kScWarps * 32, 2) sc_fwd_kernel(const ArgsSc<T> a) {
-  constexpr int ROW = kScWarps * K;
-  __shared__ T xs[32 * (ROW + 1)];
-  __shared__ T os[32 * kScWarps * DT];
+  constexpr int NPL = sc_npl(sizeof(T)), R = 32 * NPL, ROW = kScWarps * K;
+  extern __shared__ __align__(16) unsigned char sc_smem[];
+  long long* tp = reinterpret_cast<long long*>(sc_smem);
+  T* xs = reinterpret_cast<T*>(sc_smem + sc_prefix_bytes(a.num_elements));
+  T* cache = xs + sc_stage_elems<T, K, DT>();
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  T* cw = cache + static_cast<size_t>(wid) * a.m * DT;
   const int c0 = blockIdx.y * kScWarps, c = c0 + wid;
-  const long long ntiles = (a.nodes + 31) / 32;
+  const int nc = min(kScWarps, a.channels - c0);
+  sc_tile_prefix(a.eoff, a.num_elements, R, tp);
+  const long long ntiles = tp[a.num_elements];
+  int cached = -1;
   for (long long tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
-    const long long pos0 = tile * 32, pos = pos0 + lane;
+    const int e = sc_tile_element(tp, a.num_elements, tile);
+    const long long pos0 = a.eoff[e] + (tile - tp[e]) * R;
+    const int nrows = static_cast<int>(min(static_cast<long long>(R), a.eoff[e + 1] - pos0));
     __syncthreads();
-    sc_stage_x<T, K>(a, xs, pos0, c0);
-    __syncthreads();
-    const bool live = pos < a.nodes && c < a.channels;
-    const int my_e = live ? static_cast<int>(a.elem[pos]) : -1;
-    T x[K];
-#pragma unroll
-    for (int i = 0; i < K; ++i) x[i] = xs[lane * (ROW + 1) + wid * K + i];
-    T acc[DT];
-#pragma unroll
-    for (int o = 0; o < DT; ++o) acc[o] = T(0);
-    // Loop over the distinct elements of this tile (one, except at element boundaries).
-    unsigned pending = __ballot_sync(0xffffffffu, live);
-    while (pending) {
-      const int e = __shfl_sync(0xffffffffu, my_e, __ffs(pending) - 1);
-      const bool mine = live && my_e == e;
-      pending &= ~__ballot_sync(0xffffffffu, mine);
-      const T* cf = a.coef + (static_cast<size_t>(e) * a.channels + c) * a.m * DT;
-      if (mine) {
-#pragma unroll
-        for (int p = 0; p < K; ++p) {
-          T cv[DT];
-          sc_ldcoef<T, DT>(cv, cf + p * DT);
-#pragma unroll
-          for (int o = 0; o < DT; ++o) acc[o] += cv[o] * x[p];
-          if (a.degree >= 2) {
-#pragma unroll
-            for (int q = p; q < K; ++q) {
-              const T xpq = x[p] * x[q];
-              sc_ldcoef<T, DT>(cv, cf + sc_idx2<K>(p, q) * DT);
-#pragma unroll
-              for (int o = 0; o < DT; ++o) acc[o] += cv[o] * xpq;
-              if (a.degree >= 3) {
-#pragma unroll
-                for (int r = q; r < K; ++r) {
-                  const T xpqr = xpq * x[r];
-                  sc_ldcoef<T, DT>(cv, cf + sc_idx3<K>(p, q, r) * DT);
-#pragma unroll
-                  for (int o = 0; o < DT; ++o) acc[o] += cv[o] * xpqr;
-                }
-              }
-            }
-          }
-        }
-      }
+    sc_stage_x<T, K, R>(a, xs, pos0, nrows, c0);
+    if (e != cached && c < a.channels) {
+      sc_load_coef<T, DT>(a, cw, e, c, lane);
+      cached = e;
     }
-    // Stage [node][channel][o] and write each node's output columns.
-#pragma unroll
-    for (int o = 0; o < DT; ++o) os[(lane * kScWarps + wid) * DT + o] = acc[o];
     __syncthreads();
-    const int nc = min(kScWarps, a.channels - c0);
-    for (int e = threadIdx.x; e < 32 * kScWarps * a.nout; e += blockDim.x) {
-      const int r = e / (kScWarps * a.nout), q = e - r * kScWarps * a.nout;
+    T x[NPL][K], acc[NPL][DT];
+#pragma unroll
+    for (int j = 0; j < NPL; ++j) {
+#pragma unroll
+      for (int i = 0; i < K; ++i) x[j][i] = xs[(lane + 32 * j) * (ROW + 1) + wid * K + i];
+#pragma unroll
+      for (int o = 0; o < DT; ++o) acc[j][o] = T(0);
+    }
+    if (c < a.channels) sc_fwd_pass<T, K, DT, NPL>(x, acc, cw, a.degree);
+    // Stage [row][channel][o] (reusing xs) and write each node's output columns.
+    __syncthreads();
+#pragma unroll
+    for (int j = 0; j < NPL; ++j)
+#pragma unroll
+      for (int o = 0; o < DT; ++o) xs[((lane + 32 * j) * kScWarps + wid) * DT + o] = acc[j][o];
+    __syncthreads();
+    for (int t = threadIdx.x; t < nrows * kScWarps * a.nout; t += blockDim.x) {
+      const int r = t / (kScWarps * a.nout), q = t - r * kScWarps * a.nout;
       const int o = q / kScWarps, cc = q - o * kScWarps;  // consecutive threads: channels
-      const long long p = pos0 + r;
-      if (p < a.nodes && cc < nc)
-        a.out[a.perm[p] * a.out_dim + a.map.col[o] + (c0 + cc) * a.map.step[o]] =
-            os[(r * kScWarps + cc) * DT + o];
+      if (cc < nc)
+        a.out[a.perm[pos0 + r] * a.out_dim + a.map.col[o] + (c0 + cc) * a.map.step[o]] =
+            xs[(r * kScWarps + cc) * DT + o];
     }
   }
 }
 
+// dX, same mapping as the forward.
 template <class T, int K, int DT>
 __global__ void __launch_bounds__(kScWarps * 32, 2) sc_bwd_dx_kernel(const ArgsSc<T> a) {
-  constexpr int ROW = kScWarps * K;
-  __shared__ T xs[32 * (ROW + 1)];
-  __shared__ T gs[32 * kScWarps * DT];
+  constexpr int NPL = sc_npl(sizeof(T)), R = 32 * NPL, ROW = kScWarps * K;
+  extern __shared__ __align__(16) unsigned char sc_smem[];
+  long long* tp = reinterpret_cast<long long*>(sc_smem);
+  T* xs = reinterpret_cast<T*>(sc_smem + sc_prefix_bytes(a.num_elements));
+  T* cache = xs + sc_stage_elems<T, K, DT>();
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  T* cw = cache + static_cast<size_t>(wid) * a.m * DT;
   const int c0 = blockIdx.y * kScWarps, c = c0 + wid;
-  const long long ntiles = (a.nodes + 31) / 32;
   const int nc = min(kScWarps, a.channels - c0);
+  sc_tile_prefix(a.eoff, a.num_elements, R, tp);
+  const long long ntiles = tp[a.num_elements];
+  int cached = -1;
   for (long long tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
-    const long long pos0 = tile * 32, pos = pos0 + lane;
+    const int e = sc_tile_element(tp, a.num_elements, tile);
+    const long long pos0 = a.eoff[e] + (tile - tp[e]) * R;
+    const int nrows = static_cast<int>(min(static_cast<long long>(R), a.eoff[e + 1] - pos0));
+    T x[NPL][K], g[NPL][DT], dx[NPL][K];
     __syncthreads();
-    sc_stage_x<T, K>(a, xs, pos0, c0);
-    for (int e = threadIdx.x; e < 32 * kScWarps * DT; e += blockDim.x) {
-      const int r = e / (kScWarps * DT), q = e - r * kScWarps * DT;
-      const int o = q / kScWarps, cc = q - o * kScWarps;
-      const long long p = pos0 + r;
-      T v = T(0);
-      if (p < a.nodes && cc < nc && o < a.nout)
-        v = a.gout[a.perm[p] * a.out_dim + a.map.col[o] + (c0 + cc) * a.map.step[o]];
-      gs[(r * kScWarps + cc) * DT + o] = v;
+    sc_stage_x<T, K, R>(a, xs, pos0, nrows, c0);
+    if (e != cached && c < a.channels) {
+      sc_load_coef<T, DT>(a, cw, e, c, lane);
+      cached = e;
     }
     __syncthreads();
-    const bool live = pos < a.nodes && c < a.channels;
-    const int my_e = live ? static_cast<int>(a.elem[pos]) : -1;
-    T x[K], dx[K], g[DT];
 #pragma unroll
-    for (int i = 0; i < K; ++i) {
-      x[i] = xs[lane * (ROW + 1) + wid * K + i];
-      dx[i] = T(0);
-    }
+    for (int j = 0; j < NPL; ++j)
 #pragma unroll
-    for (int o = 0; o < DT; ++o) g[o] = gs[(lane * kScWarps + wid) * DT + o];
-    unsigned pending = __ballot_sync(0xffffffffu, live);
-    while (pending) {
-      const int e = __shfl_sync(0xffffffffu, my_e, __ffs(pending) - 1);
-      const bool mine = live && my_e == e;
-      pending &= ~__ballot_sync(0xffffffffu, mine);
-      const T* cf = a.coef + (static_cast<size_t>(e) * a.channels + c) * a.m * DT;
-      if (mine) {
-#pragma unroll
-        for (int p = 0; p < K; ++p) {
-          T cv[DT];
-          sc_ldcoef<T, DT>(cv, cf + p * DT);
-          T G = T(0);
-#pragma unroll
-          for (int o = 0; o < DT; ++o) G += cv[o] * g[o];
-          dx[p] += G;
-          if (a.degree >= 2) {
-#pragma unroll
-            for (int q = p; q < K; ++q) {
-              sc_ldcoef<T, DT>(cv, cf + sc_idx2<K>(p, q) * DT);
-              T G2 = T(0);
-#pragma unroll
-              for (int o = 0; o < DT; ++o) G2 += cv[o] * g[o];
-              dx[p] += G2 * x[q];
-              dx[q] += G2 * x[p];
-              if (a.degree >= 3) {
-                const T xpq = x[p] * x[q];
-#pragma unroll
-                for (int r = q; r < K; ++r) {
-                  sc_ldcoef<T, DT>(cv, cf + sc_idx3<K>(p, q, r) * DT);
-                  T G3 = T(0);
-#pragma unroll
-                  for (int o = 0; o < DT; ++o) G3 += cv[o] * g[o];
-                  const T G3r = G3 * x[r];
-                  dx[p] += G3r * x[q];
-                  dx[q] += G3r * x[p];
-                  dx[r] += G3 * xpq;
-                }
-              }
-            }
-          }
-        }
+      for (int i = 0; i < K; ++i) {
+        x[j][i] = xs[(lane + 32 * j) * (ROW + 1) + wid * K + i];
+        dx[j][i] = T(0);
       }
+    // Stage dZ of the tile as [row][channel][o] in xs.
+    __syncthreads();
+    for (int t = threadIdx.x; t < R * kScWarps * DT; t += blockDim.x) {
+      const int r = t / (kScWarps * DT), q = t - r * kScWarps * DT;
+      const int o = q / kScWarps, cc = q - o * kScWarps;
+      T v = T(0);
+      if (r < nrows && cc < nc && o < a.nout)
+        v = a.gout[a.perm[pos0 + r] * a.out_dim + a.map.col[o] + (c0 + cc) * a.map.step[o]];
+      xs[(r * kScWarps + cc) * DT + o] = v;
     }
+    __syncthreads();
+#pragma unroll
+    for (int j = 0; j < NPL; ++j)
+#pragma unroll
+      for (int o = 0; o < DT; ++o) g[j][o] = xs[((lane + 32 * j) * kScWarps + wid) * DT + o];
+    if (c < a.channels) sc_dx_pass<T, K, DT, NPL>(x, g, dx, cw, a.degree);
     // Stage dX like x and write it row-contiguously.
     __syncthreads();
 #pragma unroll
-    for (int i = 0; i < K; ++i) xs[lane * (ROW + 1) + wid * K + i] = dx[i];
+    for (int j = 0; j < NPL; ++j)
+#pragma unroll
+      for (int i = 0; i < K; ++i) xs[(lane + 32 * j) * (ROW + 1) + wid * K + i] = dx[j][i];
     __syncthreads();
-    for (int e = threadIdx.x; e < 32 * ROW; e += blockDim.x) {
-      const int r = e / ROW, q = e - r * ROW;
-      const long long p = pos0 + r;
-      if (p < a.nodes && q < nc * K) a.out[(a.perm[p] * a.channels + c0) * K + q] = xs[r * (ROW + 1) + q];
+    for (int t = threadIdx.x; t < nrows * ROW; t += blockDim.x) {
+      const int r = t / ROW, q = t - r * ROW;
+      if (q < nc * K) a.out[(a.perm[pos0 + r] * a.channels + c0) * K + q] = xs[r * (ROW + 1) + q];
     }
   }
 }

@@ -307,7 +307,7 @@ Tensor group_gemm(Tensor A, Tensor B, Tensor ragged_counts, int64_t num_W, int64
 std::vector<int> int_list(at::IntArrayRef v) { return std::vector<int>(v.begin(), v.end()); }
 
 // Fused symmetric contraction (this package's op; no reference schema).
-Tensor sc_forward(Tensor x, Tensor perm, Tensor elem_sorted, Tensor coef, at::IntArrayRef out_col,
+Tensor sc_forward(Tensor x, Tensor perm, Tensor elem_offsets, Tensor coef, at::IntArrayRef out_col,
                   at::IntArrayRef out_step, int64_t out_dim, int64_t degree) {
   TORCH_CHECK(x.is_cuda() && x.dim() == 3, "sc_forward: x must be a [N, C, K] GPU tensor");
   TORCH_CHECK(coef.dim() == 4 && coef.scalar_type() == x.scalar_type(), "sc_forward: coef must be [E, C, M, DT] of x's dtype");
@@ -319,14 +319,14 @@ Tensor sc_forward(Tensor x, Tensor perm, Tensor elem_sorted, Tensor coef, at::In
   check_rc(oeqb_sc_forward(dtype_code(x), x.size(0), static_cast<int>(x.size(1)),
                            static_cast<int>(x.size(2)), static_cast<int>(degree),
                            static_cast<int>(coef.size(3)), static_cast<int>(col.size()), col.data(),
-                           step.data(), out_dim, xc.data_ptr(), perm.data_ptr<int64_t>(),
-                           elem_sorted.data_ptr<int64_t>(), cc.data_ptr(), out.data_ptr(),
-                           stream_of(x)));
+                           step.data(), out_dim, static_cast<int>(coef.size(0)), xc.data_ptr(),
+                           perm.data_ptr<int64_t>(), elem_offsets.data_ptr<int64_t>(),
+                           cc.data_ptr(), out.data_ptr(), stream_of(x)));
   return out;
 }
 
-std::tuple<Tensor, Tensor> sc_backward(Tensor x, Tensor perm, Tensor elem_sorted,
-                                       Tensor elem_offsets, Tensor coef, Tensor grad_out,
+std::tuple<Tensor, Tensor> sc_backward(Tensor x, Tensor perm, Tensor elem_offsets,
+                                       Tensor coef, Tensor grad_out,
                                        at::IntArrayRef out_col, at::IntArrayRef out_step,
                                        int64_t degree) {
   TORCH_CHECK(x.is_cuda() && x.dim() == 3, "sc_backward: x must be a [N, C, K] GPU tensor");
@@ -339,7 +339,7 @@ std::tuple<Tensor, Tensor> sc_backward(Tensor x, Tensor perm, Tensor elem_sorted
                             static_cast<int>(x.size(2)), static_cast<int>(degree),
                             static_cast<int>(coef.size(3)), static_cast<int>(col.size()),
                             col.data(), step.data(), gc.size(1), static_cast<int>(coef.size(0)),
-                            xc.data_ptr(), perm.data_ptr<int64_t>(), elem_sorted.data_ptr<int64_t>(),
+                            xc.data_ptr(), perm.data_ptr<int64_t>(),
                             elem_offsets.data_ptr<int64_t>(), cc.data_ptr(), gc.data_ptr(),
                             gx.data_ptr(), gcoef.data_ptr(), stream_of(x)));
   return {gx, gcoef};
@@ -348,8 +348,8 @@ std::tuple<Tensor, Tensor> sc_backward(Tensor x, Tensor perm, Tensor elem_sorted
 }  // namespace
 
 TORCH_LIBRARY(oeqb200, m) {
-  m.def("sc_forward(Tensor x, Tensor perm, Tensor elem_sorted, Tensor coef, int[] out_col, int[] out_step, int out_dim, int degree) -> Tensor");
-  m.def("sc_backward(Tensor x, Tensor perm, Tensor elem_sorted, Tensor elem_offsets, Tensor coef, Tensor grad_out, int[] out_col, int[] out_step, int degree) -> (Tensor, Tensor)");
+  m.def("sc_forward(Tensor x, Tensor perm, Tensor elem_offsets, Tensor coef, int[] out_col, int[] out_step, int out_dim, int degree) -> Tensor");
+  m.def("sc_backward(Tensor x, Tensor perm, Tensor elem_offsets, Tensor coef, Tensor grad_out, int[] out_col, int[] out_step, int degree) -> (Tensor, Tensor)");
 }
 
 TORCH_LIBRARY_IMPL(oeqb200, CUDA, m) {

@@ -175,10 +175,9 @@ class SymmetricContraction(torch.nn.Module):
             if self.dt > self.nout:
                 coef = torch.nn.functional.pad(coef, (0, self.dt - self.nout))
             perm = torch.argsort(elem, stable=True)
-            elem_sorted = elem[perm]
             counts = torch.bincount(elem, minlength=self.num_elements)
             eoff = torch.cat([counts.new_zeros(1), torch.cumsum(counts, 0)])
-            return _FusedSC.apply(x, coef.contiguous(), perm, elem_sorted, eoff, self)
+            return _FusedSC.apply(x, coef.contiguous(), perm, eoff, elem, self)
         return _torch_contraction(self, x, coef, elem)
 
 
@@ -210,24 +209,22 @@ def _torch_contraction(sc: SymmetricContraction, x, coef, elem) -> torch.Tensor:
 
 class _FusedSC(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, x, coef, perm, elem_sorted, eoff, sc):
+    def forward(ctx, x, coef, perm, eoff, elem, sc):
         ctx.sc = sc
-        ctx.save_for_backward(x, coef, perm, elem_sorted, eoff)
-        return torch.ops.oeqb200.sc_forward(x, perm, elem_sorted, coef, sc._out_col, sc._out_step,
+        ctx.save_for_backward(x, coef, perm, eoff, elem)
+        return torch.ops.oeqb200.sc_forward(x, perm, eoff, coef, sc._out_col, sc._out_step,
                                             sc.out_dim, sc.degree)
 
     @staticmethod
     def backward(ctx, gout):
-        x, coef, perm, elem_sorted, eoff = ctx.saved_tensors
+        x, coef, perm, eoff, elem = ctx.saved_tensors
         sc = ctx.sc
         if torch.is_grad_enabled():
             # The backward is being recorded (double backward): differentiate the torch form.
-            elem = torch.empty_like(elem_sorted)
-            elem[perm] = elem_sorted
             out = _torch_contraction(sc, x, coef, elem)
             gx, gc = torch.autograd.grad(out, (x, coef), gout, create_graph=True, allow_unused=True)
             return gx, gc, None, None, None, None
-        gx, gc = torch.ops.oeqb200.sc_backward(x, perm, elem_sorted, eoff, coef, gout.contiguous(),
+        gx, gc = torch.ops.oeqb200.sc_backward(x, perm, eoff, coef, gout.contiguous(),
                                                sc._out_col, sc._out_step, sc.degree)
         return gx, gc, None, None, None, None
 
