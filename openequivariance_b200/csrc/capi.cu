@@ -20,6 +20,7 @@
 
 #include "oeqb200.h"
 #include "tp_core.cuh"
+#include "tp_kernels_edge.cuh"
 #include "tp_kernels_lk.cuh"
 
 namespace oeqb {
@@ -33,14 +34,13 @@ template <class T>
 const void* seg_kernel_ptr(int kind);
 template <class T>
 const void* lk_kernel_ptr();
+template <class T>
+const void* edge_kernel_ptr(int kind);
 int set_error(int code, const std::string& msg);
 }  // namespace oeqb
 
 using namespace oeqb;
 
-// Launch policies of the batch/atomic kernel table (tp_kernels.cuh: enum Policy).
-constexpr int kBatch = 0;
-constexpr int kConvAtomic = 1;
 
 namespace {
 
@@ -117,6 +117,9 @@ struct oeqb_plan {
     int nch = 0, rb = 0, nslots = 0, offY = 0, xy_elems = 0, slot_elems = 0, slot_w_off = 0;
     size_t smem = 0;
   } lk;
+  // Edge-per-lane convolution (tp_kernels_edge.cuh) for multiplicity-1 problems.
+  bool edge_ok = false;
+  EdgeLayout edge{};
 
   DevArrays off{};
   unsigned char* dmem = nullptr;
@@ -477,6 +480,18 @@ void build_lk(oeqb_plan& p) {
   c.ok = c.nslots >= 3;
 }
 
+// Convolutions whose instructions all have multiplicity 1 run one edge per lane.
+void build_edge(oeqb_plan& p) {
+  p.edge_ok = false;
+  if (p.ins_f.empty()) return;
+  for (const InstrD& in : p.ins_f)
+    if (in.code < 0 || in.m1 != 1 || in.m2 != 1 || in.m3 != 1) return;
+  p.edge = EdgeLayout{edge_pad(p.L1dim), edge_pad(p.L2dim), edge_pad(p.L3dim),
+                      edge_pad(std::max(1, p.wnumel))};
+  const size_t elem = p.dtype == 2 ? 8 : 4;
+  p.edge_ok = edge_warp_elems(p.edge, true) * elem <= 12 * 1024;
+}
+
 int parse_descriptor(const void* data, size_t n, oeqb_plan& p) {
   const unsigned char* b = static_cast<const unsigned char*>(data);
   if (n < 16 * 8) return fail(OEQB_ERR_INVALID, "descriptor too short");
@@ -616,6 +631,7 @@ int parse_descriptor(const void* data, size_t n, oeqb_plan& p) {
   build_row(p);
   build_seg(p);
   build_lk(p);
+  build_edge(p);
   return 0;
 }
 
@@ -913,6 +929,36 @@ bool lk_aligned(const oeqb_plan& p, const Args<T>& a) {
   return ok;
 }
 
+template <class T>
+int launch_edge(oeqb_plan& p, int kind, const Args<T>& a, cudaStream_t stream) {
+  if (a.nitems <= 0) return 0;
+  const void* kernel = edge_kernel_ptr<T>(kind);
+  const size_t smem = align16(sizeof(InstrD) * p.nins) +
+                      sizeof(T) * size_t(kEdgeWarps) * edge_warp_elems(p.edge, kind == 1);
+  int per_sm;
+  {
+    std::lock_guard<std::mutex> g(p.mu);
+    auto it = p.occ.find(kernel);
+    if (it == p.occ.end()) {
+      if (int rc = allow_max_smem(p.device, kernel)) return rc;
+      int n = 0;
+      OEQB_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kernel, kEdgeWarps * 32, smem));
+      if (n <= 0) return fail(OEQB_ERR_UNSUPPORTED, "edge convolution kernel does not fit");
+      it = p.occ.emplace(kernel, n).first;
+    }
+    per_sm = it->second;
+  }
+  const long long warps = (a.nitems + 31) / 32;
+  long long blocks = std::min<long long>((warps + kEdgeWarps - 1) / kEdgeWarps,
+                                         (long long)p.sm_count * per_sm);
+  blocks = std::max<long long>(1, blocks);
+  EdgeLayout L = p.edge;
+  void* params[] = {const_cast<Args<T>*>(&a), &L};
+  OEQB_CUDA(cudaLaunchKernel(kernel, dim3(static_cast<unsigned>(blocks)), dim3(kEdgeWarps * 32),
+                             params, smem, stream));
+  return 0;
+}
+
 struct DeviceGuard {
   int prev = -1;
   explicit DeviceGuard(int dev) {
@@ -1013,6 +1059,7 @@ int conv_fwd_t(oeqb_plan* p, bool db, const void* X, const void* Y, const void* 
   a.cols = reinterpret_cast<const long long*>(cols);
   if (p->det)
     return launch(*p, det_kernel_ptr<T>(0, p->uvw, db, p->kahan), a, true, true, s);
+  if (!db && p->edge_ok) return launch_edge(*p, 0, a, s);
   return launch(*p, batch_kernel_ptr<T>(0, p->uvw, db, kConvAtomic), a, true, false, s);
 }
 
@@ -1044,6 +1091,7 @@ int conv_bwd_t(oeqb_plan* p, bool db, const void* X, const void* Y, const void* 
     if (!perm) return fail(OEQB_ERR_INVALID, "deterministic convolution needs transpose_perm");
     return launch(*p, det_kernel_ptr<T>(1, p->uvw, db, p->kahan), a, false, true, s);
   }
+  if (!db && p->edge_ok) return launch_edge(*p, 1, a, s);
   return launch(*p, batch_kernel_ptr<T>(1, p->uvw, db, kConvAtomic), a, false, false, s);
 }
 

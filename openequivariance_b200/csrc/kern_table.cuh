@@ -3,6 +3,7 @@
 // here and launches them with cudaLaunchKernel.
 #pragma once
 #include "tp_kernels.cuh"
+#include "tp_kernels_edge.cuh"
 #include "tp_kernels_lk.cuh"
 
 namespace oeqb {
@@ -23,6 +24,9 @@ template <class T>
 const void* seg_kernel_ptr(int kind);
 template <class T>
 const void* lk_kernel_ptr();
+// Edge-per-lane convolution for multiplicity-1 problems (tp_kernels_edge.cuh).
+template <class T>
+const void* edge_kernel_ptr(int kind);
 
 #define OEQB_PICK4(K, T, P)                                                     \
   (uvw ? (db ? (const void*)K<T, true, true, P> : (const void*)K<T, true, false, P>) \
@@ -51,7 +55,11 @@ const void* lk_kernel_ptr();
     return kind == 0 ? (const void*)tp_fwd_seg<T> : (const void*)tp_bwd_seg<T, 16>; \
   }                                                                               \
   template <>                                                                     \
-  const void* lk_kernel_ptr<T>() { return (const void*)tp_bwd_lk<T>; }
+  const void* lk_kernel_ptr<T>() { return (const void*)tp_bwd_lk<T>; }            \
+  template <>                                                                     \
+  const void* edge_kernel_ptr<T>(int kind) {                                      \
+    return kind == 0 ? (const void*)conv_fwd_edge<T> : (const void*)conv_bwd_edge<T>; \
+  }
 
 #define OEQB_DEFINE_DET_TABLE(T, WITH_KAHAN)                                    \
   template <>                                                                   \

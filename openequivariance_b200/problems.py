@@ -76,6 +76,21 @@ def real_spherical_harmonics(vec: np.ndarray, lmax: int) -> np.ndarray:
     """
     from .cg import real_wigner_3j
 
+    if not isinstance(vec, np.ndarray):  # torch tensor: same recursion on its device
+        import torch
+
+        v = vec / torch.linalg.norm(vec, dim=-1, keepdim=True)
+        y1 = np.sqrt(3.0) * v[..., [1, 2, 0]]
+        out = [torch.ones_like(v[..., :1])] + ([y1] if lmax >= 1 else [])
+        prev = y1
+        for l in range(2, lmax + 1):
+            c = torch.tensor(real_wigner_3j(l - 1, 1, l), dtype=v.dtype, device=v.device)
+            nxt = torch.einsum("...i,...j,ijk->...k", prev, y1, c)
+            nxt = nxt * (np.sqrt(2 * l + 1) / torch.linalg.norm(nxt, dim=-1, keepdim=True))
+            out.append(nxt)
+            prev = nxt
+        return torch.cat(out, dim=-1)
+
     v = vec / np.linalg.norm(vec, axis=-1, keepdims=True)
     out = [np.ones(v.shape[:-1] + (1,))]
     y1 = np.sqrt(3.0) * v[..., [1, 2, 0]]
