@@ -212,14 +212,15 @@ def _max_over_ranks(x, world):
 
 
 def _sh_inputs(rows, lmax, seed, dtype, device):
-    import numpy as np
+    """Real spherical harmonics of random unit vectors, computed on the device (as a model
+    computes them from edge vectors), so Y is allocated like every other device input."""
     import torch
 
     from openequivariance_b200.problems import real_spherical_harmonics
 
-    rng = np.random.default_rng(seed)
-    vec = rng.normal(size=(rows, 3))
-    return torch.tensor(real_spherical_harmonics(vec, lmax), dtype=dtype, device=device)
+    gen = torch.Generator(device=device).manual_seed(seed)
+    vec = torch.randn(rows, 3, device=device, dtype=torch.float64, generator=gen)
+    return real_spherical_harmonics(vec, lmax).to(dtype).contiguous()
 
 
 # ------------------------------------------------------------------------------ TP workload

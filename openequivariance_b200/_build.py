@@ -31,7 +31,8 @@ TORCH_LIB = PKG / "libtorch_oeqb200.so"
 ARCH = "-gencode=arch=compute_100a,code=sm_100a"
 LMAX_UNROLLED = int(os.environ.get("OEQB_LMAX_UNROLLED", "3"))
 CU_SOURCES = ["capi.cu", "kern_f32_batch.cu", "kern_f64_batch.cu", "kern_f32_det.cu",
-              "kern_f64_det.cu", "kern_sc.cu"]
+              "kern_f64_det.cu", "kern_sc.cu",
+              "kern_uvw_tc.cu"]
 
 
 def _nvcc() -> str:

@@ -14,6 +14,7 @@
 #include <cstring>
 #include <mutex>
 #include <set>
+#include <type_traits>
 #include <string>
 #include <unordered_map>
 #include <vector>
@@ -22,6 +23,7 @@
 #include "tp_core.cuh"
 #include "tp_kernels_edge.cuh"
 #include "tp_kernels_lk.cuh"
+#include "tp_kernels_uvw_tc.cuh"
 
 namespace oeqb {
 template <class T>
@@ -36,6 +38,7 @@ template <class T>
 const void* lk_kernel_ptr();
 template <class T>
 const void* edge_kernel_ptr(int kind);
+const void* uvw_tc_kernel_ptr(int kind);
 int set_error(int code, const std::string& msg);
 }  // namespace oeqb
 
@@ -120,6 +123,18 @@ struct oeqb_plan {
   // Edge-per-lane convolution (tp_kernels_edge.cuh) for multiplicity-1 problems.
   bool edge_ok = false;
   EdgeLayout edge{};
+  // Tensor-core shared-weight uvw forward (tp_kernels_uvw_tc.cuh).
+  struct TcTable {
+    bool ok = false;
+    std::vector<TcPass> passes;
+    std::vector<TcStage> stages;
+    std::vector<TcIns> ins;
+    std::vector<TcOut> outs;
+    std::vector<int> woff;
+    std::vector<float> pw;
+    size_t off_passes = 0, off_stages = 0, off_ins = 0, off_outs = 0, off_woff = 0, off_pw = 0;
+    float* wsplit = nullptr;  // plan-owned operand image of the weights (rewritten per call)
+  } tc;
 
   DevArrays off{};
   unsigned char* dmem = nullptr;
@@ -492,6 +507,83 @@ void build_edge(oeqb_plan& p) {
   p.edge_ok = edge_warp_elems(p.edge, true) * elem <= 12 * 1024;
 }
 
+// Shared-weight float32 uvw problems of the NequIP shape run on the tensor cores: every
+// instruction 32 x 1 -> 32 channels, l1, l3 <= 2, every output irrep 32 channels of l <= 2.
+// Schedule: passes over runs of output irreps whose accumulators fit kTcDCols TMEM columns;
+// inside a pass, one stage per input irrep (its X block staged once), instructions in
+// output order; the first instruction into an output irrep overwrites its accumulator.
+void build_uvw_tc(oeqb_plan& p) {
+  auto& t = p.tc;
+  t = oeqb_plan::TcTable{};
+  if (p.dtype != 1 || !p.uvw || p.layout != 0 || !p.shared_w || p.ins_f.empty()) return;
+  if (p.L1dim % 4 || p.L3dim % 4 || p.L2dim > kTcYMax) return;
+  for (const IrrepD& r : p.ir1)
+    if (r.off % 4 || r.l > 2) return;
+  for (const IrrepD& r : p.ir3)
+    if (r.off % 4 || r.l > 2 || r.mul != 32) return;
+  std::vector<InstrD> ins;  // original order (weight blocks by instruction index)
+  ins.resize(p.nins);
+  for (const InstrD& in : p.ins_f) {
+    if (in.code < 0 || in.m1 != 32 || in.m2 != 1 || in.m3 != 32 || in.l1 > 2 || in.l3 > 2)
+      return;
+    if (p.ir2[in.i2].off + 2 * in.l2 + 1 > p.L2dim) return;
+  }
+  // ins_f is a stable sort of the descriptor order by output; recover each instruction's
+  // index from its weight offset (distinct per instruction).
+  std::vector<std::pair<int, int>> by_woff;
+  for (int n = 0; n < static_cast<int>(p.ins_f.size()); ++n)
+    by_woff.push_back({p.ins_f[n].woff, n});
+  std::sort(by_woff.begin(), by_woff.end());
+  std::vector<int> blk(p.ins_f.size());
+  for (size_t r = 0; r < by_woff.size(); ++r) blk[by_woff[r].second] = static_cast<int>(r);
+  t.woff.resize(p.ins_f.size());
+  t.pw.resize(p.ins_f.size());
+  for (size_t n = 0; n < p.ins_f.size(); ++n) {
+    t.woff[blk[n]] = p.ins_f[n].woff;
+    t.pw[blk[n]] = static_cast<float>(p.ins_f[n].pw);
+  }
+  int o = 0;
+  while (o < p.n3) {
+    TcPass ps{};
+    ps.stage_begin = static_cast<int>(t.stages.size());
+    ps.out_begin = static_cast<int>(t.outs.size());
+    int cols = 0, o_end = o;
+    while (o_end < p.n3 && cols + 32 * p.ir3[o_end].dim <= kTcDCols) cols += 32 * p.ir3[o_end++].dim;
+    std::vector<int> dcol(p.n3, -1);
+    cols = 0;
+    for (int r = o; r < o_end; ++r) {
+      dcol[r] = cols;
+      t.outs.push_back(TcOut{p.ir3[r].off, p.ir3[r].dim, cols, 0});
+      cols += 32 * p.ir3[r].dim;
+    }
+    std::vector<char> seen(p.n3, 0);
+    for (int i1 = 0; i1 < p.n1; ++i1) {
+      TcStage st{p.ir1[i1].off, p.ir1[i1].l, static_cast<int>(t.ins.size()), 0};
+      for (size_t n = 0; n < p.ins_f.size(); ++n) {
+        const InstrD& in = p.ins_f[n];
+        if (in.i1 != i1 || in.i3 < o || in.i3 >= o_end) continue;
+        TcIns ti{};
+        ti.l2 = in.l2;
+        ti.l3 = in.l3;
+        ti.y_off = p.ir2[in.i2].off;
+        ti.wblk = blk[n];
+        ti.dcol = dcol[in.i3];
+        ti.first = seen[in.i3] ? 0 : 1;
+        seen[in.i3] = 1;
+        t.outs[ps.out_begin + (in.i3 - o)].has = 1;
+        t.ins.push_back(ti);
+      }
+      st.ins_end = static_cast<int>(t.ins.size());
+      if (st.ins_end > st.ins_begin) t.stages.push_back(st);
+    }
+    ps.stage_end = static_cast<int>(t.stages.size());
+    ps.out_end = static_cast<int>(t.outs.size());
+    t.passes.push_back(ps);
+    o = o_end;
+  }
+  t.ok = true;
+}
+
 int parse_descriptor(const void* data, size_t n, oeqb_plan& p) {
   const unsigned char* b = static_cast<const unsigned char*>(data);
   if (n < 16 * 8) return fail(OEQB_ERR_INVALID, "descriptor too short");
@@ -632,6 +724,7 @@ int parse_descriptor(const void* data, size_t n, oeqb_plan& p) {
   build_seg(p);
   build_lk(p);
   build_edge(p);
+  build_uvw_tc(p);
   return 0;
 }
 
@@ -662,6 +755,12 @@ void layout_tables(oeqb_plan& p, std::vector<unsigned char>& buf) {
     t->off_wofs = put(buf, t->wofs);
   }
   for (auto* t : {&p.segf, &p.segb, &p.segl}) t->dev_off = put(buf, t->blob);
+  p.tc.off_passes = put(buf, p.tc.passes);
+  p.tc.off_stages = put(buf, p.tc.stages);
+  p.tc.off_ins = put(buf, p.tc.ins);
+  p.tc.off_outs = put(buf, p.tc.outs);
+  p.tc.off_woff = put(buf, p.tc.woff);
+  p.tc.off_pw = put(buf, p.tc.pw);
   p.off.total = align16(buf.size());
   buf.resize(p.off.total);
 }
@@ -673,6 +772,8 @@ int upload(oeqb_plan& p) {
   OEQB_CUDA(cudaMemcpy(p.dmem, buf.data(), p.off.total, cudaMemcpyHostToDevice));
   OEQB_CUDA(cudaMalloc(&p.d_status, sizeof(int)));
   OEQB_CUDA(cudaMemset(p.d_status, 0, sizeof(int)));
+  if (p.tc.ok)
+    OEQB_CUDA(cudaMalloc(&p.tc.wsplit, sizeof(float) * kTcWBlock * p.tc.woff.size()));
   return 0;
 }
 
@@ -959,6 +1060,53 @@ int launch_edge(oeqb_plan& p, int kind, const Args<T>& a, cudaStream_t stream) {
   return 0;
 }
 
+// Tensor-core uvw forward: split the weights into the operand image, then the persistent
+// kernel (one CTA per SM, 128-row tiles).  The weight image is plan-owned, so forward calls
+// of one plan on different streams must be ordered by the caller.
+int launch_uvw_tc(oeqb_plan& p, const Args<float>& a, cudaStream_t stream) {
+  if (a.nitems <= 0) return 0;
+  const int nins = static_cast<int>(p.tc.woff.size());
+  ArgsTcPrep pr{a.W, p.tc.wsplit, reinterpret_cast<const int*>(p.dmem + p.tc.off_woff),
+                reinterpret_cast<const float*>(p.dmem + p.tc.off_pw), nins};
+  {
+    void* params[] = {&pr};
+    OEQB_CUDA(cudaLaunchKernel(uvw_tc_kernel_ptr(1), dim3((nins * 1024 + 255) / 256), dim3(256),
+                               params, 0, stream));
+  }
+  const void* kernel = uvw_tc_kernel_ptr(0);
+  {
+    std::lock_guard<std::mutex> g(p.mu);
+    if (p.occ.find(kernel) == p.occ.end()) {
+      if (int rc = allow_max_smem(p.device, kernel)) return rc;
+      int n = 0;
+      OEQB_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kernel, kTcThreads, kTcSmemBytes));
+      if (n <= 0) return fail(OEQB_ERR_UNSUPPORTED, "tensor-core uvw kernel does not fit");
+      p.occ.emplace(kernel, n);
+    }
+  }
+  ArgsTc t{};
+  t.X = a.X;
+  t.Y = a.Y;
+  t.Wsplit = p.tc.wsplit;
+  t.Z = a.out0;
+  t.B = a.nitems;
+  t.L1dim = p.L1dim;
+  t.L2dim = p.L2dim;
+  t.L3dim = p.L3dim;
+  t.npass = static_cast<int>(p.tc.passes.size());
+  t.passes = reinterpret_cast<const TcPass*>(p.dmem + p.tc.off_passes);
+  t.stages = reinterpret_cast<const TcStage*>(p.dmem + p.tc.off_stages);
+  t.ins = reinterpret_cast<const TcIns*>(p.dmem + p.tc.off_ins);
+  t.outs = reinterpret_cast<const TcOut*>(p.dmem + p.tc.off_outs);
+  t.status = p.d_status;
+  const long long tiles = (a.nitems + kTcRows - 1) / kTcRows;
+  const long long blocks = std::min<long long>(tiles, p.sm_count);
+  void* params[] = {&t};
+  OEQB_CUDA(cudaLaunchKernel(kernel, dim3(static_cast<unsigned>(blocks)), dim3(kTcThreads), params,
+                             kTcSmemBytes, stream));
+  return 0;
+}
+
 struct DeviceGuard {
   int prev = -1;
   explicit DeviceGuard(int dev) {
@@ -986,6 +1134,9 @@ int tp_forward_t(oeqb_plan* p, int64_t B, const void* X, const void* Y, const vo
   a.Y = static_cast<const T*>(Y);
   a.W = static_cast<const T*>(W);
   a.out0 = static_cast<T*>(Z);
+  if constexpr (std::is_same_v<T, float>) {
+    if (p->tc.ok && aligned16(X) && aligned16(Z)) return launch_uvw_tc(*p, a, s);
+  }
   if (p->segf.ok) return launch_seg(*p, 0, a, s);
   if (p->row_ok) return launch_row(*p, 0, a, s);
   return launch(*p, batch_kernel_ptr<T>(0, p->uvw, false, kBatch), a, true, false, s);
@@ -1148,6 +1299,7 @@ int oeqb_plan_create(const void* descriptor, size_t nbytes, int device, oeqb_pla
   if (int rc = upload(*p)) {
     if (p->dmem) cudaFree(p->dmem);
     if (p->d_status) cudaFree(p->d_status);
+    if (p->tc.wsplit) cudaFree(p->tc.wsplit);
     delete p;
     return rc;
   }
@@ -1161,6 +1313,7 @@ int oeqb_plan_destroy(oeqb_plan* p) {
     DeviceGuard g(p->device);
     if (p->dmem) cudaFree(p->dmem);
     if (p->d_status) cudaFree(p->d_status);
+    if (p->tc.wsplit) cudaFree(p->tc.wsplit);
   }
   delete p;
   return 0;
