@@ -40,7 +40,7 @@ def _args():
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["c2", "c2ml", "conv", "sc"], default="c2")
+    ap.add_argument("--workload", choices=["c2", "c2ml", "c4", "conv", "sc"], default="c2")
     ap.add_argument("--conv-nodes", type=int, default=200000)
     ap.add_argument("--conv-mode", choices=["atomic", "deterministic"], default="atomic")
     ap.add_argument("--sc-nodes", type=int, default=100000)
@@ -227,8 +227,18 @@ def _sh_inputs(rows, lmax, seed, dtype, device):
 
 
 def _workload_desc(name, problem):
-    return (f"{name}: batch uvu CG tensor product fwd+bwd ({len(problem.instructions)} paths, "
-            f"X={problem.irreps_in1}, Y=SH l<=3, L3_dim={problem.irreps_out.dim})")
+    mode = problem.instructions[0].connection_mode
+    shared = ", shared weights" if problem.shared_weights else ""
+    return (f"{name}: batch {mode} CG tensor product fwd+bwd ({len(problem.instructions)} paths"
+            f"{shared}, X={problem.irreps_in1}, Y=SH l<={problem.irreps_in2.lmax}, "
+            f"L3_dim={problem.irreps_out.dim})")
+
+
+def _dense_flops(problem):
+    """Multiply-add FLOPs per row of the channel-mixing part of uvw paths (2 mul1 mul3 d3 per
+    path), the work the tensor cores do."""
+    return sum(2 * i.path_shape[0] * i.path_shape[2] * (2 * problem.irreps_out[i.i_out].ir.l + 1)
+               for i in problem.instructions if i.connection_mode == "uvw")
 
 
 def bench_tp(args, world, rank, local):
@@ -242,10 +252,16 @@ def bench_tp(args, world, rank, local):
     problem = baseline_problem(args.workload)
     tp = oeq.TensorProduct(problem)
     B = args.rows
+    shared = problem.shared_weights
     gen = torch.Generator(device=dev).manual_seed(1234 + rank)
     X = torch.randn(B, problem.irreps_in1.dim, device=dev, generator=gen)
-    Y = _sh_inputs(B, 3, 99 + rank, torch.float32, dev)
-    W = torch.randn(B, problem.weight_numel, device=dev, generator=gen)
+    Y = _sh_inputs(B, problem.irreps_in2.lmax, 99 + rank, torch.float32, dev)
+    if shared:  # C4: W ~ N(0, 1/sqrt(fan_in)), fan_in = 32 channels x paths into an output
+        fan = max(sum(1 for j in problem.instructions if j.i_out == i.i_out) * i.path_shape[0]
+                  for i in problem.instructions)
+        W = torch.randn(problem.weight_numel, device=dev, generator=gen) / fan ** 0.5
+    else:
+        W = torch.randn(B, problem.weight_numel, device=dev, generator=gen)
     G = torch.randn(B, problem.irreps_out.dim, device=dev, generator=gen)
     ops = torch.ops.libtorch_tp_jit
 
@@ -281,8 +297,9 @@ def bench_tp(args, world, rank, local):
     s = 4
     d1, d2, d3, wn = (problem.irreps_in1.dim, problem.irreps_in2.dim, problem.irreps_out.dim,
                       problem.weight_numel)
-    bytes_fwd = B * (d1 + d2 + d3 + wn) * s
-    bytes_bwd = B * (2 * d1 + 2 * d2 + d3 + 2 * wn) * s
+    wrow = 0 if shared else wn
+    bytes_fwd = B * (d1 + d2 + d3 + wrow) * s + (wn * s if shared else 0)
+    bytes_bwd = B * (2 * d1 + 2 * d2 + d3 + 2 * wrow) * s + (2 * wn * s if shared else 0)
     peak, peak_src = _peaks()
     dom = ("tp_bwd", bytes_bwd, t_bwd) if t_bwd >= t_fwd else ("tp_fwd", bytes_fwd, t_fwd)
     achieved = dom[1] / (dom[2] * 1e-3) / 1e9
@@ -294,7 +311,7 @@ def bench_tp(args, world, rank, local):
     E = max(1, args.e2e_steps)
     hX, hY, hW, hG = (t.cpu().pin_memory() for t in (X, Y, W, G))
     outs_h = [torch.empty(B, d3).pin_memory(), torch.empty(B, d1).pin_memory(),
-              torch.empty(B, d2).pin_memory(), torch.empty(B, wn).pin_memory()]
+              torch.empty(B, d2).pin_memory(), torch.empty_like(hW).pin_memory()]
 
     def e2e_step():
         x = hX.to(dev, non_blocking=True).requires_grad_()
@@ -342,6 +359,22 @@ def bench_tp(args, world, rank, local):
         "gpu_launches": 2 * K,
         "clocks": clk.summary(),
     }
+    fl = _dense_flops(problem) * B
+    if fl:
+        # Channel mixing of uvw paths on the tensor pipe (forward): algorithmic FLOPs and the
+        # FLOPs issued by the 3xTF32 split, against TF32 = half the measured dense bf16 rate.
+        try:
+            with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+                tf32 = float(json.load(f)["bf16_tflops"]) / 2
+            src = "measured bf16 / 2"
+        except Exception:
+            tf32, src = 1590.0 / 2, "fallback bf16 / 2"
+        tflops = fl / (t_fwd * 1e-3) / 1e12
+        line["tensor_roofline"] = {
+            "kernel": "tp_fwd", "bound": "tensor", "unit": "TFLOP/s",
+            "achieved_algorithmic": tflops, "achieved_issued_3xtf32": 3 * tflops,
+            "peak_tf32": tf32, "peak_source": src, "frac_issued": 3 * tflops / tf32,
+            "flops_per_launch": fl}
     if cpu is not None:
         line["cpu_baseline"] = cpu
     return line

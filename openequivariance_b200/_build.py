@@ -32,7 +32,7 @@ ARCH = "-gencode=arch=compute_100a,code=sm_100a"
 LMAX_UNROLLED = int(os.environ.get("OEQB_LMAX_UNROLLED", "3"))
 CU_SOURCES = ["capi.cu", "kern_f32_batch.cu", "kern_f64_batch.cu", "kern_f32_det.cu",
               "kern_f64_det.cu", "kern_sc.cu",
-              "kern_uvw_tc.cu"]
+              "kern_uvw_tc.cu", "kern_uvw_sw.cu"]
 
 
 def _nvcc() -> str:
@@ -62,8 +62,26 @@ def _run(cmd, log: Path):
         raise RuntimeError(f"command failed: {' '.join(cmd)}\n{tail}")
 
 
-def _headers():
-    return sorted(CSRC.glob("*.cuh")) + [INCLUDE / "oeqb200.h"]
+def _includes(path: Path, seen: set) -> None:
+    """Adds the repository headers `path` includes (transitively) to `seen`."""
+    for line in path.read_text().splitlines():
+        line = line.strip()
+        if not line.startswith("#include \""):
+            continue
+        name = line.split('"')[1]
+        for base in (CSRC, INCLUDE):
+            dep = base / name
+            if dep.exists() and dep not in seen:
+                seen.add(dep)
+                _includes(dep, seen)
+                break
+
+
+def _deps(src: str):
+    """The source and every repository header it includes, in a stable order."""
+    seen: set = set()
+    _includes(CSRC / src, seen)
+    return [CSRC / src] + sorted(seen)
 
 
 def build_native(jobs: int | None = None, verbose: bool = False) -> Path:
@@ -73,11 +91,10 @@ def build_native(jobs: int | None = None, verbose: bool = False) -> Path:
     flags = _nvcc_flags()
     stamp_file = BUILD / "stamps.json"
     stamps = json.loads(stamp_file.read_text()) if stamp_file.exists() else {}
-    headers = _headers()
     work = []
     for src in CU_SOURCES:
         obj = BUILD / (src + ".o")
-        dig = _digest([CSRC / src] + headers, " ".join(flags))
+        dig = _digest(_deps(src), " ".join(flags))
         if not obj.exists() or stamps.get(src) != dig:
             work.append((src, obj, dig))
     jobs = jobs or min(len(work) or 1, os.cpu_count() or 4)

@@ -7,6 +7,8 @@
 // backward terms into the input gradients).  The reference's deterministic convolution
 // needs an extra fixup launch per pass; this build snaps each warp's edge range to row
 // boundaries instead, so every pass is a single launch.
+#include <cuda.h>
+#include <cudaTypedefs.h>
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -23,6 +25,7 @@
 #include "tp_core.cuh"
 #include "tp_kernels_edge.cuh"
 #include "tp_kernels_lk.cuh"
+#include "tp_kernels_uvw_sw.cuh"
 #include "tp_kernels_uvw_tc.cuh"
 
 namespace oeqb {
@@ -39,6 +42,8 @@ const void* lk_kernel_ptr();
 template <class T>
 const void* edge_kernel_ptr(int kind);
 const void* uvw_tc_kernel_ptr(int kind);
+template <class T>
+const void* uvw_sw_kernel_ptr(int kind);
 int set_error(int code, const std::string& msg);
 }  // namespace oeqb
 
@@ -135,6 +140,18 @@ struct oeqb_plan {
     size_t off_passes = 0, off_stages = 0, off_ins = 0, off_outs = 0, off_woff = 0, off_pw = 0;
     float* wsplit = nullptr;  // plan-owned operand image of the weights (rewritten per call)
   } tc;
+  // Shared-weight uvw backward (tp_kernels_uvw_sw.cuh).
+  struct SwTable {
+    bool ok = false;
+    std::vector<SwGroup> groups;
+    std::vector<SwIns> ins;
+    std::vector<SwDw> dw;
+    std::vector<int> woff;
+    std::vector<float> pw_f;
+    std::vector<double> pw_d;
+    size_t off_groups = 0, off_ins = 0, off_dw = 0, off_woff = 0, off_pw = 0;
+    void* wt = nullptr;  // plan-owned W'^T image [nins][32][32] (rewritten per call)
+  } sw;
 
   DevArrays off{};
   unsigned char* dmem = nullptr;
@@ -509,9 +526,10 @@ void build_edge(oeqb_plan& p) {
 
 // Shared-weight float32 uvw problems of the NequIP shape run on the tensor cores: every
 // instruction 32 x 1 -> 32 channels, l1, l3 <= 2, every output irrep 32 channels of l <= 2.
-// Schedule: passes over runs of output irreps whose accumulators fit kTcDCols TMEM columns;
-// inside a pass, one stage per input irrep (its X block staged once), instructions in
-// output order; the first instruction into an output irrep overwrites its accumulator.
+// Schedule: output groups = runs of output irreps whose accumulators fit one kTcDCols-column
+// TMEM buffer (a work unit is a 128-row tile x a group); inside a group, one stage per input
+// irrep (its X block staged once), instructions in output order; the first instruction into
+// an output irrep overwrites its accumulator.
 void build_uvw_tc(oeqb_plan& p) {
   auto& t = p.tc;
   t = oeqb_plan::TcTable{};
@@ -580,6 +598,57 @@ void build_uvw_tc(oeqb_plan& p) {
     ps.out_end = static_cast<int>(t.outs.size());
     t.passes.push_back(ps);
     o = o_end;
+  }
+  t.ok = t.passes.size() <= kTcMaxGroups && t.stages.size() <= kTcMaxStages &&
+         t.ins.size() <= kTcMaxIns && t.outs.size() <= kTcMaxOuts;
+}
+
+// Shared-weight uvw problems with every instruction 32 x 1 -> 32 channels (l <= 3) use the
+// dedicated backward: row-parallel dX / dY and a split-K weight gradient.
+void build_uvw_sw(oeqb_plan& p) {
+  auto& t = p.sw;
+  t = oeqb_plan::SwTable{};
+  if (!p.uvw || p.layout != 0 || !p.shared_w || p.ins_b.empty()) return;
+  if (p.L1dim % 4 || p.L3dim % 4 || p.L2dim > kSwYMax) return;
+  for (const IrrepD& r : p.ir1)
+    if (r.off % 4) return;
+  for (const IrrepD& r : p.ir3)
+    if (r.off % 4) return;
+  for (const InstrD& in : p.ins_b)
+    if (in.code < 0 || in.m1 != 32 || in.m2 != 1 || in.m3 != 32) return;
+  std::vector<std::pair<int, int>> by_woff;
+  for (int n = 0; n < static_cast<int>(p.ins_b.size()); ++n)
+    by_woff.push_back({p.ins_b[n].woff, n});
+  std::sort(by_woff.begin(), by_woff.end());
+  std::vector<int> blk(p.ins_b.size());
+  for (size_t r = 0; r < by_woff.size(); ++r) blk[by_woff[r].second] = static_cast<int>(r);
+  t.woff.resize(p.ins_b.size());
+  t.pw_f.resize(p.ins_b.size());
+  t.pw_d.resize(p.ins_b.size());
+  for (size_t n = 0; n < p.ins_b.size(); ++n) {
+    t.woff[blk[n]] = p.ins_b[n].woff;
+    t.pw_f[blk[n]] = static_cast<float>(p.ins_b[n].pw);
+    t.pw_d[blk[n]] = p.ins_b[n].pw;
+  }
+  for (int i1 = 0; i1 < p.n1; ++i1) {  // every input irrep: dX is written (zeros if unused)
+    SwGroup g{p.ir1[i1].off, p.ir1[i1].l, static_cast<int>(t.ins.size()), 0};
+    if (p.ir1[i1].mul != 32 && p.ir1[i1].mul != 0) return;
+    for (size_t n = 0; n < p.ins_b.size(); ++n) {
+      const InstrD& in = p.ins_b[n];
+      if (in.i1 != i1) continue;
+      t.ins.push_back(SwIns{in.l2, in.l3, p.ir2[in.i2].off, p.ir3[in.i3].off, blk[n], 0, 0, 0});
+    }
+    g.ins_end = static_cast<int>(t.ins.size());
+    t.groups.push_back(g);
+  }
+  std::vector<int> order(p.ins_b.size());
+  for (size_t n = 0; n < order.size(); ++n) order[n] = static_cast<int>(n);
+  std::stable_sort(order.begin(), order.end(),
+                   [&](int a, int b) { return p.ins_b[a].l3 < p.ins_b[b].l3; });
+  for (int n : order) {
+    const InstrD& in = p.ins_b[n];
+    t.dw.push_back(SwDw{in.l1, in.l2, in.l3, p.ir1[in.i1].off, p.ir2[in.i2].off,
+                        p.ir3[in.i3].off, in.woff, 0, in.pw});
   }
   t.ok = true;
 }
@@ -725,6 +794,7 @@ int parse_descriptor(const void* data, size_t n, oeqb_plan& p) {
   build_lk(p);
   build_edge(p);
   build_uvw_tc(p);
+  build_uvw_sw(p);
   return 0;
 }
 
@@ -761,6 +831,11 @@ void layout_tables(oeqb_plan& p, std::vector<unsigned char>& buf) {
   p.tc.off_outs = put(buf, p.tc.outs);
   p.tc.off_woff = put(buf, p.tc.woff);
   p.tc.off_pw = put(buf, p.tc.pw);
+  p.sw.off_groups = put(buf, p.sw.groups);
+  p.sw.off_ins = put(buf, p.sw.ins);
+  p.sw.off_dw = put(buf, p.sw.dw);
+  p.sw.off_woff = put(buf, p.sw.woff);
+  p.sw.off_pw = p.dtype == 2 ? put(buf, p.sw.pw_d) : put(buf, p.sw.pw_f);
   p.off.total = align16(buf.size());
   buf.resize(p.off.total);
 }
@@ -774,6 +849,7 @@ int upload(oeqb_plan& p) {
   OEQB_CUDA(cudaMemset(p.d_status, 0, sizeof(int)));
   if (p.tc.ok)
     OEQB_CUDA(cudaMalloc(&p.tc.wsplit, sizeof(float) * kTcWBlock * p.tc.woff.size()));
+  if (p.sw.ok) OEQB_CUDA(cudaMalloc(&p.sw.wt, p.elem() * 1024 * p.sw.woff.size()));
   return 0;
 }
 
@@ -1060,11 +1136,44 @@ int launch_edge(oeqb_plan& p, int kind, const Args<T>& a, cudaStream_t stream) {
   return 0;
 }
 
+// cuTensorMapEncodeTiled from the driver, looked up once through the runtime (no link-time
+// dependency on libcuda).
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+  });
+  return fn;
+}
+
 // Tensor-core uvw forward: split the weights into the operand image, then the persistent
-// kernel (one CTA per SM, 128-row tiles).  The weight image is plan-owned, so forward calls
-// of one plan on different streams must be ordered by the caller.
+// kernel (one CTA per SM over 128-row tile x output-group units).  The weight image is
+// plan-owned, so forward calls of one plan on different streams must be ordered by the caller.
 int launch_uvw_tc(oeqb_plan& p, const Args<float>& a, cudaStream_t stream) {
   if (a.nitems <= 0) return 0;
+  auto encode = tensor_map_encoder();
+  if (!encode) return fail(OEQB_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+  // X as a 2D tensor [rows, L1dim]; boxes of 128 rows x 32 floats, 128-byte swizzle.
+  CUtensorMap xmap;
+  {
+    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(p.L1dim),
+                                static_cast<cuuint64_t>(a.nitems)};
+    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(p.L1dim) * sizeof(float)};
+    const cuuint32_t box[2] = {32, kTcRows};
+    const cuuint32_t estr[2] = {1, 1};
+    const CUresult r = encode(&xmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(a.X),
+                              dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                              CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS)
+      return fail(OEQB_ERR_CUDA, "cuTensorMapEncodeTiled failed with code " + std::to_string(r));
+  }
   const int nins = static_cast<int>(p.tc.woff.size());
   ArgsTcPrep pr{a.W, p.tc.wsplit, reinterpret_cast<const int*>(p.dmem + p.tc.off_woff),
                 reinterpret_cast<const float*>(p.dmem + p.tc.off_pw), nins};
@@ -1094,16 +1203,81 @@ int launch_uvw_tc(oeqb_plan& p, const Args<float>& a, cudaStream_t stream) {
   t.L2dim = p.L2dim;
   t.L3dim = p.L3dim;
   t.npass = static_cast<int>(p.tc.passes.size());
+  t.nstage = static_cast<int>(p.tc.stages.size());
+  t.nins = static_cast<int>(p.tc.ins.size());
+  t.nout = static_cast<int>(p.tc.outs.size());
   t.passes = reinterpret_cast<const TcPass*>(p.dmem + p.tc.off_passes);
   t.stages = reinterpret_cast<const TcStage*>(p.dmem + p.tc.off_stages);
   t.ins = reinterpret_cast<const TcIns*>(p.dmem + p.tc.off_ins);
   t.outs = reinterpret_cast<const TcOut*>(p.dmem + p.tc.off_outs);
   t.status = p.d_status;
-  const long long tiles = (a.nitems + kTcRows - 1) / kTcRows;
-  const long long blocks = std::min<long long>(tiles, p.sm_count);
-  void* params[] = {&t};
+  const long long units = (a.nitems + kTcRows - 1) / kTcRows * t.npass;
+  const long long blocks = std::min<long long>(units, p.sm_count);
+  void* params[] = {&t, &xmap};
   OEQB_CUDA(cudaLaunchKernel(kernel, dim3(static_cast<unsigned>(blocks)), dim3(kTcThreads), params,
                              kTcSmemBytes, stream));
+  return 0;
+}
+
+// Shared-weight uvw backward: W'^T image, row-parallel dX / dY, split-K dW (dW was zeroed).
+template <class T>
+int launch_uvw_sw(oeqb_plan& p, const Args<T>& a, cudaStream_t stream) {
+  if (a.nitems <= 0) return 0;
+  const int nins = static_cast<int>(p.sw.woff.size());
+  {
+    const T* W = a.W;
+    T* Wt = static_cast<T*>(p.sw.wt);
+    const int* woff = reinterpret_cast<const int*>(p.dmem + p.sw.off_woff);
+    const T* pw = reinterpret_cast<const T*>(p.dmem + p.sw.off_pw);
+    void* params[] = {&W, &Wt, &woff, &pw, const_cast<int*>(&nins)};
+    OEQB_CUDA(cudaLaunchKernel(uvw_sw_kernel_ptr<T>(2), dim3((nins * 1024 + 255) / 256), dim3(256),
+                               params, 0, stream));
+  }
+  ArgsSw<T> v{};
+  v.X = a.X;
+  v.Y = a.Y;
+  v.Wt = static_cast<const T*>(p.sw.wt);
+  v.dZ = a.Gz;
+  v.dX = a.out0;
+  v.dY = a.out1;
+  v.dW = a.out2;
+  v.B = a.nitems;
+  v.L1dim = p.L1dim;
+  v.L2dim = p.L2dim;
+  v.L3dim = p.L3dim;
+  v.ngroups = static_cast<int>(p.sw.groups.size());
+  v.ndw = static_cast<int>(p.sw.dw.size());
+  v.groups = reinterpret_cast<const SwGroup*>(p.dmem + p.sw.off_groups);
+  v.ins = reinterpret_cast<const SwIns*>(p.dmem + p.sw.off_ins);
+  v.dw = reinterpret_cast<const SwDw*>(p.dmem + p.sw.off_dw);
+  const void* kxy = uvw_sw_kernel_ptr<T>(0);
+  int per_sm;
+  {
+    std::lock_guard<std::mutex> g(p.mu);
+    auto it = p.occ.find(kxy);
+    if (it == p.occ.end()) {
+      int n = 0;
+      OEQB_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kxy, kSwThreads, 0));
+      if (n <= 0) return fail(OEQB_ERR_UNSUPPORTED, "uvw backward kernel does not fit");
+      it = p.occ.emplace(kxy, n).first;
+    }
+    per_sm = it->second;
+  }
+  const long long tiles = (a.nitems + kSwRows - 1) / kSwRows;
+  const long long bxy = std::max<long long>(1, std::min<long long>(tiles, (long long)p.sm_count * per_sm));
+  // Weight gradient: instruction groups x row chunks, about four CTAs per SM.
+  const int ngrp = (v.ndw + kSwDwSlots - 1) / kSwDwSlots;
+  long long chunks = std::max<long long>(1, (4LL * p.sm_count + ngrp - 1) / ngrp);
+  v.rows_per_chunk = std::max<long long>(kSwBatch, (a.nitems + chunks - 1) / chunks);
+  v.rows_per_chunk = (v.rows_per_chunk + kSwBatch - 1) / kSwBatch * kSwBatch;
+  chunks = (a.nitems + v.rows_per_chunk - 1) / v.rows_per_chunk;
+  const void* kdw = uvw_sw_kernel_ptr<T>(1);
+  if (int rc = allow_max_smem(p.device, kdw)) return rc;
+  void* params[] = {&v};
+  OEQB_CUDA(cudaLaunchKernel(kxy, dim3(static_cast<unsigned>(bxy)), dim3(kSwThreads), params, 0,
+                             stream));
+  OEQB_CUDA(cudaLaunchKernel(kdw, dim3(ngrp, static_cast<unsigned>(chunks)), dim3(kSwThreads),
+                             params, sw_dw_smem<T>(), stream));
   return 0;
 }
 
@@ -1155,6 +1329,7 @@ int tp_backward_t(oeqb_plan* p, int64_t B, const void* X, void* dX, const void* 
   a.out0 = static_cast<T*>(dX);
   a.out1 = static_cast<T*>(dY);
   a.out2 = static_cast<T*>(dW);
+  if (p->sw.ok && aligned16(dZ)) return launch_uvw_sw(*p, a, s);
   if (p->lk.ok && lk_aligned(*p, a)) return launch_lk(*p, a, s);
   if (p->segb.ok) return launch_seg(*p, 1, a, s);
   if (p->row_ok) return launch_row(*p, 1, a, s);
@@ -1300,6 +1475,7 @@ int oeqb_plan_create(const void* descriptor, size_t nbytes, int device, oeqb_pla
     if (p->dmem) cudaFree(p->dmem);
     if (p->d_status) cudaFree(p->d_status);
     if (p->tc.wsplit) cudaFree(p->tc.wsplit);
+    if (p->sw.wt) cudaFree(p->sw.wt);
     delete p;
     return rc;
   }
@@ -1314,6 +1490,7 @@ int oeqb_plan_destroy(oeqb_plan* p) {
     if (p->dmem) cudaFree(p->dmem);
     if (p->d_status) cudaFree(p->d_status);
     if (p->tc.wsplit) cudaFree(p->tc.wsplit);
+    if (p->sw.wt) cudaFree(p->sw.wt);
   }
   delete p;
   return 0;

@@ -21,15 +21,20 @@
 //  * One thread of the MMA warp issues tcgen05.mma (kind::tf32, A from TMEM, B from shared
 //    memory, D in TMEM, M = 128, N = 32, K = 8) and releases A slots / W slots / the
 //    accumulator with tcgen05.commit on mbarriers.
-//  * A producer warp stages X (per input irrep, 128 rows, double-buffered, padded rows so the
-//    row-per-thread reads are bank-conflict free) and the W ring with cp.async.bulk.
-//  * TMEM: 320 accumulator columns (one pass = a run of output irreps whose 32 * (2 l3 + 1)
-//    columns fit) + 3 A slots of 64 columns (hi | lo).  The epilogue reads D with tcgen05.ld
-//    (each thread its row, 8 channels x d3 components = one contiguous piece of the Z row).
+//  * A producer warp stages X per input irrep with 2D TMA tensor copies (boxes of 128 rows x
+//    32 floats, 128-byte swizzle so the row-per-thread reads are bank-conflict free,
+//    double-buffered); a second producer warp streams the W ring with cp.async.bulk.
+//  * Work unit = 128-row tile x output group (a run of output irreps whose 32 * (2 l3 + 1)
+//    accumulator columns fit 160).  TMEM: two 160-column accumulator buffers (unit i uses
+//    buffer i & 1, so the epilogue of unit i - 1 overlaps the MMAs of unit i) + 3 A slots of
+//    64 columns (hi | lo).  The epilogue reads D with tcgen05.ld (each thread its row,
+//    8 channels x d3 components = one contiguous piece of the Z row).
 //
 // Every mbarrier wait is bounded (status flag 3 on expiry); the producer drains its own
 // copies and the MMA thread's work is complete before TMEM is released.
 #pragma once
+
+#include <cuda.h>
 
 #include "tp_kernels_row.cuh"
 
@@ -38,16 +43,17 @@ namespace oeqb {
 constexpr int kTcRows = 128;
 constexpr int kTcComputeWarps = 16;
 constexpr int kTcMmaWarp = 16;
-constexpr int kTcProdWarp = 17;
-constexpr int kTcThreads = 18 * 32;
-constexpr int kTcDCols = 320;
+constexpr int kTcProdWarp = 17;   // X stages (TMA tensor copies)
+constexpr int kTcWProdWarp = 18;  // W ring (bulk copies)
+constexpr int kTcThreads = 19 * 32;
+constexpr int kTcDCols = 160;              // per accumulator buffer (two buffers)
 constexpr int kTcASlots = 3;
-constexpr int kTcACol0 = kTcDCols;          // A slot s: columns kTcACol0 + 64 s (+32 for lo)
+constexpr int kTcACol0 = 2 * kTcDCols;      // A slot s: columns kTcACol0 + 64 s (+32 for lo)
 constexpr int kTcWSlots = 4;
 constexpr int kTcYMax = 16;
 constexpr int kTcYStride = 17;
 constexpr int kTcMaxD = 5;
-constexpr int kTcXStrideMax = 32 * kTcMaxD + 4;   // floats per staged X row (padded)
+constexpr int kTcXBox = kTcRows * 32;            // floats per TMA box (128 rows x 32 floats)
 constexpr int kTcWBlock = 2 * 32 * 32;            // floats per instruction: hi | lo
 constexpr int kTcTmemCols = 512;
 
@@ -71,7 +77,7 @@ struct ArgsTc {
   float* Z;
   long long B;
   int L1dim, L2dim, L3dim;
-  int npass;
+  int npass, nstage, nins, nout;  // output groups (work unit = 128-row tile x group), ...
   const TcPass* passes;
   const TcStage* stages;
   const TcIns* ins;
@@ -79,13 +85,18 @@ struct ArgsTc {
   int* status;
 };
 
+// Schedule tables held in shared memory.
+constexpr int kTcMaxGroups = 16, kTcMaxStages = 64, kTcMaxIns = 64, kTcMaxOuts = 48;
+
 // Shared-memory image (dynamic; the no-swizzle operand layout needs 16-byte alignment only).
-constexpr int kTcSmemBars = 0;                                   // 20 mbarriers + TMEM base
-constexpr int kTcSmemY = 256;                                    // [2][128][17] floats
-constexpr int kTcSmemW = kTcSmemY + 2 * kTcRows * kTcYStride * 4 + 768;   // 1024-aligned
-constexpr int kTcSmemX = kTcSmemW + kTcWSlots * kTcWBlock * 4;   // [2][128][stride] floats
-constexpr int kTcSmemBytes = kTcSmemX + 2 * kTcRows * kTcXStrideMax * 4;
-static_assert(kTcSmemW % 1024 == 0, "W ring offset");
+constexpr int kTcSmemBars = 0;                                   // 23 mbarriers + TMEM base
+constexpr int kTcSmemTab = 256;                                  // schedule tables
+constexpr int kTcSmemY = kTcSmemTab + 16 * kTcMaxGroups + 16 * kTcMaxStages + 32 * kTcMaxIns +
+                         16 * kTcMaxOuts;                        // [2][128][17] floats
+constexpr int kTcSmemW = (kTcSmemY + 2 * kTcRows * kTcYStride * 4 + 1023) / 1024 * 1024;
+constexpr int kTcSmemX = kTcSmemW + kTcWSlots * kTcWBlock * 4;   // [2][kTcMaxD boxes]
+constexpr int kTcSmemBytes = kTcSmemX + 2 * kTcMaxD * kTcXBox * 4 + 1024;  // + base alignment
+static_assert(kTcSmemW % 1024 == 0 && kTcSmemX % 1024 == 0, "1024-byte aligned regions");
 static_assert(kTcSmemBytes <= 227 * 1024, "shared memory image too large");
 
 // ------------------------------------------------------------------ tcgen05 wrappers
@@ -150,6 +161,16 @@ __device__ __forceinline__ void tc_commit(unsigned long long* bar) {
       : "memory");
 }
 
+// 2D tiled TMA load of box (x, y) of `map` into shared memory, completing on `bar`.
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y,
+                                            unsigned long long* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3}], [%4];\n" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<unsigned long long>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
+
 // Instruction descriptor: D f32, A/B tf32, both K-major, N = 32, M = 128.
 constexpr unsigned kTcIdesc = (1u << 4) | (2u << 7) | (2u << 10) | ((32u >> 3) << 17) |
                               ((128u >> 4) << 24);
@@ -195,7 +216,8 @@ __global__ void tp_uvw_tc_prep(const ArgsTcPrep v) {
 // ------------------------------------------------------------------ compute-warp pieces
 
 struct TcBars {
-  unsigned long long *x_full, *x_empty, *w_full, *w_empty, *a_full, *a_empty, *d_full, *d_empty;
+  unsigned long long *x_full, *x_empty, *w_full, *w_empty, *a_full, *a_empty, *d_full, *d_empty,
+      *mma_done;
   unsigned* tmem_slot;
 };
 
@@ -209,29 +231,56 @@ __device__ __forceinline__ TcBars tc_bars(unsigned char* smem) {
   b.a_full = p + 4 + 2 * kTcWSlots;
   b.a_empty = b.a_full + kTcASlots;
   b.d_full = b.a_empty + kTcASlots;
-  b.d_empty = b.d_full + 1;
-  b.tmem_slot = reinterpret_cast<unsigned*>(b.d_empty + 1);
+  b.d_empty = b.d_full + 2;
+  b.mma_done = b.d_empty + 2;
+  b.tmem_slot = reinterpret_cast<unsigned*>(b.mma_done + 1);
   return b;
 }
 
-// Empty-barrier wait of use `it` of a ring of n buffers (the first n uses start free).
-__device__ __forceinline__ bool tc_wait_empty(unsigned long long* bar, unsigned it, unsigned n,
-                                              int* status) {
+// Barrier wait that lets the thread sleep until the phase completes (suspend-time hint), so
+// waiting warps do not compete for issue slots; bounded like mbar_wait.
+__device__ __forceinline__ bool tc_try_wait(unsigned long long* bar, unsigned parity) {
+  unsigned ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n"
+      " selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(20000u)
+      : "memory");
+  return ok != 0;
+}
+
+__device__ __forceinline__ bool tc_wait(unsigned long long* bar, unsigned parity, int* status) {
+  if (tc_try_wait(bar, parity)) return true;
+  const unsigned long long t0 = global_ns();
+  for (;;) {
+    if (tc_try_wait(bar, parity)) return true;
+    if (status && *reinterpret_cast<volatile int*>(status) == 3) return false;
+    if (global_ns() - t0 > kWaitNs) {
+      if (status) atomicCAS(status, 0, 3);
+      return false;
+    }
+  }
+}
+
+__device__ __forceinline__ bool tc_wait_ring(unsigned long long* bar, unsigned it, unsigned n,
+                                            int* status) {
   if (it < n) return true;
-  return mbar_wait(bar, ((it / n) - 1) & 1, status);
+  return tc_wait(bar, ((it / n) - 1) & 1, status);
 }
 
 // One stage (an input irrep of degree L1): the thread's X values x[8][D1] are in registers;
 // runs every instruction of the stage, producing A slots.
 template <int L1>
-__device__ __forceinline__ void tc_stage_compute(const ArgsTc& a, const TcBars& bars,
+__device__ __forceinline__ void tc_stage_compute(const ArgsTc& a, const TcIns* insv,
+                                                 const TcBars& bars,
                                                  const TcStage& st, const float* yrow,
                                                  const float (&x)[8 * (2 * L1 + 1)],
                                                  unsigned tbase_lane, int c, unsigned& a_it,
                                                  int lane) {
   constexpr int D1 = 2 * L1 + 1;
   for (int ni = st.ins_begin; ni < st.ins_end; ++ni) {
-    const TcIns in = a.ins[ni];
+    const TcIns in = insv[ni];
     dispatch_bc<L1>(pair_code(in.l2, in.l3), [&]<int L2, int L3>() {
       constexpr int D3 = 2 * L3 + 1;
       float P[D1 * D3];
@@ -250,7 +299,7 @@ __device__ __forceinline__ void tc_stage_compute(const ArgsTc& a, const TcBars& 
           lo[uu] = tf32_bits(t - __uint_as_float(hi[uu]));
         }
         const unsigned s = a_it % kTcASlots;
-        tc_wait_empty(&bars.a_empty[s], a_it, kTcASlots, a.status);
+        tc_wait_ring(&bars.a_empty[s], a_it, kTcASlots, a.status);
         tc_fence_after();
         const unsigned col = tbase_lane + kTcACol0 + 64 * s + 8 * c;
         tmem_st8(col, hi);
@@ -295,19 +344,34 @@ __device__ __forceinline__ void tc_store_out(const ArgsTc& a, const TcOut& o, un
 // ------------------------------------------------------------------ the kernel
 
 template <class T>
-__global__ void __launch_bounds__(kTcThreads, 1) tp_uvw_tc_fwd(const ArgsTc a) {
-  extern __shared__ __align__(16) unsigned char smem[];
+__global__ void __launch_bounds__(kTcThreads, 1)
+    tp_uvw_tc_fwd(const __grid_constant__ ArgsTc a, const __grid_constant__ CUtensorMap xmap) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  // 128-byte swizzled TMA boxes need a 1024-byte aligned destination.
+  unsigned char* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
   const TcBars bars = tc_bars(smem);
   float* ybuf = reinterpret_cast<float*>(smem + kTcSmemY);
   float* wring = reinterpret_cast<float*>(smem + kTcSmemW);
   float* xbuf = reinterpret_cast<float*>(smem + kTcSmemX);
+  TcPass* groups = reinterpret_cast<TcPass*>(smem + kTcSmemTab);
+  TcStage* stages = reinterpret_cast<TcStage*>(groups + kTcMaxGroups);
+  TcIns* insv = reinterpret_cast<TcIns*>(stages + kTcMaxStages);
+  TcOut* outs = reinterpret_cast<TcOut*>(insv + kTcMaxIns);
   const long long ntiles = (a.B + kTcRows - 1) / kTcRows;
+  const int ng = a.npass;
+  const long long nunits = ntiles * ng;
 
+  for (int i = threadIdx.x; i < a.npass; i += blockDim.x) groups[i] = a.passes[i];
+  for (int i = threadIdx.x; i < a.nstage; i += blockDim.x) stages[i] = a.stages[i];
+  for (int i = threadIdx.x; i < a.nins; i += blockDim.x) insv[i] = a.ins[i];
+  for (int i = threadIdx.x; i < a.nout; i += blockDim.x) outs[i] = a.outs[i];
   if (threadIdx.x == 0) {
     for (int i = 0; i < 2; ++i) {
       mbar_init(&bars.x_full[i], 1);
       mbar_init(&bars.x_empty[i], kTcComputeWarps);
+      mbar_init(&bars.d_full[i], 1);
+      mbar_init(&bars.d_empty[i], kTcComputeWarps);
     }
     for (int i = 0; i < kTcWSlots; ++i) {
       mbar_init(&bars.w_full[i], 1);
@@ -317,8 +381,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tp_uvw_tc_fwd(const ArgsTc a) {
       mbar_init(&bars.a_full[i], kTcComputeWarps);
       mbar_init(&bars.a_empty[i], 1);
     }
-    mbar_init(bars.d_full, 1);
-    mbar_init(bars.d_empty, kTcComputeWarps);
+    mbar_init(bars.mma_done, 1);
     fence_mbar_init();
   }
   if (wid == kTcMmaWarp) {
@@ -334,160 +397,176 @@ __global__ void __launch_bounds__(kTcThreads, 1) tp_uvw_tc_fwd(const ArgsTc a) {
   const unsigned tmem = *bars.tmem_slot;
 
   if (wid == kTcProdWarp) {
-    // ---------------- producer: X stages and W ring, in schedule order
-    unsigned xs_it = 0, w_it = 0;
-    unsigned long long* last_x = nullptr;
-    unsigned last_x_par = 0;
-    unsigned long long* last_w = nullptr;
-    unsigned last_w_par = 0;
-    for (long long tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
-      const long long row0 = tile * kTcRows;
-      const long long rem = a.B - row0;
-      const int nr = rem < kTcRows ? static_cast<int>(rem) : kTcRows;
-      for (int pi = 0; pi < a.npass; ++pi) {
-        const TcPass ps = a.passes[pi];
-        for (int si = ps.stage_begin; si < ps.stage_end; ++si) {
-          const TcStage st = a.stages[si];
-          const int d1 = 2 * st.l1 + 1;
-          const int stride = 32 * d1 + 4;
+    // ---------------- X producer: one TMA box per 32 floats of the stage's input block
+    if (lane == 0) {
+      unsigned xs_it = 0;
+      for (long long u = blockIdx.x; u < nunits; u += gridDim.x) {
+        const int row0 = static_cast<int>((u / ng) * kTcRows);
+        const TcPass gp = groups[u % ng];
+        for (int si = gp.stage_begin; si < gp.stage_end; ++si) {
+          const TcStage st = stages[si];
+          const int nbox = 2 * st.l1 + 1;
           const unsigned b = xs_it & 1;
-          tc_wait_empty(&bars.x_empty[b], xs_it, 2, a.status);
-          const unsigned bytes = static_cast<unsigned>(32 * d1 * 4);
-          if (lane == 0) mbar_expect_tx(&bars.x_full[b], bytes * nr);
-          __syncwarp();
-          float* dst = xbuf + static_cast<size_t>(b) * kTcRows * kTcXStrideMax;
-          for (int r = lane; r < nr; r += 32)
-            bulk_g2s(dst + r * stride, a.X + (row0 + r) * a.L1dim + st.x_off, bytes,
-                     &bars.x_full[b]);
-          last_x = &bars.x_full[b];
-          last_x_par = (xs_it >> 1) & 1;
+          tc_wait_ring(&bars.x_empty[b], xs_it, 2, a.status);
+          mbar_expect_tx(&bars.x_full[b], static_cast<unsigned>(nbox * kTcXBox * 4));
+          float* dst = xbuf + static_cast<size_t>(b) * kTcMaxD * kTcXBox;
+          for (int j = 0; j < nbox; ++j)
+            tma_load_2d(dst + j * kTcXBox, &xmap, st.x_off + 32 * j, row0, &bars.x_full[b]);
           ++xs_it;
+        }
+      }
+      // Drain (also after a timed-out wait): the last phase issued on each buffer has landed.
+      for (unsigned i = xs_it > 2 ? xs_it - 2 : 0; i < xs_it; ++i)
+        mbar_wait(&bars.x_full[i & 1], (i >> 1) & 1, nullptr);
+    }
+    __syncwarp();
+  } else if (wid == kTcWProdWarp) {
+    // ---------------- W producer: one 8 KiB operand image per instruction
+    if (lane == 0) {
+      unsigned w_it = 0;
+      for (long long u = blockIdx.x; u < nunits; u += gridDim.x) {
+        const TcPass gp = groups[u % ng];
+        for (int si = gp.stage_begin; si < gp.stage_end; ++si) {
+          const TcStage st = stages[si];
           for (int ni = st.ins_begin; ni < st.ins_end; ++ni) {
             const unsigned ws = w_it % kTcWSlots;
-            tc_wait_empty(&bars.w_empty[ws], w_it, kTcWSlots, a.status);
-            if (lane == 0) {
-              mbar_expect_tx(&bars.w_full[ws], kTcWBlock * 4);
-              bulk_g2s(wring + ws * kTcWBlock,
-                       a.Wsplit + static_cast<size_t>(a.ins[ni].wblk) * kTcWBlock,
-                       kTcWBlock * 4, &bars.w_full[ws]);
-            }
-            last_w = &bars.w_full[ws];
-            last_w_par = (w_it / kTcWSlots) & 1;
+            tc_wait_ring(&bars.w_empty[ws], w_it, kTcWSlots, a.status);
+            mbar_expect_tx(&bars.w_full[ws], kTcWBlock * 4);
+            bulk_g2s(wring + ws * kTcWBlock,
+                     a.Wsplit + static_cast<size_t>(insv[ni].wblk) * kTcWBlock, kTcWBlock * 4,
+                     &bars.w_full[ws]);
             ++w_it;
           }
         }
       }
+      for (unsigned i = w_it > kTcWSlots ? w_it - kTcWSlots : 0; i < w_it; ++i)  // drain
+        mbar_wait(&bars.w_full[i % kTcWSlots], (i / kTcWSlots) & 1, nullptr);
     }
-    // Drain: the last copies issued have landed (normally long since).
-    if (last_x) mbar_wait(last_x, last_x_par, nullptr);
-    if (last_w) mbar_wait(last_w, last_w_par, nullptr);
+    __syncwarp();
   } else if (wid == kTcMmaWarp) {
-    // ---------------- MMA issuer (one thread)
+    // ---------------- MMA issuer (one thread); unit i accumulates into D buffer i & 1
     if (lane == 0) {
-      unsigned a_it = 0, w_it = 0, pass_it = 0;
-      const unsigned wring_s = smem_u32(wring);
-      for (long long tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
-        for (int pi = 0; pi < a.npass; ++pi) {
-          const TcPass ps = a.passes[pi];
-          if (pass_it > 0) mbar_wait(bars.d_empty, (pass_it - 1) & 1, a.status);
-          tc_fence_after();
-          for (int si = ps.stage_begin; si < ps.stage_end; ++si) {
-            const TcStage st = a.stages[si];
-            for (int ni = st.ins_begin; ni < st.ins_end; ++ni) {
-              const TcIns in = a.ins[ni];
-              const unsigned ws = w_it % kTcWSlots;
-              mbar_wait(&bars.w_full[ws], (w_it / kTcWSlots) & 1, a.status);
-              const unsigned bh = wring_s + ws * kTcWBlock * 4, bl = bh + 4096;
-              const int d3 = 2 * in.l3 + 1;
-              for (int k = 0; k < d3; ++k) {
-                const unsigned s = a_it % kTcASlots;
-                mbar_wait(&bars.a_full[s], (a_it / kTcASlots) & 1, a.status);
-                tc_fence_after();
-                const unsigned dcol = tmem + in.dcol + 32 * k;
-                const unsigned acol = tmem + kTcACol0 + 64 * s;
+      unsigned a_it = 0, w_it = 0, it = 0;
+      const unsigned long long wdesc0 = tc_bdesc(smem_u32(wring));
+      for (long long u = blockIdx.x; u < nunits; u += gridDim.x, ++it) {
+        const TcPass gp = groups[u % ng];
+        const unsigned db = it & 1;
+        if (it >= 2) tc_wait(&bars.d_empty[db], ((it >> 1) - 1) & 1, a.status);
+        tc_fence_after();
+        for (int si = gp.stage_begin; si < gp.stage_end; ++si) {
+          const TcStage st = stages[si];
+          for (int ni = st.ins_begin; ni < st.ins_end; ++ni) {
+            const TcIns in = insv[ni];
+            const unsigned ws = w_it % kTcWSlots;
+            tc_wait(&bars.w_full[ws], (w_it / kTcWSlots) & 1, a.status);
+            // Start-address field advances in 16-byte units: slot ws at ws * 8 KiB, lo half at
+            // +4 KiB, K step ks at +256 B.
+            const unsigned long long dh = wdesc0 + ws * (kTcWBlock * 4 / 16);
+            const unsigned long long dl = dh + 4096 / 16;
+            const int d3 = 2 * in.l3 + 1;
+            const unsigned dcol0 = tmem + db * kTcDCols + in.dcol;
+            for (int k = 0; k < d3; ++k) {
+              const unsigned s = a_it % kTcASlots;
+              tc_wait(&bars.a_full[s], (a_it / kTcASlots) & 1, a.status);
+              tc_fence_after();
+              const unsigned dcol = dcol0 + 32 * k;
+              const unsigned acol = tmem + kTcACol0 + 64 * s;
+              tc_mma_tf32(dcol, acol, dh, kTcIdesc, in.first ? 0u : 1u);
+              tc_mma_tf32(dcol, acol, dl, kTcIdesc, 1u);
+              tc_mma_tf32(dcol, acol + 32, dh, kTcIdesc, 1u);
 #pragma unroll
-                for (int ks = 0; ks < 4; ++ks) {
-                  tc_mma_tf32(dcol, acol + 8 * ks, tc_bdesc(bh + 256 * ks), kTcIdesc,
-                              (in.first && ks == 0) ? 0u : 1u);
-                  tc_mma_tf32(dcol, acol + 8 * ks, tc_bdesc(bl + 256 * ks), kTcIdesc, 1u);
-                  tc_mma_tf32(dcol, acol + 32 + 8 * ks, tc_bdesc(bh + 256 * ks), kTcIdesc, 1u);
-                }
-                tc_commit(&bars.a_empty[s]);
-                ++a_it;
+              for (int ks = 1; ks < 4; ++ks) {
+                tc_mma_tf32(dcol, acol + 8 * ks, dh + 16 * ks, kTcIdesc, 1u);
+                tc_mma_tf32(dcol, acol + 8 * ks, dl + 16 * ks, kTcIdesc, 1u);
+                tc_mma_tf32(dcol, acol + 32 + 8 * ks, dh + 16 * ks, kTcIdesc, 1u);
               }
-              tc_commit(&bars.w_empty[ws]);
-              ++w_it;
+              tc_commit(&bars.a_empty[s]);
+              ++a_it;
             }
+            tc_commit(&bars.w_empty[ws]);
+            ++w_it;
           }
-          tc_commit(bars.d_full);
-          ++pass_it;
         }
+        tc_commit(&bars.d_full[db]);
       }
+      // Every MMA of this thread has completed before TMEM is released (also when a wait
+      // timed out and the pipeline ran on without its handshakes).
+      tc_commit(bars.mma_done);
+      mbar_wait(bars.mma_done, 0, nullptr);
     }
     __syncwarp();
   } else {
-    // ---------------- compute warps
+    // ---------------- compute warps: A slots of unit i, then the epilogue of unit i - 1
     const int q = wid & 3, c = wid >> 2;
     const int rl = 32 * q + lane;  // row within the tile
     const unsigned tbase_lane = tmem + (static_cast<unsigned>(32 * q) << 16);
-    unsigned a_it = 0, xs_it = 0, pass_it = 0, tile_it = 0;
-    for (long long tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++tile_it) {
-      const long long row0 = tile * kTcRows;
-      const long long row = row0 + rl;
+    unsigned a_it = 0, xs_it = 0, it = 0;
+    long long prev_row = 0;
+    int prev_g = 0;
+    auto epilogue = [&](unsigned pit, int g, long long row) {
+      const unsigned db = pit & 1;
+      tc_wait(&bars.d_full[db], (pit >> 1) & 1, a.status);
+      tc_fence_after();
+      const TcPass gp = groups[g];
+      const unsigned dbase = tbase_lane + db * kTcDCols;
       const bool valid = row < a.B;
-      float* yb = ybuf + (tile_it & 1) * kTcRows * kTcYStride;
+      for (int oi = gp.out_begin; oi < gp.out_end; ++oi) {
+        const TcOut o = outs[oi];
+        if (o.d3 == 1)
+          tc_store_out<1>(a, o, dbase, c, row, valid);
+        else if (o.d3 == 3)
+          tc_store_out<3>(a, o, dbase, c, row, valid);
+        else
+          tc_store_out<5>(a, o, dbase, c, row, valid);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars.d_empty[db]);
+    };
+    for (long long u = blockIdx.x; u < nunits; u += gridDim.x, ++it) {
+      const long long row = (u / ng) * kTcRows + rl;
+      const int g = static_cast<int>(u % ng);
+      const TcPass gp = groups[g];
+      float* yb = ybuf + (it & 1) * kTcRows * kTcYStride;
       if (c == 0) {
+        const bool valid = row < a.B;
         for (int j = 0; j < kTcYMax; ++j)
           yb[rl * kTcYStride + j] = (valid && j < a.L2dim) ? a.Y[row * a.L2dim + j] : 0.f;
       }
       asm volatile("bar.sync 1, %0;\n" ::"n"(kTcComputeWarps * 32) : "memory");
       const float* yrow = yb + rl * kTcYStride;
-      for (int pi = 0; pi < a.npass; ++pi) {
-        const TcPass ps = a.passes[pi];
-        for (int si = ps.stage_begin; si < ps.stage_end; ++si) {
-          const TcStage st = a.stages[si];
-          const unsigned b = xs_it & 1;
-          mbar_wait(&bars.x_full[b], (xs_it >> 1) & 1, a.status);
-          const float* xs = xbuf + static_cast<size_t>(b) * kTcRows * kTcXStrideMax;
-          dispatch_l(st.l1, [&]<int L1>() {
-            if constexpr (L1 <= 2) {
-              constexpr int D1 = 2 * L1 + 1;
-              float x[8 * D1];
-              const float4* src =
-                  reinterpret_cast<const float4*>(xs + rl * (32 * D1 + 4) + 8 * c * D1);
+      for (int si = gp.stage_begin; si < gp.stage_end; ++si) {
+        const TcStage st = stages[si];
+        const unsigned b = xs_it & 1;
+        tc_wait(&bars.x_full[b], (xs_it >> 1) & 1, a.status);
+        // Row rl of box j: 32 floats, 16-byte chunk q stored at chunk q ^ (rl & 7).
+        const float* xs = xbuf + static_cast<size_t>(b) * kTcMaxD * kTcXBox + rl * 32;
+        dispatch_l(st.l1, [&]<int L1>() {
+          if constexpr (L1 <= 2) {
+            constexpr int D1 = 2 * L1 + 1;
+            float x[8 * D1];
 #pragma unroll
-              for (int e = 0; e < 2 * D1; ++e) {
-                const float4 t = src[e];
-                x[4 * e] = t.x;
-                x[4 * e + 1] = t.y;
-                x[4 * e + 2] = t.z;
-                x[4 * e + 3] = t.w;
-              }
-              __syncwarp();
-              if (lane == 0) mbar_arrive(&bars.x_empty[b]);
-              tc_stage_compute<L1>(a, bars, st, yrow, x, tbase_lane, c, a_it, lane);
+            for (int e = 0; e < 2 * D1; ++e) {
+              const int f = 8 * c * D1 + 4 * e;  // float index inside the input block
+              const float4 t = *reinterpret_cast<const float4*>(
+                  xs + (f >> 5) * kTcXBox + ((((f & 31) >> 2) ^ (rl & 7)) << 2));
+              x[4 * e] = t.x;
+              x[4 * e + 1] = t.y;
+              x[4 * e + 2] = t.z;
+              x[4 * e + 3] = t.w;
             }
-          });
-          ++xs_it;
-        }
-        // epilogue of the pass
-        mbar_wait(bars.d_full, pass_it & 1, a.status);
-        tc_fence_after();
-        for (int oi = ps.out_begin; oi < ps.out_end; ++oi) {
-          const TcOut o = a.outs[oi];
-          if (o.d3 == 1)
-            tc_store_out<1>(a, o, tbase_lane, c, row, valid);
-          else if (o.d3 == 3)
-            tc_store_out<3>(a, o, tbase_lane, c, row, valid);
-          else
-            tc_store_out<5>(a, o, tbase_lane, c, row, valid);
-        }
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(bars.d_empty);
-        ++pass_it;
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&bars.x_empty[b]);
+            tc_stage_compute<L1>(a, insv, bars, st, yrow, x, tbase_lane, c, a_it, lane);
+          }
+        });
+        ++xs_it;
       }
+      if (it > 0) epilogue(it - 1, prev_g, prev_row);
+      prev_g = g;
+      prev_row = row;
     }
+    if (it > 0) epilogue(it - 1, prev_g, prev_row);
   }
   tc_fence_before();
   __syncthreads();

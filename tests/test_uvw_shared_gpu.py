@@ -1,9 +1,10 @@
-"""Tensor-core (tcgen05, 3xTF32) forward of shared-weight uvw problems vs the CPU oracle.
+"""Shared-weight uvw problems (BASELINE config C4 shape) vs the CPU oracle.
 
-The NequIP-shaped problem of BASELINE config C4 (32 channels per irrep, l <= 2, shared
-weights, float32) runs on ``tp_uvw_tc_fwd``.  The forward must stay within the float32
-bound (normalised max error 1e-5) on partial tiles, many tiles, and problems whose output
-irreps are ordered differently or receive no instruction.
+The forward of the NequIP-shaped problem (32 channels per irrep, l <= 2, shared weights,
+float32) runs on the tensor cores (``tp_uvw_tc_fwd``); the backward of this class (float32
+and float64) runs on ``tp_uvw_sw_dxy`` / ``tp_uvw_sw_dw``.  Results must stay within the
+bounds (normalised max error 1e-5 fp32, 1e-12 fp64) on partial tiles, many tiles, and
+problems whose output irreps are ordered differently or receive no instruction.
 """
 
 import numpy as np
@@ -110,3 +111,38 @@ def test_unfed_output_irrep_and_mixed_order(cuda_device):
     assert nerr(Z, want) <= TOL[np.float32]
     off = p.irreps_out.slices()[3]
     assert torch.count_nonzero(Z[:, off]).item() == 0
+    # Backward of the same problem (every input irrep is read; the 2e output gets no path).
+    G = rng.normal(size=(rows, p.irreps_out.dim))
+    x, y, w = (t.clone().requires_grad_() for t in (xs, ys, ws))
+    tp(x, y, w).backward(to_dev(G, np.float32))
+    gX, gY, gW = O.backward(op, X, Y, W, G)
+    assert nerr(x.grad, gX) <= TOL[np.float32]
+    assert nerr(y.grad, gY) <= TOL[np.float32]
+    assert nerr(w.grad, gW[perm]) <= TOL[np.float32]
+
+
+@pytest.mark.parametrize("dtype", [np.float32, np.float64], ids=["f32", "f64"])
+@pytest.mark.parametrize("rows", [1, 33, 1000])
+def test_c4_backward_vs_oracle(rows, dtype, cuda_device):
+    import openequivariance_b200 as oeq
+    from openequivariance_b200.problems import fully_connected_tpp
+
+    p = fully_connected_tpp(*C4, shared_weights=True, internal_weights=False,
+                            irrep_dtype=dtype, weight_dtype=dtype)
+    op = _oracle(p)
+    perm = O.oeq_permutation(op)
+    rng = np.random.default_rng(100 + rows)
+    X = rng.normal(size=(rows, p.irreps_in1.dim))
+    Y = rng.normal(size=(rows, p.irreps_in2.dim))
+    W = rng.normal(size=(p.weight_numel,)) / np.sqrt(32 * 5)
+    G = rng.normal(size=(rows, p.irreps_out.dim))
+    tp = oeq.TensorProduct(p)
+    x = to_dev(X, dtype).requires_grad_()
+    y = to_dev(Y, dtype).requires_grad_()
+    w = to_dev(W[perm], dtype).requires_grad_()
+    names = _kernel_names(lambda: tp(x, y, w).backward(to_dev(G, dtype)))
+    assert any("tp_uvw_sw_dxy" in n for n in names) and any("tp_uvw_sw_dw" in n for n in names)
+    gX, gY, gW = O.backward(op, X, Y, W, G)
+    for got, want, what in ((x.grad, gX, "dX"), (y.grad, gY, "dY"), (w.grad, gW[perm], "dW")):
+        e = nerr(got, want)
+        assert e <= TOL[dtype], f"{what}: normalised max error {e:.3e}"
