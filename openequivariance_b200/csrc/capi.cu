@@ -125,9 +125,12 @@ struct oeqb_plan {
     int nch = 0, rb = 0, nslots = 0, offY = 0, xy_elems = 0, slot_elems = 0, slot_w_off = 0;
     size_t smem = 0;
   } lk;
-  // Edge-per-lane convolution (tp_kernels_edge.cuh) for multiplicity-1 problems.
+  // Edge-per-lane convolution (tp_kernels_edge.cuh) for multiplicity-1 problems; edge1 = the
+  // single-path variant (one instruction whose irreps are the whole rows).
   bool edge_ok = false;
   EdgeLayout edge{};
+  bool edge1_ok = false;
+  Edge1 edge1{};
   // Tensor-core shared-weight uvw forward (tp_kernels_uvw_tc.cuh).
   struct TcTable {
     bool ok = false;
@@ -522,6 +525,9 @@ void build_edge(oeqb_plan& p) {
                       edge_pad(std::max(1, p.wnumel))};
   const size_t elem = p.dtype == 2 ? 8 : 4;
   p.edge_ok = edge_warp_elems(p.edge, true) * elem <= 12 * 1024;
+  p.edge1_ok = p.edge_ok && p.ins_f.size() == 1 && p.n1 == 1 && p.n2 == 1 && p.n3 == 1 &&
+               p.ir1[0].off == 0 && p.ir2[0].off == 0 && p.ir3[0].off == 0;
+  if (p.edge1_ok) p.edge1 = Edge1{p.ins_f[0].code, p.ins_f[0].woff, p.ins_f[0].pw};
 }
 
 // Shared-weight float32 uvw problems of the NequIP shape run on the tensor cores: every
@@ -1281,6 +1287,33 @@ int launch_uvw_sw(oeqb_plan& p, const Args<T>& a, cudaStream_t stream) {
   return 0;
 }
 
+template <class T>
+int launch_edge1(oeqb_plan& p, int kind, const Args<T>& a, cudaStream_t stream) {
+  if (a.nitems <= 0) return 0;
+  const void* kernel = edge_kernel_ptr<T>(kind == 0 ? 2 : 3);
+  int per_sm;
+  {
+    std::lock_guard<std::mutex> g(p.mu);
+    auto it = p.occ.find(kernel);
+    if (it == p.occ.end()) {
+      int n = 0;
+      OEQB_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kernel, kEdgeWarps * 32, 0));
+      if (n <= 0) return fail(OEQB_ERR_UNSUPPORTED, "edge convolution kernel does not fit");
+      it = p.occ.emplace(kernel, n).first;
+    }
+    per_sm = it->second;
+  }
+  const long long warps = (a.nitems + 31) / 32;
+  long long blocks = std::min<long long>((warps + kEdgeWarps - 1) / kEdgeWarps,
+                                         (long long)p.sm_count * per_sm);
+  blocks = std::max<long long>(1, blocks);
+  Edge1 e = p.edge1;
+  void* params[] = {const_cast<Args<T>*>(&a), &e};
+  OEQB_CUDA(cudaLaunchKernel(kernel, dim3(static_cast<unsigned>(blocks)), dim3(kEdgeWarps * 32),
+                             params, 0, stream));
+  return 0;
+}
+
 struct DeviceGuard {
   int prev = -1;
   explicit DeviceGuard(int dev) {
@@ -1385,6 +1418,7 @@ int conv_fwd_t(oeqb_plan* p, bool db, const void* X, const void* Y, const void* 
   a.cols = reinterpret_cast<const long long*>(cols);
   if (p->det)
     return launch(*p, det_kernel_ptr<T>(0, p->uvw, db, p->kahan), a, true, true, s);
+  if (!db && p->edge1_ok) return launch_edge1(*p, 0, a, s);
   if (!db && p->edge_ok) return launch_edge(*p, 0, a, s);
   return launch(*p, batch_kernel_ptr<T>(0, p->uvw, db, kConvAtomic), a, true, false, s);
 }
@@ -1417,6 +1451,7 @@ int conv_bwd_t(oeqb_plan* p, bool db, const void* X, const void* Y, const void* 
     if (!perm) return fail(OEQB_ERR_INVALID, "deterministic convolution needs transpose_perm");
     return launch(*p, det_kernel_ptr<T>(1, p->uvw, db, p->kahan), a, false, true, s);
   }
+  if (!db && p->edge1_ok) return launch_edge1(*p, 1, a, s);
   if (!db && p->edge_ok) return launch_edge(*p, 1, a, s);
   return launch(*p, batch_kernel_ptr<T>(1, p->uvw, db, kConvAtomic), a, false, false, s);
 }

@@ -24,7 +24,8 @@ template <class T>
 const void* seg_kernel_ptr(int kind);
 template <class T>
 const void* lk_kernel_ptr();
-// Edge-per-lane convolution for multiplicity-1 problems (tp_kernels_edge.cuh).
+// Edge-per-lane convolution for multiplicity-1 problems (tp_kernels_edge.cuh); kind 0/1 =
+// forward/backward, 2/3 = the single-path variants.
 template <class T>
 const void* edge_kernel_ptr(int kind);
 
@@ -58,7 +59,10 @@ const void* edge_kernel_ptr(int kind);
   const void* lk_kernel_ptr<T>() { return (const void*)tp_bwd_lk<T>; }            \
   template <>                                                                     \
   const void* edge_kernel_ptr<T>(int kind) {                                      \
-    return kind == 0 ? (const void*)conv_fwd_edge<T> : (const void*)conv_bwd_edge<T>; \
+    return kind == 0   ? (const void*)conv_fwd_edge<T>                           \
+           : kind == 1 ? (const void*)conv_bwd_edge<T>                           \
+           : kind == 2 ? (const void*)conv_fwd_edge1<T>                          \
+                       : (const void*)conv_bwd_edge1<T>;                         \
   }
 
 #define OEQB_DEFINE_DET_TABLE(T, WITH_KAHAN)                                    \

@@ -149,9 +149,14 @@ def test_shared_weights_atomic(cuda_device):
     conv = oeq.TensorProductConv(p, deterministic=False)
     op = O.make_problem("1x2e", "1x3e", "1x2e", [(0, 0, 0, "uvu", True)], shared_weights=True)
     W = np.array([0.7])
-    Z = conv(to_dev(g["X"], np.float64), to_dev(g["Y"], np.float64), to_dev(W, np.float64),
-             _idx(g["rows"]), _idx(g["cols"]))
+    x, y, w = (to_dev(t, np.float64).requires_grad_() for t in (g["X"], g["Y"], W))
+    Z = conv(x, y, w, _idx(g["rows"]), _idx(g["cols"]))
     assert nerr(Z, O.conv_forward(op, g["X"], g["Y"], W, g["rows"], g["cols"])) <= 1e-12
+    Z.backward(to_dev(g["G"], np.float64))
+    gX, gY, gW = O.conv_backward(op, g["X"], g["Y"], W, g["G"], g["rows"], g["cols"])
+    assert nerr(x.grad, gX) <= 1e-12
+    assert nerr(y.grad, gY) <= 1e-12
+    assert nerr(w.grad, gW) <= 1e-12
     with pytest.raises(AssertionError, match="shared weights"):
         oeq.TensorProductConv(p, deterministic=True)
 
