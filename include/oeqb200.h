@@ -63,8 +63,11 @@ const char* oeqb_last_error(void);
 int oeqb_plan_create(const void* descriptor, size_t nbytes, int device, oeqb_plan** out);
 int oeqb_plan_destroy(oeqb_plan* plan);
 
-/* Bytes of workspace the convolution entry points need (0 for this implementation;
- * kept so callers that allocate the reference's workspace keep working). */
+/* Bytes of workspace oeqb_conv_backward needs for `nnz` edges (replaces the reference's
+ * workspace sizing, core/LoopUnrollConv.py:138-170).  Nonzero only for deterministic plans of
+ * single-path multiplicity-1 problems, whose fast backward keeps one 8-value record per edge;
+ * with a smaller workspace those plans fall back to the generic deterministic kernels.  The
+ * forward and the double backward need none. */
 size_t oeqb_conv_workspace_bytes(const oeqb_plan* plan, int64_t nnz, int64_t node_count);
 
 /* Synchronises `stream` and reports (then clears) the plan's device error flag:

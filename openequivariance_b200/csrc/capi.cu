@@ -1287,31 +1287,49 @@ int launch_uvw_sw(oeqb_plan& p, const Args<T>& a, cudaStream_t stream) {
   return 0;
 }
 
+// Single-path edge kernels (tp_kernels_edge.cuh).  kind: 2 atomic forward, 3 atomic backward,
+// 4 deterministic forward, 5 deterministic backward pass A, 6 pass B.  The deterministic
+// kernels split the edges over a fixed number of warps (the device's resident capacity), so a
+// plan on one device always sums in the same order.
 template <class T>
-int launch_edge1(oeqb_plan& p, int kind, const Args<T>& a, cudaStream_t stream) {
+int launch_edge1(oeqb_plan& p, int kind, const Args<T>& a, T* ws, cudaStream_t stream) {
   if (a.nitems <= 0) return 0;
-  const void* kernel = edge_kernel_ptr<T>(kind == 0 ? 2 : 3);
+  const void* kernel = edge_kernel_ptr<T>(kind);
+  const int d2 = 2 * ((p.edge1.code >> 4) & 15) + 1;
+  const int per_warp = kind == 2 || kind == 4 ? 32 * d2 : kind == 3 ? 64 * d2
+                       : kind == 5 ? 64 * d2 + 32 * kE1Rec : 0;
+  const size_t smem = sizeof(T) * size_t(kEdgeWarps) * per_warp;
   int per_sm;
   {
     std::lock_guard<std::mutex> g(p.mu);
     auto it = p.occ.find(kernel);
     if (it == p.occ.end()) {
       int n = 0;
-      OEQB_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kernel, kEdgeWarps * 32, 0));
+      OEQB_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kernel, kEdgeWarps * 32, smem));
       if (n <= 0) return fail(OEQB_ERR_UNSUPPORTED, "edge convolution kernel does not fit");
       it = p.occ.emplace(kernel, n).first;
     }
     per_sm = it->second;
   }
-  const long long warps = (a.nitems + 31) / 32;
-  long long blocks = std::min<long long>((warps + kEdgeWarps - 1) / kEdgeWarps,
-                                         (long long)p.sm_count * per_sm);
-  blocks = std::max<long long>(1, blocks);
+  const long long cap = (long long)p.sm_count * per_sm;
+  long long blocks;
+  if (kind == 4 || kind == 6) {
+    blocks = cap;  // fixed partition (deterministic summation order)
+  } else {
+    const long long warps = (a.nitems + 31) / 32;
+    blocks = std::max<long long>(1, std::min<long long>((warps + kEdgeWarps - 1) / kEdgeWarps, cap));
+  }
   Edge1 e = p.edge1;
-  void* params[] = {const_cast<Args<T>*>(&a), &e};
+  void* params[] = {const_cast<Args<T>*>(&a), &e, &ws};
   OEQB_CUDA(cudaLaunchKernel(kernel, dim3(static_cast<unsigned>(blocks)), dim3(kEdgeWarps * 32),
-                             params, 0, stream));
+                             params, smem, stream));
   return 0;
+}
+
+// Workspace of the single-path deterministic backward: one record per edge.
+size_t edge1_det_ws_bytes(const oeqb_plan& p, int64_t nnz) {
+  if (!(p.edge1_ok && p.det && !p.kahan) || nnz <= 0) return 0;
+  return size_t(nnz) * kE1Rec * p.elem();
 }
 
 struct DeviceGuard {
@@ -1416,9 +1434,12 @@ int conv_fwd_t(oeqb_plan* p, bool db, const void* X, const void* Y, const void* 
   a.out0 = static_cast<T*>(Z);
   a.rows = reinterpret_cast<const long long*>(rows);
   a.cols = reinterpret_cast<const long long*>(cols);
-  if (p->det)
+  if (p->det) {
+    if (!db && p->edge1_ok && !p->kahan && aligned16(Y))
+      return launch_edge1<T>(*p, 4, a, nullptr, s);
     return launch(*p, det_kernel_ptr<T>(0, p->uvw, db, p->kahan), a, true, true, s);
-  if (!db && p->edge1_ok) return launch_edge1(*p, 0, a, s);
+  }
+  if (!db && p->edge1_ok && aligned16(Y)) return launch_edge1<T>(*p, 2, a, nullptr, s);
   if (!db && p->edge_ok) return launch_edge(*p, 0, a, s);
   return launch(*p, batch_kernel_ptr<T>(0, p->uvw, db, kConvAtomic), a, true, false, s);
 }
@@ -1427,9 +1448,8 @@ template <class T>
 int conv_bwd_t(oeqb_plan* p, bool db, const void* X, const void* Y, const void* W, const void* dZ,
                const void* ddX, const void* ddY, const void* ddW, void* gX, void* gY, void* gW,
                const int64_t* rows, const int64_t* cols, const int64_t* perm, int64_t nnz,
-               int64_t nodes, cudaStream_t s) {
+               int64_t nodes, void* ws, size_t ws_bytes, cudaStream_t s) {
   OEQB_CUDA(cudaMemsetAsync(gX, 0, sizeof(T) * size_t(nodes) * p->L1dim, s));
-  if (p->det) OEQB_CUDA(cudaMemsetAsync(gY, 0, sizeof(T) * size_t(nnz) * p->L2dim, s));
   if (p->shared_w) OEQB_CUDA(cudaMemsetAsync(gW, 0, sizeof(T) * p->wnumel, s));
   Args<T> a = base_args<T>(*p, false);
   a.nitems = nnz;
@@ -1449,9 +1469,16 @@ int conv_bwd_t(oeqb_plan* p, bool db, const void* X, const void* Y, const void* 
   a.perm = reinterpret_cast<const long long*>(perm);
   if (p->det) {
     if (!perm) return fail(OEQB_ERR_INVALID, "deterministic convolution needs transpose_perm");
+    const size_t need = edge1_det_ws_bytes(*p, nnz);
+    if (!db && need && ws && ws_bytes >= need && aligned16(ws) && aligned16(Y) && aligned16(gY)) {
+      if (int rc = launch_edge1<T>(*p, 5, a, static_cast<T*>(ws), s)) return rc;
+      return launch_edge1<T>(*p, 6, a, static_cast<T*>(ws), s);
+    }
+    OEQB_CUDA(cudaMemsetAsync(gY, 0, sizeof(T) * size_t(nnz) * p->L2dim, s));
     return launch(*p, det_kernel_ptr<T>(1, p->uvw, db, p->kahan), a, false, true, s);
   }
-  if (!db && p->edge1_ok) return launch_edge1(*p, 1, a, s);
+  if (!db && p->edge1_ok && aligned16(Y) && aligned16(gY))
+    return launch_edge1<T>(*p, 3, a, nullptr, s);
   if (!db && p->edge_ok) return launch_edge(*p, 1, a, s);
   return launch(*p, batch_kernel_ptr<T>(1, p->uvw, db, kConvAtomic), a, false, false, s);
 }
@@ -1532,10 +1559,8 @@ int oeqb_plan_destroy(oeqb_plan* p) {
 }
 
 size_t oeqb_conv_workspace_bytes(const oeqb_plan* p, int64_t nnz, int64_t node_count) {
-  (void)p;
-  (void)nnz;
   (void)node_count;
-  return 0;
+  return p ? edge1_det_ws_bytes(*p, nnz) : 0;
 }
 
 int oeqb_plan_check_status(oeqb_plan* p, int* status, void* stream) {
@@ -1609,8 +1634,6 @@ int oeqb_conv_backward(oeqb_plan* p, const void* L1_in, void* L1_grad, const voi
                        const int64_t* rows, const int64_t* cols, int64_t nnz, int64_t node_count,
                        void* workspace, size_t workspace_bytes, const int64_t* transpose_perm,
                        void* stream) {
-  (void)workspace;
-  (void)workspace_bytes;
   if (nnz < 0 || node_count < 0) return fail(OEQB_ERR_INVALID, "negative size");
   if (int rc = check_plan(p)) return rc;
   DeviceGuard g(p->device);
@@ -1618,10 +1641,10 @@ int oeqb_conv_backward(oeqb_plan* p, const void* L1_in, void* L1_grad, const voi
   return p->dtype == 1
              ? conv_bwd_t<float>(p, false, L1_in, L2_in, W, L3_grad, nullptr, nullptr, nullptr,
                                  L1_grad, L2_grad, W_grad, rows, cols, transpose_perm, nnz,
-                                 node_count, s)
+                                 node_count, workspace, workspace_bytes, s)
              : conv_bwd_t<double>(p, false, L1_in, L2_in, W, L3_grad, nullptr, nullptr, nullptr,
                                   L1_grad, L2_grad, W_grad, rows, cols, transpose_perm, nnz,
-                                  node_count, s);
+                                  node_count, workspace, workspace_bytes, s);
 }
 
 int oeqb_conv_double_backward(oeqb_plan* p, const void* L1_in, const void* L2_in, const void* W,
@@ -1631,7 +1654,7 @@ int oeqb_conv_double_backward(oeqb_plan* p, const void* L1_in, const void* L2_in
                               int64_t nnz, int64_t node_count, void* workspace,
                               size_t workspace_bytes, const int64_t* transpose_perm,
                               void* stream) {
-  (void)workspace;
+  (void)workspace;  // the double backward runs the generic kernels, which need none
   (void)workspace_bytes;
   if (nnz < 0 || node_count < 0) return fail(OEQB_ERR_INVALID, "negative size");
   if (int rc = check_plan(p)) return rc;
@@ -1643,14 +1666,14 @@ int oeqb_conv_double_backward(oeqb_plan* p, const void* L1_in, const void* L2_in
       return rc;
     return conv_bwd_t<float>(p, true, L1_in, L2_in, W, L3_grad, L1_dgrad, L2_dgrad, W_dgrad,
                              L1_grad, L2_grad, W_grad, rows, cols, transpose_perm, nnz, node_count,
-                             s);
+                             nullptr, 0, s);
   }
   if (int rc = conv_fwd_t<double>(p, true, L1_in, L2_in, W, L1_dgrad, L2_dgrad, W_dgrad, L3_dgrad,
                                   rows, cols, nnz, node_count, s))
     return rc;
   return conv_bwd_t<double>(p, true, L1_in, L2_in, W, L3_grad, L1_dgrad, L2_dgrad, W_dgrad,
                             L1_grad, L2_grad, W_grad, rows, cols, transpose_perm, nnz, node_count,
-                            s);
+                            nullptr, 0, s);
 }
 
 int oeqb_tp_forward_noalloc(const void* descriptor, size_t nbytes, int device, int64_t batch,

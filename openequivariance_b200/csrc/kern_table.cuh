@@ -25,7 +25,8 @@ const void* seg_kernel_ptr(int kind);
 template <class T>
 const void* lk_kernel_ptr();
 // Edge-per-lane convolution for multiplicity-1 problems (tp_kernels_edge.cuh); kind 0/1 =
-// forward/backward, 2/3 = the single-path variants.
+// forward/backward, 2/3 = the single-path variants, 4/5/6 = single-path deterministic
+// forward, backward pass A (messages to the workspace) and pass B (sender-ordered sums).
 template <class T>
 const void* edge_kernel_ptr(int kind);
 
@@ -59,10 +60,15 @@ const void* edge_kernel_ptr(int kind);
   const void* lk_kernel_ptr<T>() { return (const void*)tp_bwd_lk<T>; }            \
   template <>                                                                     \
   const void* edge_kernel_ptr<T>(int kind) {                                      \
-    return kind == 0   ? (const void*)conv_fwd_edge<T>                           \
-           : kind == 1 ? (const void*)conv_bwd_edge<T>                           \
-           : kind == 2 ? (const void*)conv_fwd_edge1<T>                          \
-                       : (const void*)conv_bwd_edge1<T>;                         \
+    switch (kind) {                                                               \
+      case 0: return (const void*)conv_fwd_edge<T>;                               \
+      case 1: return (const void*)conv_bwd_edge<T>;                               \
+      case 2: return (const void*)conv_fwd_edge1<T>;                              \
+      case 3: return (const void*)conv_bwd_edge1<T>;                              \
+      case 4: return (const void*)conv_fwd_edge1_det<T>;                          \
+      case 5: return (const void*)conv_bwd_edge1_msg<T>;                          \
+      default: return (const void*)conv_bwd_edge1_gather<T>;                      \
+    }                                                                             \
   }
 
 #define OEQB_DEFINE_DET_TABLE(T, WITH_KAHAN)                                    \

@@ -230,10 +230,16 @@ std::tuple<Tensor, Tensor, Tensor> jit_conv_backward(Tensor json_bytes, int64_t 
   Tensor x = L1_in.contiguous(), y = L2_in.contiguous(), w = W.contiguous(),
          gz = L3_grad.contiguous(), r = rows.contiguous(), cl = cols.contiguous();
   Tensor tp = k.deterministic ? transpose_perm.contiguous() : Tensor();
+  // The single-path deterministic backward keeps one record per edge in the workspace; a
+  // module's buffer that is too small is replaced for this call (torch's caching allocator).
+  Tensor ws = workspace;
+  const size_t need = oeqb_conv_workspace_bytes(k.plan, c.nnz, c.nodes);
+  if (need > static_cast<size_t>(workspace.numel()))
+    ws = at::empty({static_cast<int64_t>(need)}, workspace.options());
   check_rc(oeqb_conv_backward(
       k.plan, x.data_ptr(), L1_grad.data_ptr(), y.data_ptr(), L2_grad.data_ptr(), w.data_ptr(),
       W_grad.data_ptr(), gz.data_ptr(), r.data_ptr<int64_t>(), cl.data_ptr<int64_t>(), c.nnz,
-      c.nodes, workspace.data_ptr(), static_cast<size_t>(workspace.numel()),
+      c.nodes, ws.data_ptr(), static_cast<size_t>(ws.numel()),
       k.deterministic ? tp.data_ptr<int64_t>() : nullptr, stream_of(L1_in)));
   return {L1_grad, L2_grad, W_grad};
 }

@@ -278,77 +278,208 @@ struct Edge1 {
   double pw;
 };
 
+// Row r (0..31) of a warp's D consecutive-row block, staged in shared memory at r * D.
+// Global rows [base, base + 32) of width D start at base * D: 16-byte aligned when base is a
+// multiple of 32 and the tensor is (float) / when D is even or base a multiple of 32 (double),
+// so the block moves with 16-byte copies; the tail of the last block goes element-wise.
+template <class T, int D>
+__device__ __forceinline__ void e1_stage_in(T* dst, const T* src, long long base, long long n,
+                                            int lane) {
+  const long long rows = n - base < 32 ? n - base : 32;
+  const int total = static_cast<int>(rows) * D;
+  const T* g = src + base * D;
+  constexpr int V = 16 / sizeof(T);
+  const int nv = total / V;
+  for (int q = lane; q < nv; q += 32) {
+    if constexpr (sizeof(T) == 4) {
+      const float4 t = __ldg(reinterpret_cast<const float4*>(g) + q);
+      dst[4 * q] = t.x;
+      dst[4 * q + 1] = t.y;
+      dst[4 * q + 2] = t.z;
+      dst[4 * q + 3] = t.w;
+    } else {
+      const double2 t = __ldg(reinterpret_cast<const double2*>(g) + q);
+      dst[2 * q] = t.x;
+      dst[2 * q + 1] = t.y;
+    }
+  }
+  for (int e = nv * V + lane; e < total; e += 32) dst[e] = g[e];
+}
+
+template <class T, int D>
+__device__ __forceinline__ void e1_stage_out(T* dst, const T* src, long long base, long long n,
+                                             int lane) {
+  const long long rows = n - base < 32 ? n - base : 32;
+  const int total = static_cast<int>(rows) * D;
+  T* g = dst + base * D;
+  constexpr int V = 16 / sizeof(T);
+  const int nv = total / V;
+  for (int q = lane; q < nv; q += 32) {
+    if constexpr (sizeof(T) == 4)
+      reinterpret_cast<float4*>(g)[q] =
+          make_float4(src[4 * q], src[4 * q + 1], src[4 * q + 2], src[4 * q + 3]);
+    else
+      reinterpret_cast<double2*>(g)[q] = make_double2(src[2 * q], src[2 * q + 1]);
+  }
+  for (int e = nv * V + lane; e < total; e += 32) g[e] = src[e];
+}
+
+// Gathers row `node` (D values) of a [nodes, D] tensor: 16-byte loads of the aligned window
+// that contains it (all D values in (D + 6) / 4 loads), element-wise where the window would
+// pass the end of the tensor.
+template <class T, int D>
+__device__ __forceinline__ void e1_gather(T (&v)[D], const T* src, long long node, long long nodes) {
+  if constexpr (sizeof(T) == 4) {
+    constexpr int NW = (D + 6) / 4;
+    const long long f = node * D;
+    const int o = static_cast<int>(f & 3);
+    const long long b4 = f - o;
+    if (b4 + 4 * NW <= nodes * D) {
+      float w[4 * NW];
+#pragma unroll
+      for (int q = 0; q < NW; ++q) {
+        const float4 t = __ldg(reinterpret_cast<const float4*>(src + b4) + q);
+        w[4 * q] = t.x;
+        w[4 * q + 1] = t.y;
+        w[4 * q + 2] = t.z;
+        w[4 * q + 3] = t.w;
+      }
+      switch (o) {
+        case 0:
+#pragma unroll
+          for (int i = 0; i < D; ++i) v[i] = w[i];
+          break;
+        case 1:
+#pragma unroll
+          for (int i = 0; i < D; ++i) v[i] = w[i + 1];
+          break;
+        case 2:
+#pragma unroll
+          for (int i = 0; i < D; ++i) v[i] = w[i + 2];
+          break;
+        default:
+#pragma unroll
+          for (int i = 0; i < D; ++i) v[i] = w[i + 3];
+          break;
+      }
+      return;
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < D; ++i) v[i] = src[node * D + i];
+}
+
+// Per-lane edge record of one 32-edge block: receiver, sender, validity (bounds-checked).
+struct E1Lane {
+  long long e, row, col;
+  bool valid;
+};
+
+template <class T>
+__device__ __forceinline__ E1Lane e1_lane(const Args<T>& a, long long base, int lane) {
+  E1Lane l;
+  l.e = base + lane;
+  l.valid = l.e < a.nitems;
+  l.row = l.valid ? a.rows[l.e] : -1;
+  l.col = l.valid ? a.cols[l.e] : 0;
+  if (l.valid && (l.row < 0 || l.row >= a.nnodes || l.col < 0 || l.col >= a.nnodes)) {
+    flag(a.status, 1);
+    l.valid = false;
+    l.row = -1;
+    l.col = 0;
+  }
+  return l;
+}
+
+// Forward message of one lane: z = w pw CG(x[col], y[e]).
 template <class T, int A, int B, int C>
-__device__ __forceinline__ void edge1_fwd_chunk(const Args<T>& a, const Edge1& p, long long e,
-                                                bool valid, long long row, long long col,
-                                                int lane) {
+__device__ __forceinline__ void e1_message(const Args<T>& a, const Edge1& p, const E1Lane& l,
+                                           const T* ys, int lane, T (&z)[2 * C + 1]) {
   constexpr int D1 = 2 * A + 1, D2 = 2 * B + 1, D3 = 2 * C + 1;
-  T z[D3];
 #pragma unroll
   for (int k = 0; k < D3; ++k) z[k] = T(0);
-  if (valid) {
-    const T w = (a.shared_w ? a.W[p.woff] : a.W[e * a.wnumel + p.woff]) * T(p.pw);
+  if (l.valid) {
+    const T w = (a.shared_w ? a.W[p.woff] : a.W[l.e * a.wnumel + p.woff]) * T(p.pw);
     T x[D1], y[D2];
+    e1_gather<T, D1>(x, a.X, l.col, a.nnodes);
 #pragma unroll
-    for (int i = 0; i < D1; ++i) x[i] = a.X[col * D1 + i] * w;
+    for (int i = 0; i < D1; ++i) x[i] *= w;
 #pragma unroll
-    for (int j = 0; j < D2; ++j) y[j] = a.Y[e * D2 + j];
+    for (int j = 0; j < D2; ++j) y[j] = ys[lane * D2 + j];
     CG<A, B, C>::fwd(x, y, z);
   }
-  // Segmented suffix sums over equal receivers (rows are sorted), one reduction per segment.
-  const int r32 = static_cast<int>(row);
-  const int prev = __shfl_up_sync(0xffffffffu, r32, 1);
-  const bool head = row >= 0 && (lane == 0 || prev != r32);
+}
+
+// Suffix sums over runs of equal keys (keys sorted within the warp): afterwards the first lane
+// of each run holds the run's sum.  The tree is fixed, so the result is deterministic.
+template <class T, int D>
+__device__ __forceinline__ void e1_seg_sum(T (&z)[D], int key, int lane) {
 #pragma unroll
   for (int off = 1; off < 32; off <<= 1) {
-    const int ro = __shfl_down_sync(0xffffffffu, r32, off);
-    const bool take = lane + off < 32 && ro == r32;
+    const int ko = __shfl_down_sync(0xffffffffu, key, off);
+    const bool take = lane + off < 32 && ko == key;
 #pragma unroll
-    for (int k = 0; k < D3; ++k) {
+    for (int k = 0; k < D; ++k) {
       const T vo = __shfl_down_sync(0xffffffffu, z[k], off);
       if (take) z[k] += vo;
     }
   }
-  if (head) red_vec(a.out0 + row * D3, z);
 }
 
 template <class T>
-__global__ void __launch_bounds__(kEdgeWarps * 32) conv_fwd_edge1(const Args<T> a, const Edge1 p) {
-  const int lane = threadIdx.x & 31;
-  const long long nw = static_cast<long long>(gridDim.x) * kEdgeWarps;
-  for (long long base = (static_cast<long long>(blockIdx.x) * kEdgeWarps + (threadIdx.x >> 5)) * 32;
-       base < a.nitems; base += nw * 32) {
-    const long long e = base + lane;
-    bool valid = e < a.nitems;
-    long long row = valid ? a.rows[e] : -1, col = valid ? a.cols[e] : 0;
-    if (valid && (row < 0 || row >= a.nnodes || col < 0 || col >= a.nnodes)) {
-      flag(a.status, 1);
-      valid = false;
-      row = -1;
-      col = 0;
-    }
-    dispatch_triple(p.code, [&]<int A, int B, int C>() {
-      edge1_fwd_chunk<T, A, B, C>(a, p, e, valid, row, col, lane);
-    });
-  }
+__device__ __forceinline__ T* e1_warp_smem(unsigned char* smem, int elems) {
+  return reinterpret_cast<T*>(smem) + static_cast<size_t>(threadIdx.x >> 5) * elems;
 }
 
+// ----------------------------------------------------------------------- atomic mode
+
+template <class T>
+__global__ void __launch_bounds__(kEdgeWarps * 32) conv_fwd_edge1(const Args<T> a, const Edge1 p) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  const int lane = threadIdx.x & 31;
+  const long long nw = static_cast<long long>(gridDim.x) * kEdgeWarps;
+  dispatch_triple(p.code, [&]<int A, int B, int C>() {
+    constexpr int D2 = 2 * B + 1, D3 = 2 * C + 1;
+    T* ys = e1_warp_smem<T>(smem, 32 * D2);
+    for (long long base = (static_cast<long long>(blockIdx.x) * kEdgeWarps + (threadIdx.x >> 5)) * 32;
+         base < a.nitems; base += nw * 32) {
+      const E1Lane l = e1_lane(a, base, lane);
+      e1_stage_in<T, D2>(ys, a.Y, base, a.nitems, lane);
+      __syncwarp();
+      T z[D3];
+      e1_message<T, A, B, C>(a, p, l, ys, lane, z);
+      __syncwarp();
+      const int r32 = static_cast<int>(l.row);
+      const int prev = __shfl_up_sync(0xffffffffu, r32, 1);
+      const bool head = l.row >= 0 && (lane == 0 || prev != r32);
+      e1_seg_sum<T, D3>(z, r32, lane);
+      if (head) red_vec(a.out0 + l.row * D3, z);
+    }
+  });
+}
+
+// Backward pieces of one lane: h (message to the sender, weight applied), dY (in ys_out),
+// sdot = dW of the edge.
 template <class T, int A, int B, int C>
-__device__ __forceinline__ void edge1_bwd_chunk(const Args<T>& a, const Edge1& p, long long e,
-                                                bool valid, long long row, long long col,
-                                                int lane) {
+__device__ __forceinline__ T e1_backward(const Args<T>& a, const Edge1& p, const E1Lane& l,
+                                         const T* ys, T* ys_out, int lane, T (&h)[2 * A + 1]) {
   constexpr int D1 = 2 * A + 1, D2 = 2 * B + 1, D3 = 2 * C + 1;
   T sdot = T(0);
-  if (valid) {
-    const T w = a.shared_w ? a.W[p.woff] : a.W[e * a.wnumel + p.woff];
+  T ev[D2];
+#pragma unroll
+  for (int i = 0; i < D1; ++i) h[i] = T(0);
+#pragma unroll
+  for (int j = 0; j < D2; ++j) ev[j] = T(0);
+  if (l.valid) {
+    const T w = a.shared_w ? a.W[p.woff] : a.W[l.e * a.wnumel + p.woff];
     const T pw = T(p.pw);
-    T x[D1], y[D2], g[D3], h[D1], ev[D2];
+    T x[D1], y[D2], g[D3];
+    e1_gather<T, D1>(x, a.X, l.col, a.nnodes);
+    e1_gather<T, D3>(g, a.Gz, l.row, a.nnodes);
 #pragma unroll
-    for (int i = 0; i < D1; ++i) x[i] = a.X[col * D1 + i];
+    for (int k = 0; k < D3; ++k) g[k] *= pw;
 #pragma unroll
-    for (int j = 0; j < D2; ++j) y[j] = a.Y[e * D2 + j];
-#pragma unroll
-    for (int k = 0; k < D3; ++k) g[k] = a.Gz[row * D3 + k] * pw;
+    for (int j = 0; j < D2; ++j) y[j] = ys[lane * D2 + j];
     CG<A, B, C>::hvec(g, y, h);
     CG<A, B, C>::evec(g, x, ev);
 #pragma unroll
@@ -357,36 +488,257 @@ __device__ __forceinline__ void edge1_bwd_chunk(const Args<T>& a, const Edge1& p
       h[i] *= w;
     }
 #pragma unroll
-    for (int j = 0; j < D2; ++j) a.out1[e * D2 + j] = w * ev[j];
-    if (!a.shared_w) a.out2[e * a.wnumel + p.woff] = sdot;
-    red_vec(a.out0 + col * D1, h);
+    for (int j = 0; j < D2; ++j) ev[j] *= w;
   }
+#pragma unroll
+  for (int j = 0; j < D2; ++j) ys_out[lane * D2 + j] = ev[j];
+  return sdot;
+}
+
+template <class T>
+__device__ __forceinline__ void e1_write_dw(const Args<T>& a, const Edge1& p, const E1Lane& l,
+                                            T sdot, int lane) {
   if (a.shared_w) {
-    T s = sdot;
+    T s = l.valid ? sdot : T(0);
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
     if (lane == 0) atomic_add(a.out2 + p.woff, s);
+  } else if (l.valid) {
+    a.out2[l.e * a.wnumel + p.woff] = sdot;
   }
 }
 
 template <class T>
 __global__ void __launch_bounds__(kEdgeWarps * 32) conv_bwd_edge1(const Args<T> a, const Edge1 p) {
+  extern __shared__ __align__(16) unsigned char smem[];
   const int lane = threadIdx.x & 31;
   const long long nw = static_cast<long long>(gridDim.x) * kEdgeWarps;
-  for (long long base = (static_cast<long long>(blockIdx.x) * kEdgeWarps + (threadIdx.x >> 5)) * 32;
-       base < a.nitems; base += nw * 32) {
-    const long long e = base + lane;
-    bool valid = e < a.nitems;
-    long long row = valid ? a.rows[e] : 0, col = valid ? a.cols[e] : 0;
-    if (valid && (row < 0 || row >= a.nnodes || col < 0 || col >= a.nnodes)) {
-      flag(a.status, 1);
-      valid = false;
-      row = col = 0;
+  dispatch_triple(p.code, [&]<int A, int B, int C>() {
+    constexpr int D1 = 2 * A + 1, D2 = 2 * B + 1;
+    T* ys = e1_warp_smem<T>(smem, 64 * D2);
+    T* yo = ys + 32 * D2;
+    for (long long base = (static_cast<long long>(blockIdx.x) * kEdgeWarps + (threadIdx.x >> 5)) * 32;
+         base < a.nitems; base += nw * 32) {
+      const E1Lane l = e1_lane(a, base, lane);
+      e1_stage_in<T, D2>(ys, a.Y, base, a.nitems, lane);
+      __syncwarp();
+      T h[D1];
+      const T sdot = e1_backward<T, A, B, C>(a, p, l, ys, yo, lane, h);
+      __syncwarp();
+      e1_stage_out<T, D2>(a.out1, yo, base, a.nitems, lane);
+      e1_write_dw(a, p, l, sdot, lane);
+      if (l.valid) red_vec(a.out0 + l.col * D1, h);
+      __syncwarp();
     }
-    dispatch_triple(p.code, [&]<int A, int B, int C>() {
-      edge1_bwd_chunk<T, A, B, C>(a, p, e, valid, row, col, lane);
-    });
+  });
+}
+
+// ----------------------------------------------------------------------- deterministic mode
+//
+// Forward: warp w owns the edges of whole receivers: its nominal range [w E / W, (w+1) E / W)
+// moved forward to receiver boundaries.  It walks the range in 32-edge blocks; the sums of
+// receivers that continue into the next block are carried in registers (carry + block sum, a
+// fixed order), and every receiver row is written once with plain stores.
+//
+// Backward, two passes.  Pass A (receiver order, coalesced) writes dY, dW and each edge's
+// message to its sender, h_e (D1 values) plus the sender index, into the workspace.  Pass B
+// walks the sender-sorted positions t, reads h of edge transpose_perm[t] and sums runs of
+// equal senders the same way as the forward, one plain store per sender row.
+
+// First position >= p whose key differs from its predecessor's (or n).
+template <class F>
+__device__ __forceinline__ long long e1_snap(long long p, long long n, F&& key, int lane) {
+  if (p <= 0) return 0;
+  if (p >= n) return n;
+  long long kp = key(p - 1);
+  for (long long q = p; q < n; q += 32) {
+    const long long t = q + lane;
+    const bool brk = t < n && key(t) != kp;
+    const unsigned m = __ballot_sync(0xffffffffu, brk);
+    if (m) return q + __ffs(m) - 1;
   }
+  return n;
+}
+
+template <class T, int D>
+__device__ __forceinline__ void e1_store_row(T* dst, const T (&v)[D]) {
+#pragma unroll
+  for (int k = 0; k < D; ++k) dst[k] = v[k];
+}
+
+// Block-wise segmented sums with a carried tail segment.  key = -1 marks invalid lanes (past the
+// range end).  `more` = the range continues after this block.
+template <class T, int D>
+__device__ __forceinline__ void e1_seg_block(T (&z)[D], long long key, long long next_key,
+                                             bool more, T (&carry)[D], long long& carry_key,
+                                             T* out, int lane) {
+  const int k32 = static_cast<int>(key);
+  const int prev = __shfl_up_sync(0xffffffffu, k32, 1);
+  const bool head = key >= 0 && (lane == 0 || prev != k32);
+  e1_seg_sum<T, D>(z, k32, lane);
+  // The run holding lane 0 continues a carried run from the previous block.
+  if (lane == 0 && key >= 0 && key == carry_key) {
+#pragma unroll
+    for (int k = 0; k < D; ++k) z[k] = carry[k] + z[k];
+  }
+  // Key of the last valid lane, and whether its run goes on into the next block.
+  const unsigned vm = __ballot_sync(0xffffffffu, key >= 0);
+  const int last = vm ? 31 - __clz(vm) : -1;
+  const long long last_key = last >= 0 ? __shfl_sync(0xffffffffu, key, last) : -1;
+  const bool cont = more && last == 31 && next_key == last_key;
+  // Head lane of the last run.
+  const unsigned hm = __ballot_sync(0xffffffffu, head);
+  const int last_head = hm ? 31 - __clz(hm) : -1;
+  if (head && !(cont && lane == last_head)) e1_store_row(out + key * D, z);
+  carry_key = -2;
+  if (cont) {
+#pragma unroll
+    for (int k = 0; k < D; ++k) carry[k] = __shfl_sync(0xffffffffu, z[k], last_head);
+    carry_key = last_key;
+  }
+}
+
+template <class T>
+__global__ void __launch_bounds__(kEdgeWarps * 32) conv_fwd_edge1_det(const Args<T> a, const Edge1 p) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  const int lane = threadIdx.x & 31;
+  const long long nwarps = static_cast<long long>(gridDim.x) * kEdgeWarps;
+  const long long wg = static_cast<long long>(blockIdx.x) * kEdgeWarps + (threadIdx.x >> 5);
+  const long long n = a.nitems;
+  auto key = [&](long long e) { return a.rows[e]; };
+  const long long p0 = e1_snap(static_cast<long long>((static_cast<__int128>(n) * wg) / nwarps), n, key, lane);
+  const long long p1 = e1_snap(static_cast<long long>((static_cast<__int128>(n) * (wg + 1)) / nwarps), n, key, lane);
+  dispatch_triple(p.code, [&]<int A, int B, int C>() {
+    constexpr int D2 = 2 * B + 1, D3 = 2 * C + 1;
+    T* ys = e1_warp_smem<T>(smem, 32 * D2);
+    T carry[D3];
+    long long carry_key = -2;
+    for (long long base = p0; base < p1; base += 32) {
+      E1Lane l = e1_lane(a, base, lane);
+      if (l.e >= p1) {
+        l.valid = false;
+        l.row = -1;
+      }
+      // Rows staged from the block start (not 32-aligned here: element-wise copy).
+      const long long nb = p1 - base < 32 ? p1 - base : 32;
+      for (int q = lane; q < nb * D2; q += 32) ys[q] = a.Y[base * D2 + q];
+      __syncwarp();
+      T z[D3];
+      e1_message<T, A, B, C>(a, p, l, ys, lane, z);
+      __syncwarp();
+      const bool more = base + 32 < p1;
+      const long long nk = more ? a.rows[base + 32] : -3;
+      e1_seg_block<T, D3>(z, l.valid ? l.row : -1, nk, more, carry, carry_key, a.out0, lane);
+    }
+  });
+}
+
+// Workspace record of pass A, 8 values: h (D1 <= 7 values), and at index 7 the bits of the
+// sender index (int32 in a float slot, int64 in a double slot).  32 bytes (float): one sector,
+// 16-byte loads.
+constexpr int kE1Rec = 8;
+
+template <class T>
+__device__ __forceinline__ T e1_key_bits(long long k) {
+  if constexpr (sizeof(T) == 4)
+    return __int_as_float(static_cast<int>(k));
+  else
+    return __longlong_as_double(k);
+}
+
+template <class T>
+__device__ __forceinline__ long long e1_bits_key(T v) {
+  if constexpr (sizeof(T) == 4)
+    return __float_as_int(v);
+  else
+    return __double_as_longlong(v);
+}
+
+template <class T>
+__global__ void __launch_bounds__(kEdgeWarps * 32) conv_bwd_edge1_msg(const Args<T> a, const Edge1 p,
+                                                                      T* ws) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  const int lane = threadIdx.x & 31;
+  const long long nw = static_cast<long long>(gridDim.x) * kEdgeWarps;
+  dispatch_triple(p.code, [&]<int A, int B, int C>() {
+    constexpr int D1 = 2 * A + 1, D2 = 2 * B + 1, R = kE1Rec;
+    T* ys = e1_warp_smem<T>(smem, 64 * D2 + 32 * R);
+    T* yo = ys + 32 * D2;
+    T* hs = yo + 32 * D2;
+    for (long long base = (static_cast<long long>(blockIdx.x) * kEdgeWarps + (threadIdx.x >> 5)) * 32;
+         base < a.nitems; base += nw * 32) {
+      const E1Lane l = e1_lane(a, base, lane);
+      e1_stage_in<T, D2>(ys, a.Y, base, a.nitems, lane);
+      __syncwarp();
+      T h[D1];
+      const T sdot = e1_backward<T, A, B, C>(a, p, l, ys, yo, lane, h);
+#pragma unroll
+      for (int i = 0; i < R - 1; ++i) hs[lane * R + i] = i < D1 ? h[i] : T(0);
+      hs[lane * R + R - 1] = e1_key_bits<T>(l.valid ? l.col : -1);
+      __syncwarp();
+      e1_stage_out<T, D2>(a.out1, yo, base, a.nitems, lane);
+      e1_stage_out<T, R>(ws, hs, base, a.nitems, lane);
+      e1_write_dw(a, p, l, sdot, lane);
+      __syncwarp();
+    }
+  });
+}
+
+template <class T>
+__global__ void __launch_bounds__(kEdgeWarps * 32) conv_bwd_edge1_gather(const Args<T> a,
+                                                                         const Edge1 p, const T* ws) {
+  const int lane = threadIdx.x & 31;
+  const long long nwarps = static_cast<long long>(gridDim.x) * kEdgeWarps;
+  const long long wg = static_cast<long long>(blockIdx.x) * kEdgeWarps + (threadIdx.x >> 5);
+  const long long n = a.nitems;
+  dispatch_l(p.code >> 8, [&]<int A>() {
+    constexpr int D1 = 2 * A + 1, R = kE1Rec;
+    // Sender of sender-sorted position t (the permutation is range-checked).
+    auto sender = [&](long long t) -> long long {
+      const long long e = a.perm[t];
+      if (e < 0 || e >= n) return -1;
+      return e1_bits_key(ws[e * R + R - 1]);
+    };
+    const long long p0 = e1_snap(static_cast<long long>((static_cast<__int128>(n) * wg) / nwarps), n, sender, lane);
+    const long long p1 = e1_snap(static_cast<long long>((static_cast<__int128>(n) * (wg + 1)) / nwarps), n, sender, lane);
+    T carry[D1];
+    long long carry_key = -2;
+    for (long long base = p0; base < p1; base += 32) {
+      const long long t = base + lane;
+      long long key = -1;
+      T h[D1];
+#pragma unroll
+      for (int i = 0; i < D1; ++i) h[i] = T(0);
+      if (t < p1) {
+        const long long e = a.perm[t];
+        if (e < 0 || e >= n) {
+          flag(a.status, 2);
+        } else {
+          T rec[R];
+          const T* r = ws + e * R;
+          if constexpr (sizeof(T) == 4) {
+            const float4 u = __ldg(reinterpret_cast<const float4*>(r));
+            const float4 v = __ldg(reinterpret_cast<const float4*>(r) + 1);
+            rec[0] = u.x; rec[1] = u.y; rec[2] = u.z; rec[3] = u.w;
+            rec[4] = v.x; rec[5] = v.y; rec[6] = v.z; rec[7] = v.w;
+          } else {
+#pragma unroll
+            for (int q = 0; q < R / 2; ++q) {
+              const double2 u = __ldg(reinterpret_cast<const double2*>(r) + q);
+              rec[2 * q] = u.x;
+              rec[2 * q + 1] = u.y;
+            }
+          }
+#pragma unroll
+          for (int i = 0; i < D1; ++i) h[i] = rec[i];
+          key = e1_bits_key(rec[R - 1]);
+        }
+      }
+      const bool more = base + 32 < p1;
+      const long long nk = more ? sender(base + 32) : -3;
+      e1_seg_block<T, D1>(h, key, nk, more, carry, carry_key, a.out0, lane);
+    }
+  });
 }
 
 }  // namespace oeqb

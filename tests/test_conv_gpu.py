@@ -174,3 +174,36 @@ def test_conv_input_validation(cuda_device):
         conv(X, Y, W, rows.cpu(), cols, tp)
     with pytest.raises(RuntimeError, match="Dtype mismatch"):
         conv(X, Y, W, rows.int(), cols, tp)
+
+
+@pytest.mark.parametrize("dtype", [np.float32, np.float64], ids=["f32", "f64"])
+def test_deterministic_single_path_dense_graph(dtype, cuda_device):
+    """C3-class deterministic conv on a dense graph (~150 neighbours per node), so receiver and
+    sender runs span several 32-edge blocks: forward, backward and bitwise repeatability."""
+    import openequivariance_b200 as oeq
+
+    pos, rows, cols, tperm, _ = radius_graph(300, 10.0, 4.5, seed=3)
+    assert len(rows) / 300 > 100
+    prob = oeq.TPProblem("1x2e", "1x3e", "1x2e", [(0, 0, 0, "uvu", True)],
+                         shared_weights=False, internal_weights=False, irrep_dtype=dtype,
+                         weight_dtype=dtype)
+    conv = oeq.TensorProductConv(prob, deterministic=True)
+    p = O.make_problem("1x2e", "1x3e", "1x2e", [(0, 0, 0, "uvu", True)])
+    rng = np.random.default_rng(8)
+    X, Y = rng.normal(size=(300, 5)), rng.normal(size=(len(rows), 7))
+    W, G = rng.normal(size=(len(rows), 1)), rng.normal(size=(300, 5))
+    r, c, t = _idx(rows), _idx(cols), _idx(tperm)
+    outs = []
+    for _ in range(2):
+        x, y, w = (to_dev(X, dtype).requires_grad_(), to_dev(Y, dtype).requires_grad_(),
+                   to_dev(W, dtype).requires_grad_())
+        Z = conv(x, y, w, r, c, t)
+        Z.backward(to_dev(G, dtype))
+        outs.append([Z.detach(), x.grad, y.grad, w.grad])
+    assert_close(outs[0][0], O.conv_forward(p, X, Y, W, rows, cols), dtype, "forward")
+    gX, gY, gW = O.conv_backward(p, X, Y, W, G, rows, cols)
+    assert_close(outs[0][1], gX, dtype, "dX")
+    assert_close(outs[0][2], gY, dtype, "dY")
+    assert_close(outs[0][3], gW, dtype, "dW")
+    for a, b in zip(outs[0], outs[1]):
+        assert torch.equal(a, b)
