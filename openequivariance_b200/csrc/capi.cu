@@ -1262,8 +1262,9 @@ int launch_uvw_sw(oeqb_plan& p, const Args<T>& a, cudaStream_t stream) {
     std::lock_guard<std::mutex> g(p.mu);
     auto it = p.occ.find(kxy);
     if (it == p.occ.end()) {
+      if (int rc = allow_max_smem(p.device, kxy)) return rc;
       int n = 0;
-      OEQB_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kxy, kSwThreads, 0));
+      OEQB_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kxy, kSwThreads, sw_dxy_smem<T>()));
       if (n <= 0) return fail(OEQB_ERR_UNSUPPORTED, "uvw backward kernel does not fit");
       it = p.occ.emplace(kxy, n).first;
     }
@@ -1280,8 +1281,8 @@ int launch_uvw_sw(oeqb_plan& p, const Args<T>& a, cudaStream_t stream) {
   const void* kdw = uvw_sw_kernel_ptr<T>(1);
   if (int rc = allow_max_smem(p.device, kdw)) return rc;
   void* params[] = {&v};
-  OEQB_CUDA(cudaLaunchKernel(kxy, dim3(static_cast<unsigned>(bxy)), dim3(kSwThreads), params, 0,
-                             stream));
+  OEQB_CUDA(cudaLaunchKernel(kxy, dim3(static_cast<unsigned>(bxy)), dim3(kSwThreads), params,
+                             sw_dxy_smem<T>(), stream));
   OEQB_CUDA(cudaLaunchKernel(kdw, dim3(ngrp, static_cast<unsigned>(chunks)), dim3(kSwThreads),
                              params, sw_dw_smem<T>(), stream));
   return 0;

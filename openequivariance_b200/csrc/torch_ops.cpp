@@ -7,6 +7,7 @@
 // so torch fakes, autograd registration, torch.compile and export keep working unchanged.
 // The `json_bytes` argument carries this package's binary problem descriptor; `hash` keys
 // the plan cache (one plan per (hash, device)), as in torch_core.hpp:185-296.
+#include <cstring>
 #include <ATen/ATen.h>
 #include <ATen/Context.h>
 #include <c10/cuda/CUDAGuard.h>
@@ -143,6 +144,15 @@ std::tuple<Tensor, Tensor, Tensor> jit_tp_backward(Tensor json_bytes, int64_t ha
   return {L1_grad, L2_grad, W_grad};
 }
 
+// Problem-descriptor flags (the int64 header of json_bytes, include/oeqb200.h): uvw and
+// shared weights.
+bool shared_weight_uvw(const Tensor& json_bytes) {
+  if (json_bytes.numel() < 16 * 8 || !json_bytes.is_cpu()) return false;
+  int64_t h[16];
+  std::memcpy(h, json_bytes.contiguous().data_ptr<uint8_t>(), sizeof(h));
+  return h[4] != 0 && h[5] != 0;
+}
+
 std::tuple<Tensor, Tensor, Tensor, Tensor> jit_tp_double_backward(
     Tensor json_bytes, int64_t hash, Tensor L1_in, Tensor L2_in, Tensor W, Tensor L3_grad,
     Tensor L1_dgrad, Tensor L2_dgrad, Tensor W_dgrad) {
@@ -163,6 +173,33 @@ std::tuple<Tensor, Tensor, Tensor, Tensor> jit_tp_double_backward(
   Tensor x = L1_in.contiguous(), y = L2_in.contiguous(), w = W.contiguous(),
          gz = L3_grad.contiguous(), dx = L1_dgrad.contiguous(), dy = L2_dgrad.contiguous(),
          dw = W_dgrad.contiguous();
+  if (shared_weight_uvw(json_bytes) && B > 0) {
+    // Shared-weight uvw: the product is trilinear, so the double backward is three forwards
+    // and three backwards with one operand swapped (the dedicated kernels of this class),
+    // summed here; the generic double-backward kernels would add every row's weight gradient
+    // with global atomics.
+    const auto st = stream_of(L1_in);
+    auto fwd = [&](const Tensor& a, const Tensor& b, const Tensor& c) {
+      Tensor z = at::empty_like(L3_grad, at::MemoryFormat::Contiguous);
+      check_rc(oeqb_tp_forward(k.plan, B, a.data_ptr(), b.data_ptr(), c.data_ptr(), z.data_ptr(), st));
+      return z;
+    };
+    auto bwd = [&](const Tensor& a, const Tensor& b, const Tensor& c) {
+      Tensor ga = at::empty_like(L1_in, at::MemoryFormat::Contiguous);
+      Tensor gb = at::empty_like(L2_in, at::MemoryFormat::Contiguous);
+      Tensor gc = at::empty_like(W, at::MemoryFormat::Contiguous);
+      check_rc(oeqb_tp_backward(k.plan, B, a.data_ptr(), ga.data_ptr(), b.data_ptr(),
+                                gb.data_ptr(), c.data_ptr(), gc.data_ptr(), gz.data_ptr(), st));
+      return std::make_tuple(ga, gb, gc);
+    };
+    L3_dgrad = fwd(dx, y, w);
+    L3_dgrad.add_(fwd(x, dy, w));
+    L3_dgrad.add_(fwd(x, y, dw));
+    auto [gx1, unused_y1, gw1] = bwd(x, dy, w);
+    auto [unused_x2, gy2, gw2] = bwd(dx, y, w);
+    auto [gx3, gy3, unused_w3] = bwd(x, y, dw);
+    return {gx1.add_(gx3), gy2.add_(gy3), gw1.add_(gw2), L3_dgrad};
+  }
   check_rc(oeqb_tp_double_backward(k.plan, B, x.data_ptr(), y.data_ptr(), w.data_ptr(),
                                    gz.data_ptr(), dx.data_ptr(), dy.data_ptr(), dw.data_ptr(),
                                    L1_grad.data_ptr(), L2_grad.data_ptr(), W_grad.data_ptr(),

@@ -11,9 +11,9 @@
 //
 //  * tp_uvw_sw_dxy: CTA = 32 rows x 8 channel groups of 4.  Per input irrep the thread keeps
 //    its 4 x d1 dX values and x in registers; per instruction it forms G for its 4 channels
-//    from 4 x 4 register blocks of W'^T (prepared once per call, [n][w][u]) and dZ (float4
-//    loads of 4 w x d3 contiguous values), then adds hvec (dX) and evec (dY) of the unrolled
-//    CG tables.  dY is folded over the 8 channel groups with shuffles and summed per row in
+//    from 4 x 4 register blocks of W'^T (prepared once per call, [n][w][u]) and dZ, both
+//    staged in shared memory by cp.async one instruction ahead, then adds hvec (dX) and evec
+//    (dY) of the unrolled CG tables.  dY is folded over the 8 channel groups with shuffles and summed per row in
 //    shared memory.  No atomics; every dX / dY element is written once.
 //  * tp_uvw_sw_dw: split-K over row chunks.  CTA = 4 instructions (same l3) x 64 threads, each
 //    thread a 4 x 4 (u, w) block of dW_n accumulated over the chunk's rows from shared-memory
@@ -99,43 +99,113 @@ __device__ __forceinline__ void st4(T* p, const T* v) {
 }
 
 // ------------------------------------------------------------------ dX and dY
+//
+// Per instruction the CTA's dZ tile (32 rows x the output block, 32 d3 values, row pitch
+// padded by 4) and W'^T block (32 x 32) are copied into shared memory with cp.async, one
+// instruction ahead of the compute (double buffer), so the FMA loop reads shared memory only.
+
+constexpr int kSwZPitchMax = 32 * 7 + 4;
+
+template <class T>
+constexpr size_t sw_dxy_smem() {
+  return sizeof(T) * (2 * static_cast<size_t>(kSwRows) * kSwZPitchMax + 2 * 1024 +
+                      kSwRows * (kSwYMax + 1));
+}
+
+__device__ __forceinline__ void cp_async16(void* dst, const void* src, bool pred) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(static_cast<unsigned>(__cvta_generic_to_shared(dst))), "l"(src),
+               "r"(pred ? 16 : 0)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+  asm volatile("cp.async.commit_group;\n" ::: "memory");
+}
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
+}
+
+// Issues the copies of instruction `in` into buffer b: dZ rows (invalid rows zero-filled) and
+// the W'^T block.
+template <class T>
+__device__ __forceinline__ void sw_dxy_prefetch(const ArgsSw<T>& a, const SwIns& in,
+                                                long long row0, T* zbuf, T* wbuf) {
+  constexpr int V = 16 / sizeof(T);
+  const int d3 = 2 * in.l3 + 1;
+  const int pitch = 32 * d3 + 4;
+  const int per_row = 32 * d3 / V;  // 16-byte granules per row
+  for (int q = threadIdx.x; q < kSwRows * per_row; q += kSwThreads) {
+    const int rr = q / per_row, e = q - rr * per_row;
+    const long long row = row0 + rr;
+    const bool ok = row < a.B;
+    const T* src = a.dZ + (ok ? row : 0) * a.L3dim + in.z_off + e * V;
+    cp_async16(zbuf + rr * pitch + e * V, src, ok);
+  }
+  const T* wsrc = a.Wt + static_cast<size_t>(in.wblk) * 1024;
+  for (int q = threadIdx.x; q < 1024 / V; q += kSwThreads) cp_async16(wbuf + q * V, wsrc + q * V, true);
+}
 
 template <class T, int L1, int L2, int L3>
 __device__ __forceinline__ void sw_dxy_ins(const ArgsSw<T>& a, const SwIns& in, long long row,
-                                           bool valid, int g, const T (&x)[4][2 * L1 + 1],
-                                           T (&dx)[4][2 * L1 + 1], T* dys_row, int lane) {
+                                           bool valid, int g, int r, const T (&x)[4][2 * L1 + 1],
+                                           T (&dx)[4][2 * L1 + 1], T* dys_row, const T* zbuf,
+                                           const T* wbuf) {
   constexpr int D1 = 2 * L1 + 1, D2 = 2 * L2 + 1, D3 = 2 * L3 + 1;
+  constexpr int PITCH = 32 * D3 + 4;
   T G[4][D3];
 #pragma unroll
   for (int uu = 0; uu < 4; ++uu)
 #pragma unroll
     for (int k = 0; k < D3; ++k) G[uu][k] = T(0);
-  T y[D2];
-  if (valid) {
-    const T* zrow = a.dZ + row * a.L3dim + in.z_off;
-    const T* wt = a.Wt + static_cast<size_t>(in.wblk) * 1024 + 4 * g;
-#pragma unroll 1
-    for (int w0 = 0; w0 < 32; w0 += 4) {
-      T z[4 * D3];
+  const T* zrow = zbuf + r * PITCH;
+  const T* wt = wbuf + 4 * g;
+#pragma unroll 2
+  for (int w0 = 0; w0 < 32; w0 += 4) {
+    T z[4 * D3];
 #pragma unroll
-      for (int e = 0; e < D3; ++e) ld4(z + 4 * e, zrow + w0 * D3 + 4 * e);
-#pragma unroll
-      for (int ww = 0; ww < 4; ++ww) {
-        T wv[4];
-        ld4(wv, wt + (w0 + ww) * 32);
-#pragma unroll
-        for (int uu = 0; uu < 4; ++uu)
-#pragma unroll
-          for (int k = 0; k < D3; ++k) G[uu][k] = fma(wv[uu], z[ww * D3 + k], G[uu][k]);
+    for (int e = 0; e < D3; ++e) {
+      if constexpr (sizeof(T) == 4) {
+        const float4 t = *reinterpret_cast<const float4*>(zrow + w0 * D3 + 4 * e);
+        z[4 * e] = t.x;
+        z[4 * e + 1] = t.y;
+        z[4 * e + 2] = t.z;
+        z[4 * e + 3] = t.w;
+      } else {
+        const double2 t0 = *reinterpret_cast<const double2*>(zrow + w0 * D3 + 4 * e);
+        const double2 t1 = *reinterpret_cast<const double2*>(zrow + w0 * D3 + 4 * e + 2);
+        z[4 * e] = t0.x;
+        z[4 * e + 1] = t0.y;
+        z[4 * e + 2] = t1.x;
+        z[4 * e + 3] = t1.y;
       }
     }
-    const T* yrow = a.Y + row * a.L2dim + in.y_off;
 #pragma unroll
-    for (int j = 0; j < D2; ++j) y[j] = yrow[j];
-  } else {
+    for (int ww = 0; ww < 4; ++ww) {
+      T wv[4];
+      if constexpr (sizeof(T) == 4) {
+        const float4 t = *reinterpret_cast<const float4*>(wt + (w0 + ww) * 32);
+        wv[0] = t.x;
+        wv[1] = t.y;
+        wv[2] = t.z;
+        wv[3] = t.w;
+      } else {
+        const double2 t0 = *reinterpret_cast<const double2*>(wt + (w0 + ww) * 32);
+        const double2 t1 = *reinterpret_cast<const double2*>(wt + (w0 + ww) * 32 + 2);
+        wv[0] = t0.x;
+        wv[1] = t0.y;
+        wv[2] = t1.x;
+        wv[3] = t1.y;
+      }
 #pragma unroll
-    for (int j = 0; j < D2; ++j) y[j] = T(0);
+      for (int uu = 0; uu < 4; ++uu)
+#pragma unroll
+        for (int k = 0; k < D3; ++k) G[uu][k] = fma(wv[uu], z[ww * D3 + k], G[uu][k]);
+    }
   }
+  T y[D2];
+  const T* yrow = a.Y + row * a.L2dim + in.y_off;
+#pragma unroll
+  for (int j = 0; j < D2; ++j) y[j] = valid ? yrow[j] : T(0);
   T es[D2];
 #pragma unroll
   for (int j = 0; j < D2; ++j) es[j] = T(0);
@@ -162,62 +232,69 @@ __device__ __forceinline__ void sw_dxy_ins(const ArgsSw<T>& a, const SwIns& in, 
 #pragma unroll
     for (int j = 0; j < D2; ++j) dys_row[in.y_off + j] += es[j];
   }
-  (void)lane;
-}
-
-template <class T, int L1>
-__device__ __forceinline__ void sw_dxy_group(const ArgsSw<T>& a, const SwGroup& gp,
-                                             long long row, bool valid, int g, T* dys_row,
-                                             int lane) {
-  constexpr int D1 = 2 * L1 + 1;
-  T x[4][D1], dx[4][D1];
-  const T* xp = a.X + row * a.L1dim + gp.x_off + 4 * g * D1;
-#pragma unroll
-  for (int uu = 0; uu < 4; ++uu)
-#pragma unroll
-    for (int i = 0; i < D1; ++i) {
-      x[uu][i] = valid ? xp[uu * D1 + i] : T(0);
-      dx[uu][i] = T(0);
-    }
-  for (int ni = gp.ins_begin; ni < gp.ins_end; ++ni) {
-    const SwIns in = a.ins[ni];
-    dispatch_bc<L1>(pair_code(in.l2, in.l3), [&]<int L2, int L3>() {
-      sw_dxy_ins<T, L1, L2, L3>(a, in, row, valid, g, x, dx, dys_row, lane);
-    });
-  }
-  if (valid) {
-    T* dp = a.dX + row * a.L1dim + gp.x_off + 4 * g * D1;
-#pragma unroll
-    for (int uu = 0; uu < 4; ++uu)
-#pragma unroll
-      for (int i = 0; i < D1; ++i) dp[uu * D1 + i] = dx[uu][i];
-  }
 }
 
 template <class T>
 __global__ void __launch_bounds__(kSwThreads) tp_uvw_sw_dxy(const ArgsSw<T> a) {
-  __shared__ T dys[kSwRows][kSwYMax + 1];
-  const int g = threadIdx.x & 7, r = threadIdx.x >> 3, lane = threadIdx.x & 31;
+  extern __shared__ __align__(16) unsigned char sw_dxy_raw[];
+  T* zb = reinterpret_cast<T*>(sw_dxy_raw);                    // [2][32][pitch]
+  T* wb = zb + 2 * kSwRows * kSwZPitchMax;                     // [2][1024]
+  T* dys = wb + 2 * 1024;                                      // [32][kSwYMax + 1]
+  const int g = threadIdx.x & 7, r = threadIdx.x >> 3;
   const long long ntiles = (a.B + kSwRows - 1) / kSwRows;
+  const int nins = a.ngroups > 0 ? a.groups[a.ngroups - 1].ins_end : 0;
   for (long long tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
     const long long row0 = tile * kSwRows;
-    for (int i = threadIdx.x; i < kSwRows * (kSwYMax + 1); i += blockDim.x)
-      (&dys[0][0])[i] = T(0);
-    __syncthreads();
+    for (int i = threadIdx.x; i < kSwRows * (kSwYMax + 1); i += blockDim.x) dys[i] = T(0);
+    if (nins > 0) sw_dxy_prefetch(a, a.ins[0], row0, zb, wb);
+    cp_async_commit();
     const long long row = row0 + r;
     const bool valid = row < a.B;
+    int ni = 0;  // running instruction index (buffer ni & 1)
     for (int gi = 0; gi < a.ngroups; ++gi) {
       const SwGroup gp = a.groups[gi];
       dispatch_l(gp.l1, [&]<int L1>() {
-        sw_dxy_group<T, L1>(a, gp, row, valid, g, dys[r], lane);
+        constexpr int D1 = 2 * L1 + 1;
+        T x[4][D1], dx[4][D1];
+        const T* xp = a.X + row * a.L1dim + gp.x_off + 4 * g * D1;
+#pragma unroll
+        for (int uu = 0; uu < 4; ++uu)
+#pragma unroll
+          for (int i = 0; i < D1; ++i) {
+            x[uu][i] = valid ? xp[uu * D1 + i] : T(0);
+            dx[uu][i] = T(0);
+          }
+        for (; ni < gp.ins_end; ++ni) {
+          const int b = ni & 1;
+          if (ni + 1 < nins)
+            sw_dxy_prefetch(a, a.ins[ni + 1], row0, zb + (b ^ 1) * kSwRows * kSwZPitchMax,
+                            wb + (b ^ 1) * 1024);
+          cp_async_commit();
+          cp_async_wait<1>();
+          __syncthreads();
+          const SwIns in = a.ins[ni];
+          dispatch_bc<L1>(pair_code(in.l2, in.l3), [&]<int L2, int L3>() {
+            sw_dxy_ins<T, L1, L2, L3>(a, in, row, valid, g, r, x, dx, dys + r * (kSwYMax + 1),
+                                      zb + b * kSwRows * kSwZPitchMax, wb + b * 1024);
+          });
+          __syncthreads();  // buffer b is refilled by the prefetch two instructions on
+        }
+        if (valid) {
+          T* dp = a.dX + row * a.L1dim + gp.x_off + 4 * g * D1;
+#pragma unroll
+          for (int uu = 0; uu < 4; ++uu)
+#pragma unroll
+            for (int i = 0; i < D1; ++i) dp[uu * D1 + i] = dx[uu][i];
+        }
       });
     }
+    cp_async_wait<0>();
     __syncthreads();
     const long long left = a.B - row0;
     const int nr = left < kSwRows ? static_cast<int>(left) : kSwRows;
     for (int i = threadIdx.x; i < nr * a.L2dim; i += blockDim.x) {
       const int rr = i / a.L2dim, j = i - rr * a.L2dim;
-      a.dY[(row0 + rr) * a.L2dim + j] = dys[rr][j];
+      a.dY[(row0 + rr) * a.L2dim + j] = dys[rr * (kSwYMax + 1) + j];
     }
     __syncthreads();
   }
