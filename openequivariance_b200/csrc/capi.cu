@@ -149,6 +149,9 @@ struct oeqb_plan {
     std::vector<SwGroup> groups;
     std::vector<SwIns> ins;
     std::vector<SwDw> dw;
+    std::vector<SwOut> fouts;  // forward (float64): paths grouped by output irrep
+    std::vector<SwFIns> fins;
+    size_t off_fouts = 0, off_fins = 0;
     std::vector<int> woff;
     std::vector<float> pw_f;
     std::vector<double> pw_d;
@@ -649,6 +652,16 @@ void build_uvw_sw(oeqb_plan& p) {
     g.ins_end = static_cast<int>(t.ins.size());
     t.groups.push_back(g);
   }
+  for (int i3 = 0; i3 < p.n3; ++i3) {  // forward tables (every output irrep is written)
+    if (p.ir3[i3].mul != 32 && p.ir3[i3].mul != 0) return;
+    SwOut o{p.ir3[i3].off, p.ir3[i3].l, static_cast<int>(t.fins.size()), 0};
+    for (const InstrD& in : p.ins_f)
+      if (in.i3 == i3)
+        t.fins.push_back(SwFIns{in.l1, in.l2, p.ir1[in.i1].off, p.ir2[in.i2].off, in.woff, 0, 0,
+                                0, in.pw});
+    o.ins_end = static_cast<int>(t.fins.size());
+    t.fouts.push_back(o);
+  }
   std::vector<int> order(p.ins_b.size());
   for (size_t n = 0; n < order.size(); ++n) order[n] = static_cast<int>(n);
   std::stable_sort(order.begin(), order.end(),
@@ -842,6 +855,8 @@ void layout_tables(oeqb_plan& p, std::vector<unsigned char>& buf) {
   p.sw.off_groups = put(buf, p.sw.groups);
   p.sw.off_ins = put(buf, p.sw.ins);
   p.sw.off_dw = put(buf, p.sw.dw);
+  p.sw.off_fouts = put(buf, p.sw.fouts);
+  p.sw.off_fins = put(buf, p.sw.fins);
   p.sw.off_woff = put(buf, p.sw.woff);
   p.sw.off_pw = p.dtype == 2 ? put(buf, p.sw.pw_d) : put(buf, p.sw.pw_f);
   p.off.total = align16(buf.size());
@@ -1335,6 +1350,44 @@ size_t edge1_det_ws_bytes(const oeqb_plan& p, int64_t nnz) {
   return size_t(nnz) * kE1Rec * p.elem();
 }
 
+// Shared-weight uvw forward on CUDA cores (float64).
+template <class T>
+int launch_uvw_sw_fwd(oeqb_plan& p, const Args<T>& a, cudaStream_t stream) {
+  if (a.nitems <= 0) return 0;
+  const void* kernel = uvw_sw_kernel_ptr<T>(3);
+  int per_sm;
+  {
+    std::lock_guard<std::mutex> g(p.mu);
+    auto it = p.occ.find(kernel);
+    if (it == p.occ.end()) {
+      if (int rc = allow_max_smem(p.device, kernel)) return rc;
+      int n = 0;
+      OEQB_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kernel, kSwThreads, sw_fwd_smem<T>()));
+      if (n <= 0) return fail(OEQB_ERR_UNSUPPORTED, "uvw forward kernel does not fit");
+      it = p.occ.emplace(kernel, n).first;
+    }
+    per_sm = it->second;
+  }
+  ArgsSwF<T> v{};
+  v.X = a.X;
+  v.Y = a.Y;
+  v.W = a.W;
+  v.Z = a.out0;
+  v.B = a.nitems;
+  v.L1dim = p.L1dim;
+  v.L2dim = p.L2dim;
+  v.L3dim = p.L3dim;
+  v.nout = static_cast<int>(p.sw.fouts.size());
+  v.outs = reinterpret_cast<const SwOut*>(p.dmem + p.sw.off_fouts);
+  v.ins = reinterpret_cast<const SwFIns*>(p.dmem + p.sw.off_fins);
+  const long long tiles = (a.nitems + kSwRows - 1) / kSwRows;
+  const long long blocks = std::max<long long>(1, std::min<long long>(tiles, (long long)p.sm_count * per_sm));
+  void* params[] = {&v};
+  OEQB_CUDA(cudaLaunchKernel(kernel, dim3(static_cast<unsigned>(blocks)), dim3(kSwThreads), params,
+                             sw_fwd_smem<T>(), stream));
+  return 0;
+}
+
 struct DeviceGuard {
   int prev = -1;
   explicit DeviceGuard(int dev) {
@@ -1364,6 +1417,8 @@ int tp_forward_t(oeqb_plan* p, int64_t B, const void* X, const void* Y, const vo
   a.out0 = static_cast<T*>(Z);
   if constexpr (std::is_same_v<T, float>) {
     if (p->tc.ok && aligned16(X) && aligned16(Z)) return launch_uvw_tc(*p, a, s);
+  } else {
+    if (p->sw.ok && aligned16(W)) return launch_uvw_sw_fwd(*p, a, s);
   }
   if (p->segf.ok) return launch_seg(*p, 0, a, s);
   if (p->row_ok) return launch_row(*p, 0, a, s);

@@ -300,6 +300,167 @@ __global__ void __launch_bounds__(kSwThreads) tp_uvw_sw_dxy(const ArgsSw<T> a) {
   }
 }
 
+// ------------------------------------------------------------------ forward (CUDA cores)
+//
+// Used for float64 (float32 runs on the tensor cores, tp_kernels_uvw_tc.cuh).  CTA = 32 rows x
+// 8 groups of 4 output channels.  Per output irrep the thread accumulates Z[w][k] for its 4
+// channels over the paths into it: per path the CTA computes T[u][k] = pw sum_i P[i][k] x[u][i]
+// for its rows into shared memory (each thread 4 channels u), the path's 32 x 32 weight block
+// is staged by cp.async (one path ahead), then Z[w][k] += sum_u W[u][w] T[u][k].
+
+struct SwOut {  // one output irrep and the paths into it
+  int z_off, l3, ins_begin, ins_end;
+};
+struct SwFIns {
+  int l1, l2, x_off, y_off, woff, pad0, pad1, pad2;
+  double pw;
+};
+
+constexpr int kSwTPitch = 32 * 7 + 1;  // T tile row pitch (odd: conflict-free row reads)
+
+template <class T>
+__host__ __device__ constexpr size_t sw_fwd_smem() {
+  return sizeof(T) * (static_cast<size_t>(kSwRows) * kSwTPitch + 2 * 1024);
+}
+
+template <class T>
+struct ArgsSwF {
+  const T* X;
+  const T* Y;
+  const T* W;
+  T* Z;
+  long long B;
+  int L1dim, L2dim, L3dim, nout;
+  const SwOut* outs;
+  const SwFIns* ins;
+};
+
+template <class T, int L1, int L2, int L3>
+__device__ __forceinline__ void sw_fwd_t(const ArgsSwF<T>& a, const SwFIns& in, long long row,
+                                         bool valid, int g, int r, T* ts) {
+  constexpr int D1 = 2 * L1 + 1, D2 = 2 * L2 + 1, D3 = 2 * L3 + 1;
+  T P[D1 * D3];
+#pragma unroll
+  for (int e = 0; e < D1 * D3; ++e) P[e] = T(0);
+  T x[4][D1];
+  if (valid) {
+    T y[D2];
+    const T* yrow = a.Y + row * a.L2dim + in.y_off;
+#pragma unroll
+    for (int j = 0; j < D2; ++j) y[j] = yrow[j] * T(in.pw);
+    CG<L1, L2, L3>::pmat(y, P);
+    const T* xp = a.X + row * a.L1dim + in.x_off + 4 * g * D1;
+#pragma unroll
+    for (int uu = 0; uu < 4; ++uu)
+#pragma unroll
+      for (int i = 0; i < D1; ++i) x[uu][i] = xp[uu * D1 + i];
+  } else {
+#pragma unroll
+    for (int uu = 0; uu < 4; ++uu)
+#pragma unroll
+      for (int i = 0; i < D1; ++i) x[uu][i] = T(0);
+  }
+  T* tr = ts + r * kSwTPitch + 4 * g * D3;
+#pragma unroll
+  for (int uu = 0; uu < 4; ++uu)
+#pragma unroll
+    for (int k = 0; k < D3; ++k) {
+      T t = T(0);
+#pragma unroll
+      for (int i = 0; i < D1; ++i) t = fma(P[i * D3 + k], x[uu][i], t);
+      tr[uu * D3 + k] = t;
+    }
+}
+
+template <class T, int L3>
+__device__ __forceinline__ void sw_fwd_acc(const T* ts, const T* wb, int g, int r,
+                                           T (&z)[4][2 * L3 + 1]) {
+  constexpr int D3 = 2 * L3 + 1;
+  const T* tr = ts + r * kSwTPitch;
+#pragma unroll 4
+  for (int u = 0; u < 32; ++u) {
+    T t[D3], wv[4];
+#pragma unroll
+    for (int k = 0; k < D3; ++k) t[k] = tr[u * D3 + k];
+    if constexpr (sizeof(T) == 4) {
+      const float4 q = *reinterpret_cast<const float4*>(wb + u * 32 + 4 * g);
+      wv[0] = q.x;
+      wv[1] = q.y;
+      wv[2] = q.z;
+      wv[3] = q.w;
+    } else {
+      const double2 q0 = *reinterpret_cast<const double2*>(wb + u * 32 + 4 * g);
+      const double2 q1 = *reinterpret_cast<const double2*>(wb + u * 32 + 4 * g + 2);
+      wv[0] = q0.x;
+      wv[1] = q0.y;
+      wv[2] = q1.x;
+      wv[3] = q1.y;
+    }
+#pragma unroll
+    for (int ww = 0; ww < 4; ++ww)
+#pragma unroll
+      for (int k = 0; k < D3; ++k) z[ww][k] = fma(wv[ww], t[k], z[ww][k]);
+  }
+}
+
+template <class T>
+__device__ __forceinline__ void sw_fwd_prefetch_w(const ArgsSwF<T>& a, const SwFIns& in, T* wbuf) {
+  constexpr int V = 16 / sizeof(T);
+  for (int q = threadIdx.x; q < 1024 / V; q += kSwThreads) cp_async16(wbuf + q * V, a.W + in.woff + q * V, true);
+}
+
+template <class T>
+__global__ void __launch_bounds__(kSwThreads) tp_uvw_sw_fwd(const ArgsSwF<T> a) {
+  extern __shared__ __align__(16) unsigned char sw_fwd_raw[];
+  T* ts = reinterpret_cast<T*>(sw_fwd_raw);  // [32 rows][pitch]
+  T* wb = ts + kSwRows * kSwTPitch;           // [2][1024]
+  const int g = threadIdx.x & 7, r = threadIdx.x >> 3;
+  const long long ntiles = (a.B + kSwRows - 1) / kSwRows;
+  const int nins = a.nout > 0 ? a.outs[a.nout - 1].ins_end : 0;
+  for (long long tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
+    const long long row = tile * kSwRows + r;
+    const bool valid = row < a.B;
+    if (nins > 0) sw_fwd_prefetch_w(a, a.ins[0], wb);
+    cp_async_commit();
+    int ni = 0;
+    for (int oi = 0; oi < a.nout; ++oi) {
+      const SwOut o = a.outs[oi];
+      dispatch_l(o.l3, [&]<int L3>() {
+        constexpr int D3 = 2 * L3 + 1;
+        T z[4][D3];
+#pragma unroll
+        for (int ww = 0; ww < 4; ++ww)
+#pragma unroll
+          for (int k = 0; k < D3; ++k) z[ww][k] = T(0);
+        for (; ni < o.ins_end; ++ni) {
+          const int b = ni & 1;
+          const SwFIns in = a.ins[ni];
+          dispatch_l(in.l1, [&]<int L1>() {
+            dispatch_bc<L1>(pair_code(in.l2, L3), [&]<int L2, int C>() {
+              if constexpr (C == L3) sw_fwd_t<T, L1, L2, L3>(a, in, row, valid, g, r, ts);
+            });
+          });
+          if (ni + 1 < nins) sw_fwd_prefetch_w(a, a.ins[ni + 1], wb + (b ^ 1) * 1024);
+          cp_async_commit();
+          cp_async_wait<1>();
+          __syncthreads();
+          sw_fwd_acc<T, L3>(ts, wb + b * 1024, g, r, z);
+          __syncthreads();
+        }
+        if (valid) {
+          T* zp = a.Z + row * a.L3dim + o.z_off + 4 * g * D3;
+#pragma unroll
+          for (int ww = 0; ww < 4; ++ww)
+#pragma unroll
+            for (int k = 0; k < D3; ++k) zp[ww * D3 + k] = z[ww][k];
+        }
+      });
+    }
+    cp_async_wait<0>();
+    __syncthreads();
+  }
+}
+
 // ------------------------------------------------------------------ dW
 
 template <class T, int L1, int L2, int L3>

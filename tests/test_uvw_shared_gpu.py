@@ -43,11 +43,15 @@ C4 = ("32x0e+32x0o+32x1e+32x1o+32x2e+32x2o", "1x0e+1x1o+1x2e",
       "32x0e+32x0o+32x1e+32x1o+32x2e+32x2o")
 
 
+@pytest.mark.parametrize("dtype", [np.float32, np.float64], ids=["f32", "f64"])
 @pytest.mark.parametrize("rows", [1, 6, 127, 128, 129, 1000])
-def test_c4_forward_vs_oracle(rows, cuda_device):
+def test_c4_forward_vs_oracle(rows, dtype, cuda_device):
+    """float32: tcgen05 kernel; float64: the CUDA-core kernel of the same class."""
     import openequivariance_b200 as oeq
+    from openequivariance_b200.problems import fully_connected_tpp
 
-    p = _fc(*C4)
+    p = fully_connected_tpp(*C4, shared_weights=True, internal_weights=False,
+                            irrep_dtype=dtype, weight_dtype=dtype)
     op = _oracle(p)
     perm = O.oeq_permutation(op)
     rng = np.random.default_rng(rows)
@@ -55,9 +59,12 @@ def test_c4_forward_vs_oracle(rows, cuda_device):
     Y = rng.normal(size=(rows, p.irreps_in2.dim))
     W = rng.normal(size=(p.weight_numel,)) / np.sqrt(32 * 5)
     tp = oeq.TensorProduct(p)
-    Z = tp(to_dev(X, np.float32), to_dev(Y, np.float32), to_dev(W[perm], np.float32))
-    e = nerr(Z, O.forward(op, X, Y, W))
-    assert e <= TOL[np.float32], f"normalised max error {e:.3e}"
+    xs, ys, ws = to_dev(X, dtype), to_dev(Y, dtype), to_dev(W[perm], dtype)
+    names = _kernel_names(lambda: tp(xs, ys, ws))
+    want = "tp_uvw_tc_fwd" if dtype == np.float32 else "tp_uvw_sw_fwd"
+    assert any(want in n for n in names), names
+    e = nerr(tp(xs, ys, ws), O.forward(op, X, Y, W))
+    assert e <= TOL[dtype], f"normalised max error {e:.3e}"
 
 
 def test_c4_forward_runs_on_tensor_cores_and_matches_fp64(cuda_device):
