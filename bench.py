@@ -273,6 +273,7 @@ def bench_tp(args, world, rank, local):
     for _ in range(args.warmup):
         step()
     torch.cuda.synchronize()
+    launches = _launches_per_step(step)
     K = args.steps
     ev = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(K)]
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -356,7 +357,7 @@ def bench_tp(args, world, rank, local):
                      "fwd_frac": bytes_fwd / (t_fwd * 1e-3) / 1e9 / peak,
                      "bwd_frac": bytes_bwd / (t_bwd * 1e-3) / 1e9 / peak},
         "e2e": e2e,
-        "gpu_launches": 2 * K,
+        "gpu_launches": launches * K,
         "clocks": clk.summary(),
     }
     fl = _dense_flops(problem) * B
@@ -452,6 +453,20 @@ def bench_reference(args, world, rank):
     }
 
 
+def _launches_per_step(step):
+    """Kernels of this library (namespace oeqb) one step launches, counted by the profiler on
+    an untimed step; gpu_launches = this x K."""
+    import torch
+    from torch.profiler import ProfilerActivity, profile
+
+    torch.cuda.synchronize()
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        step()
+        torch.cuda.synchronize()
+    return sum(1 for e in prof.events()
+               if e.device_type == torch.autograd.DeviceType.CUDA and "oeqb::" in e.name)
+
+
 def _time_steps(step, K, world, local):
     """K steps between barriers + device syncs; (max-over-ranks elapsed ms, clock summary)."""
     import torch
@@ -510,6 +525,7 @@ def bench_conv(args, world, rank, local):
     for _ in range(args.warmup):
         step()
     torch.cuda.synchronize()
+    launches = _launches_per_step(step)
     K = args.steps
     elapsed_ms, clocks = _time_steps(step, K, world, local)
     # Kernel-only timing of this rank's fused backward (the dominant pass), CUDA events.
@@ -578,7 +594,7 @@ def bench_conv(args, world, rank, local):
         "e2e": {"value": E * E2 / e2e_s, "unit": UNIT, "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "steps": E2,
                 "path": "PartitionedConv forward+backward, pinned host buffers per rank"},
-        "gpu_launches": 3 * K,
+        "gpu_launches": launches * K,
         "clocks": clocks,
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -648,6 +664,7 @@ def bench_sc(args, world, rank, local):
     for _ in range(args.warmup):
         step()
     torch.cuda.synchronize()
+    launches = _launches_per_step(step)
     K = args.steps
     elapsed_ms, clocks = _time_steps(step, K, world, local)
     return {
@@ -658,7 +675,7 @@ def bench_sc(args, world, rank, local):
         "config": {"workload": "sc: MACE symmetric contraction 128x0e+128x1o+128x2e -> "
                                "128x0e+128x1o, correlation 3, 10 elements",
                    "nodes_per_gpu": n, "parallelism": f"dp{world} (independent node shards)"},
-        "gpu_launches": 3 * K, "clocks": clocks,
+        "gpu_launches": launches * K, "clocks": clocks,
     }
 
 
