@@ -186,6 +186,19 @@ __global__ void __launch_bounds__((kLkWarps + 1) * 32, 1) tp_bwd_lk(const ArgsLk
   }
   const int r = wid / v.nch, c = wid - r * v.nch;  // this warp's row in the block and chunk
   const int ch = c * 32 + lane;
+  // Loop invariants in registers: after the barrier waits (asm with memory clobbers) the
+  // compiler would otherwise reload these kernel parameters from the constant bank per path.
+  const int nslots = v.nslots;
+  const size_t slot_elems = static_cast<size_t>(v.slot_elems);
+  const int gz_base = r * v.nch * 32 * kSegD;           // this warp's dZ rows in a slot
+  const int w_base = v.slot_w_off + r * v.nch * 32 + ch;  // this lane's weight in a slot
+  const bool shared_w = a.shared_w != 0;
+  const T* __restrict__ Wg = a.W;
+  int* status = a.status;
+  const T* ring = s.ring;
+  unsigned long long* slot_bar = s.slot_bar;
+  unsigned long long* slot_emp = s.slot_emp;
+  const SegInstr* insv = s.ins;
   int t = 0;          // ring sequence number
   int slot = 0;       // t % nslots
   unsigned par = 0;   // (t / nslots) & 1
@@ -227,19 +240,19 @@ __global__ void __launch_bounds__((kLkWarps + 1) * 32, 1) tp_bwd_lk(const ArgsLk
           gx[i] = T(0);
         }
         for (int n = run.n0; n < run.n1; ++n) {
-          mbar_wait(&s.slot_bar[slot], par, a.status);
-          const SegInstr in = s.ins[n];
-          const T* sl = s.ring + static_cast<size_t>(slot) * v.slot_elems;
+          mbar_wait(&slot_bar[slot], par, status);
+          const SegInstr in = insv[n];
+          const T* sl = ring + static_cast<size_t>(slot) * slot_elems;
           if (active) {
             dispatch_bc<A>(in.bc, [&]<int Bd, int C>() {
               constexpr int D2 = 2 * Bd + 1, D3 = 2 * C + 1;
               T P[seg_vpad<T>(D1 * D3)];
               lds_vec(P, Pr + in.p_off);
               T gz[D3];
-              const T* gs = sl + r * v.nch * 32 * kSegD + ch * D3;
+              const T* gs = sl + gz_base + ch * D3;
 #pragma unroll
               for (int kk = 0; kk < D3; ++kk) gz[kk] = gs[kk];
-              const T w = a.shared_w ? a.W[in.w_off + ch] : sl[v.slot_w_off + r * v.nch * 32 + ch];
+              const T w = shared_w ? Wg[in.w_off + ch] : sl[w_base];
               T sdot = T(0);
 #pragma unroll
               for (int i = 0; i < D1; ++i) {
@@ -249,7 +262,7 @@ __global__ void __launch_bounds__((kLkWarps + 1) * 32, 1) tp_bwd_lk(const ArgsLk
                 gx[i] += w * h;
                 sdot += x[i] * h;
               }
-              if (a.shared_w)
+              if (shared_w)
                 atomic_add(dwrow + in.w_off + ch, sdot);
               else
                 dwrow[in.w_off + ch] = sdot;
@@ -261,9 +274,9 @@ __global__ void __launch_bounds__((kLkWarps + 1) * 32, 1) tp_bwd_lk(const ArgsLk
             });
           }
           __syncwarp();
-          if (lane == 0) mbar_arrive(&s.slot_emp[slot]);
+          if (lane == 0) mbar_arrive(&slot_emp[slot]);
           ++t;
-          if (++slot == v.nslots) {
+          if (++slot == nslots) {
             slot = 0;
             par ^= 1u;
           }
