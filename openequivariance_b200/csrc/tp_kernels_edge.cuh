@@ -613,15 +613,15 @@ __global__ void __launch_bounds__(kEdgeWarps * 32) conv_fwd_edge1_det(const Args
     T* ys = e1_warp_smem<T>(smem, 32 * D2);
     T carry[D3];
     long long carry_key = -2;
-    for (long long base = p0; base < p1; base += 32) {
+    // Blocks start at the 4-aligned edge at or below p0 (lanes before p0 belong to the previous
+    // warp and are masked), so the Y rows of a block start 16-byte aligned.
+    for (long long base = p0 & ~3LL; base < p1; base += 32) {
       E1Lane l = e1_lane(a, base, lane);
-      if (l.e >= p1) {
+      if (l.e >= p1 || l.e < p0) {
         l.valid = false;
         l.row = -1;
       }
-      // Rows staged from the block start (not 32-aligned here: element-wise copy).
-      const long long nb = p1 - base < 32 ? p1 - base : 32;
-      for (int q = lane; q < nb * D2; q += 32) ys[q] = a.Y[base * D2 + q];
+      e1_stage_in<T, D2>(ys, a.Y, base, p1, lane);
       __syncwarp();
       T z[D3];
       e1_message<T, A, B, C>(a, p, l, ys, lane, z);
