@@ -38,7 +38,7 @@ const void* row_kernel_ptr(int kind, int nwarps);
 template <class T>
 const void* seg_kernel_ptr(int kind);
 template <class T>
-const void* lk_kernel_ptr();
+const void* lk_kernel_ptr(int cpl);
 template <class T>
 const void* edge_kernel_ptr(int kind);
 const void* uvw_tc_kernel_ptr(int kind);
@@ -122,7 +122,8 @@ struct oeqb_plan {
   // Lockstep backward (tp_kernels_lk.cuh) over the tables of segl.
   struct LkCfg {
     bool ok = false;
-    int nch = 0, rb = 0, nslots = 0, offY = 0, xy_elems = 0, slot_elems = 0, slot_w_off = 0;
+    int nch = 0, cpl = 1, rb = 0, nslots = 0, offY = 0, xy_elems = 0, slot_elems = 0,
+        slot_w_off = 0;
     size_t smem = 0;
   } lk;
   // Edge-per-lane convolution (tp_kernels_edge.cuh) for multiplicity-1 problems; edge1 = the
@@ -472,7 +473,8 @@ void build_seg(oeqb_plan& p) {
 
 // Lockstep backward: segment-eligible problems whose instructions all span the same number
 // of 32-channel chunks (dividing 16), that use every X irrep, and whose Y is the spherical-
-// harmonic layout (one irrep of each degree 0..L in order).
+// harmonic layout (one irrep of each degree 0..L in order).  An even chunk count runs two
+// channels per lane (a warp covers 64 channels) on 12 consumer warps where they divide.
 void build_lk(oeqb_plan& p) {
   p.lk = {};
   p.segl = {};
@@ -488,7 +490,7 @@ void build_lk(oeqb_plan& p) {
     nch = c;
     used[in.i1] = 1;
   }
-  if (nch <= 0 || kLkWarps % nch != 0) return;
+  if (nch <= 0) return;
   for (size_t r = 0; r < p.ir1.size(); ++r)
     if (!used[r] || p.ir1[r].mul != nch * 32) return;
   std::vector<int> order(p.ins_f.size());
@@ -505,19 +507,26 @@ void build_lk(oeqb_plan& p) {
   const size_t elem = p.dtype == 2 ? 8 : 4;
   oeqb_plan::LkCfg& c = p.lk;
   c.nch = nch;
-  c.rb = kLkWarps / nch;
   c.offY = static_cast<int>(round_elems(p.L1dim, elem));
   c.xy_elems = c.offY + static_cast<int>(round_elems(p.L2dim, elem));
-  c.slot_w_off = c.rb * nch * 32 * kSegD;
-  c.slot_elems = c.slot_w_off + (p.shared_w ? 0 : c.rb * nch * 32);
-  const size_t fixed = p.segl.blob.size() + 8 * (4 + 2 * kLkMaxSlots) +
-                       elem * (size_t(2) * c.rb * c.xy_elems + size_t(c.rb) * p.segl.psize +
-                               size_t(kLkWarps) * kLkGy);
-  for (c.nslots = kLkMaxSlots; c.nslots >= 3; --c.nslots) {
-    c.smem = fixed + elem * size_t(c.nslots) * c.slot_elems;
-    if (c.smem <= 220 * 1024) break;
+  // Two channels per lane when the chunk count is even, the row-block mapping divides and at
+  // least 3 ring slots still fit beside the larger row block; otherwise one.
+  for (c.cpl = nch % 2 == 0 ? 2 : 1; c.cpl >= 1; --c.cpl) {
+    c.nslots = 0;
+    if (lk_warps(c.cpl) % (nch / c.cpl) != 0) continue;
+    c.rb = lk_warps(c.cpl) / (nch / c.cpl);
+    c.slot_w_off = c.rb * nch * 32 * kSegD;
+    c.slot_elems = c.slot_w_off + (p.shared_w ? 0 : c.rb * nch * 32);
+    const size_t fixed = p.segl.blob.size() + 8 * (4 + 2 * kLkMaxSlots) +
+                         elem * (size_t(2) * c.rb * c.xy_elems + size_t(c.rb) * p.segl.psize +
+                                 size_t(kLkWarps) * kLkGy);
+    for (c.nslots = kLkMaxSlots; c.nslots >= 3; --c.nslots) {
+      c.smem = fixed + elem * size_t(c.nslots) * c.slot_elems;
+      if (c.smem <= 220 * 1024) break;
+    }
+    if (c.nslots >= 3) break;
   }
-  c.ok = c.nslots >= 3;
+  c.ok = c.cpl >= 1 && c.nslots >= 3;
 }
 
 // Convolutions whose instructions all have multiplicity 1 run one edge per lane.
@@ -1097,15 +1106,15 @@ int launch_lk(oeqb_plan& p, const Args<T>& a, cudaStream_t stream) {
   v.xy_elems = c.xy_elems;
   v.slot_elems = c.slot_elems;
   v.slot_w_off = c.slot_w_off;
-  const void* kernel = lk_kernel_ptr<T>();
+  const void* kernel = lk_kernel_ptr<T>(c.cpl);
   {
     std::lock_guard<std::mutex> g(p.mu);
     auto it = p.occ.find(kernel);
     if (it == p.occ.end()) {
       if (int rc = allow_max_smem(p.device, kernel)) return rc;
       int n = 0;
-      OEQB_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kernel, 32 * (kLkWarps + 1),
-                                                              c.smem));
+      OEQB_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(
+          &n, kernel, 32 * (lk_warps(c.cpl) + 1), c.smem));
       if (n <= 0) return fail(OEQB_ERR_UNSUPPORTED, "lockstep kernel does not fit on the device");
       p.occ.emplace(kernel, n);
     }
@@ -1113,8 +1122,8 @@ int launch_lk(oeqb_plan& p, const Args<T>& a, cudaStream_t stream) {
   const long long nblk = (a.nitems + c.rb - 1) / c.rb;
   const long long blocks = std::max<long long>(1, std::min<long long>(nblk, p.sm_count));
   void* params[] = {&v};
-  OEQB_CUDA(cudaLaunchKernel(kernel, dim3(static_cast<unsigned>(blocks)), dim3(32 * (kLkWarps + 1)),
-                             params, c.smem, stream));
+  OEQB_CUDA(cudaLaunchKernel(kernel, dim3(static_cast<unsigned>(blocks)),
+                             dim3(32 * (lk_warps(c.cpl) + 1)), params, c.smem, stream));
   return 0;
 }
 

@@ -23,7 +23,7 @@ const void* row_kernel_ptr(int kind, int nwarps);
 template <class T>
 const void* seg_kernel_ptr(int kind);
 template <class T>
-const void* lk_kernel_ptr();
+const void* lk_kernel_ptr(int cpl);  // cpl = channels per lane (1 or 2)
 // Edge-per-lane convolution for multiplicity-1 problems (tp_kernels_edge.cuh); kind 0/1 =
 // forward/backward, 2/3 = the single-path variants, 4/5/6 = single-path deterministic
 // forward, backward pass A (messages to the workspace) and pass B (sender-ordered sums).
@@ -57,7 +57,9 @@ const void* edge_kernel_ptr(int kind);
     return kind == 0 ? (const void*)tp_fwd_seg<T> : (const void*)tp_bwd_seg<T, 16>; \
   }                                                                               \
   template <>                                                                     \
-  const void* lk_kernel_ptr<T>() { return (const void*)tp_bwd_lk<T>; }            \
+  const void* lk_kernel_ptr<T>(int cpl) {                                        \
+    return cpl == 2 ? (const void*)tp_bwd_lk<T, 2> : (const void*)tp_bwd_lk<T, 1>; \
+  }                                                                               \
   template <>                                                                     \
   const void* edge_kernel_ptr<T>(int kind) {                                      \
     switch (kind) {                                                               \

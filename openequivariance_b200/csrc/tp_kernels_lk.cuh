@@ -4,10 +4,13 @@
 // is built once in shared memory, and for channel u of instruction n
 //     h_i = sum_k P[i][k] gz[u][k];  dX[u][i] += w[u] h_i;  dW[u] = sum_i x[u][i] h_i;
 //     dY[j] += w[u] pw sum_(i,k) c_ijk x[u][i] gz[u][k].
-// Work mapping: a CTA takes RB rows at a time and its 16 warps are (row, 32-channel chunk)
-// pairs (RB x NCH = 16).  Every warp walks the whole instruction list in the same order, so
-// all warps run the same code at the same time (one instruction-cache footprint, equal work,
-// no barrier imbalance), and each warp owns complete dX rows of its chunk (no partials).
+// Work mapping: a CTA takes RB rows at a time and its NW consumer warps (16; 12 with CPL = 2)
+// are (row, chunk) pairs, a chunk being 32 x CPL channels (lane l owns channels l, l + 32,
+// ...; RB x NCH / CPL = NW).  Every warp walks the whole instruction list in the same order,
+// so all warps run the same code at the same time (one instruction-cache footprint, equal
+// work, no barrier imbalance), and each warp owns complete dX rows of its chunk (no
+// partials).  With CPL = 2 one P block load, barrier wait and instruction decode serve two
+// channels.
 //
 // Data movement (warp-specialised): a 17th warp is the producer.  X and Y of the RB rows are
 // double-buffered at row-block granularity.  dZ and W are streamed per instruction through a
@@ -29,7 +32,11 @@
 
 namespace oeqb {
 
-constexpr int kLkWarps = 16;  // consumer warps; one producer warp more
+constexpr int kLkWarps = 16;  // largest consumer warp count; one producer warp more
+// Consumer warps for CPL channels per lane.  Registers are split per SM sub-partition, so 17
+// warps (5 on one quarter) cap a thread at 96 registers; two channels per lane need more, and
+// 12 + 1 warps (at most 4 per quarter) allow 128.
+__host__ __device__ constexpr int lk_warps(int cpl) { return cpl == 2 ? 12 : 16; }
 constexpr int kLkMaxSlots = 12;
 constexpr int kLkGy = (kLMaxUnrolled + 1) * (kLMaxUnrolled + 1);  // dY registers per lane
 
@@ -40,14 +47,16 @@ struct ArgsLk {
   int table_bytes;
   int off_run, off_grp, off_x, off_pent, off_term;
   int ninstr, nrun, npent, psize;
-  int nch, rb;                  // chunks per instruction, rows per block (nch * rb = 16)
+  int nch, rb;                  // 32-channel chunks per instruction, rows per block
+                                // (nch / CPL * rb = NW)
   int nslots;                   // ring slots
   int offY, xy_elems;           // X | Y row layout in the row buffer
   int slot_elems, slot_w_off;   // ring slot size; W part offset inside a slot
 };
 
+template <int NW>
 __device__ __forceinline__ void consumer_sync() {
-  asm volatile("bar.sync 1, %0;\n" ::"n"(kLkWarps * 32) : "memory");
+  asm volatile("bar.sync 1, %0;\n" ::"n"(NW * 32) : "memory");
 }
 
 template <class T>
@@ -108,8 +117,9 @@ __device__ __forceinline__ void lk_load_rows(const ArgsLk<T>& v, const SmemLk<T>
   }
 }
 
-template <class T>
-__global__ void __launch_bounds__((kLkWarps + 1) * 32, 1) tp_bwd_lk(const ArgsLk<T> v) {
+template <class T, int CPL>
+__global__ void __launch_bounds__((lk_warps(CPL) + 1) * 32, 1) tp_bwd_lk(const ArgsLk<T> v) {
+  constexpr int NW = lk_warps(CPL);
   extern __shared__ __align__(16) unsigned char smem[];
   const Args<T>& a = v.a;
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
@@ -136,11 +146,11 @@ __global__ void __launch_bounds__((kLkWarps + 1) * 32, 1) tp_bwd_lk(const ArgsLk
     if (threadIdx.x == 0) {
       for (int i = 0; i < 2; ++i) {
         mbar_init(&s.row_bar[i], 1);
-        mbar_init(&s.row_emp[i], kLkWarps);
+        mbar_init(&s.row_emp[i], NW);
       }
       for (int i = 0; i < kLkMaxSlots; ++i) {
         mbar_init(&s.slot_bar[i], 1);
-        mbar_init(&s.slot_emp[i], kLkWarps);
+        mbar_init(&s.slot_emp[i], NW);
       }
       fence_mbar_init();
     }
@@ -148,7 +158,7 @@ __global__ void __launch_bounds__((kLkWarps + 1) * 32, 1) tp_bwd_lk(const ArgsLk
   }
   const long long B = a.nitems;
   const long long nblk = (B + v.rb - 1) / v.rb;
-  if (wid == kLkWarps) {
+  if (wid == NW) {
     // Producer warp: row blocks and ring slots in consumption order.
     if (blockIdx.x < nblk) {
       const int myblk = static_cast<int>((nblk - blockIdx.x + gridDim.x - 1) / gridDim.x);
@@ -184,8 +194,9 @@ __global__ void __launch_bounds__((kLkWarps + 1) * 32, 1) tp_bwd_lk(const ArgsLk
     }
     return;
   }
-  const int r = wid / v.nch, c = wid - r * v.nch;  // this warp's row in the block and chunk
-  const int ch = c * 32 + lane;
+  const int nchw = v.nch / CPL;                       // warps per row
+  const int r = wid / nchw, c = wid - r * nchw;       // this warp's row in the block and chunk
+  const int ch = c * 32 * CPL + lane;                 // first channel; then + 32, ...
   // Loop invariants in registers: after the barrier waits (asm with memory clobbers) the
   // compiler would otherwise reload these kernel parameters from the constant bank per path.
   const int nslots = v.nslots;
@@ -210,7 +221,7 @@ __global__ void __launch_bounds__((kLkWarps + 1) * 32, 1) tp_bwd_lk(const ArgsLk
     mbar_wait(&s.row_bar[b], (k >> 1) & 1, a.status);
     const T* xyb = s.rowbuf + static_cast<size_t>(b) * v.rb * v.xy_elems;
     // P blocks of the block's rows.
-    for (int e = threadIdx.x; e < v.npent * nr; e += kLkWarps * 32) {
+    for (int e = threadIdx.x; e < v.npent * nr; e += NW * 32) {
       const int rr = e / v.npent, q = e - rr * v.npent;
       const SegPEnt pe = s.pent[q];
       const T* y = xyb + rr * v.xy_elems + v.offY;
@@ -219,7 +230,7 @@ __global__ void __launch_bounds__((kLkWarps + 1) * 32, 1) tp_bwd_lk(const ArgsLk
       for (int tt = t0; tt < t0 + nt; ++tt) acc += s.term[tt].c * y[s.term[tt].j];
       s.P[rr * v.psize + pe.dst] = acc;
     }
-    consumer_sync();
+    consumer_sync<NW>();
     T gy[kLkGy];
 #pragma unroll
     for (int j = 0; j < kLkGy; ++j) gy[j] = T(0);
@@ -232,13 +243,15 @@ __global__ void __launch_bounds__((kLkWarps + 1) * 32, 1) tp_bwd_lk(const ArgsLk
       const SegRun run = s.runs[q];
       dispatch_l(run.l1, [&]<int A>() {
         constexpr int D1 = 2 * A + 1;
-        T x[D1], gx[D1];
+        T x[CPL][D1], gx[CPL][D1];
         const T* xs = xr + run.x_off + ch * D1;
 #pragma unroll
-        for (int i = 0; i < D1; ++i) {
-          x[i] = active ? xs[i] : T(0);
-          gx[i] = T(0);
-        }
+        for (int q = 0; q < CPL; ++q)
+#pragma unroll
+          for (int i = 0; i < D1; ++i) {
+            x[q][i] = active ? xs[q * 32 * D1 + i] : T(0);
+            gx[q][i] = T(0);
+          }
         for (int n = run.n0; n < run.n1; ++n) {
           mbar_wait(&slot_bar[slot], par, status);
           const SegInstr in = insv[n];
@@ -248,29 +261,38 @@ __global__ void __launch_bounds__((kLkWarps + 1) * 32, 1) tp_bwd_lk(const ArgsLk
               constexpr int D2 = 2 * Bd + 1, D3 = 2 * C + 1;
               T P[seg_vpad<T>(D1 * D3)];
               lds_vec(P, Pr + in.p_off);
-              T gz[D3];
+              T gz[CPL][D3], w[CPL];
               const T* gs = sl + gz_base + ch * D3;
 #pragma unroll
-              for (int kk = 0; kk < D3; ++kk) gz[kk] = gs[kk];
-              const T w = shared_w ? Wg[in.w_off + ch] : sl[w_base];
-              T sdot = T(0);
+              for (int q = 0; q < CPL; ++q) {
 #pragma unroll
-              for (int i = 0; i < D1; ++i) {
-                T h = T(0);
-#pragma unroll
-                for (int kk = 0; kk < D3; ++kk) h += P[i * D3 + kk] * gz[kk];
-                gx[i] += w * h;
-                sdot += x[i] * h;
+                for (int kk = 0; kk < D3; ++kk) gz[q][kk] = gs[q * 32 * D3 + kk];
+                w[q] = shared_w ? Wg[in.w_off + ch + 32 * q] : sl[w_base + 32 * q];
               }
-              if (shared_w)
-                atomic_add(dwrow + in.w_off + ch, sdot);
-              else
-                dwrow[in.w_off + ch] = sdot;
-              T e[D2];
-              CG<A, Bd, C>::evec(gz, x, e);
-              const T wp = w * T(in.pw);
 #pragma unroll
-              for (int j = 0; j < D2; ++j) gy[Bd * Bd + j] += wp * e[j];
+              for (int q = 0; q < CPL; ++q) {
+                T sdot = T(0);
+#pragma unroll
+                for (int i = 0; i < D1; ++i) {
+                  T h = T(0);
+#pragma unroll
+                  for (int kk = 0; kk < D3; ++kk) h += P[i * D3 + kk] * gz[q][kk];
+                  gx[q][i] += w[q] * h;
+                  sdot += x[q][i] * h;
+                }
+                if (shared_w)
+                  atomic_add(dwrow + in.w_off + ch + 32 * q, sdot);
+                else
+                  dwrow[in.w_off + ch + 32 * q] = sdot;
+              }
+#pragma unroll
+              for (int q = 0; q < CPL; ++q) {
+                T e[D2];
+                CG<A, Bd, C>::evec(gz[q], x[q], e);
+                const T wp = w[q] * T(in.pw);
+#pragma unroll
+                for (int j = 0; j < D2; ++j) gy[Bd * Bd + j] += wp * e[j];
+              }
             });
           }
           __syncwarp();
@@ -285,7 +307,9 @@ __global__ void __launch_bounds__((kLkWarps + 1) * 32, 1) tp_bwd_lk(const ArgsLk
         if (active) {
           T* dst = a.out0 + row * a.L1dim + run.x_off + ch * D1;
 #pragma unroll
-          for (int i = 0; i < D1; ++i) dst[i] = gx[i];
+          for (int q = 0; q < CPL; ++q)
+#pragma unroll
+            for (int i = 0; i < D1; ++i) dst[q * 32 * D1 + i] = gx[q][i];
         }
       });
     }
@@ -316,14 +340,14 @@ __global__ void __launch_bounds__((kLkWarps + 1) * 32, 1) tp_bwd_lk(const ArgsLk
       h1 += __shfl_xor_sync(0xffffffffu, h1, 1);
       if ((lane & 1) == 0) s.gys[wid * kLkGy + (lane >> 1)] = h1;
     }
-    consumer_sync();
+    consumer_sync<NW>();
     // Row buffer b and P are free (the producer refills b for the block after next).
     if (lane == 0) mbar_arrive(&s.row_emp[b]);
     // dY of the block's rows: the row's chunk warps in order.
-    for (int task = threadIdx.x; task < nr * a.L2dim; task += kLkWarps * 32) {
+    for (int task = threadIdx.x; task < nr * a.L2dim; task += NW * 32) {
       const int rr = task / a.L2dim, j = task - rr * a.L2dim;
       T acc = T(0);
-      for (int cc = 0; cc < v.nch; ++cc) acc += s.gys[(rr * v.nch + cc) * kLkGy + j];
+      for (int cc = 0; cc < nchw; ++cc) acc += s.gys[(rr * nchw + cc) * kLkGy + j];
       a.out1[(row0 + rr) * a.L2dim + j] = acc;
     }
   }
