@@ -301,9 +301,11 @@ int blob_put(std::vector<unsigned char>& blob, const std::vector<V>& v) {
 
 // Builds the table image of one segment-kernel pass.  `order` lists the instructions sorted
 // by X irrep; `bounds` splits it into contiguous groups (backward units; one group forward).
+// P block of an instruction: D1 x D3 packed (row_pad false) or with each row padded to a
+// multiple of 4 values, so that every row starts 16-byte aligned (row_pad true).
 template <class T>
 void seg_tables(const oeqb_plan& p, const std::vector<int>& order, const std::vector<int>& bounds,
-                oeqb_plan::SegTable& t) {
+                oeqb_plan::SegTable& t, bool row_pad = false) {
   std::vector<SegInstr> ins;
   std::vector<SegRun> runs;
   std::vector<int> grp;
@@ -331,13 +333,15 @@ void seg_tables(const oeqb_plan& p, const std::vector<int>& order, const std::ve
       const CGEntry& c = p.cg[e];
       cell[size_t(c.i) * r3.dim + c.k].push_back({si.y_off + c.j, in.pw * c.c});
     }
+    const int rstride = row_pad ? (r3.dim + 3) / 4 * 4 : r3.dim;
     for (size_t q = 0; q < cell.size(); ++q) {
       if (cell[q].empty()) continue;
-      pent.push_back(SegPEnt{poff + static_cast<int>(q),
+      const int i = static_cast<int>(q) / r3.dim, k = static_cast<int>(q) % r3.dim;
+      pent.push_back(SegPEnt{poff + i * rstride + k,
                              (static_cast<int>(term.size()) << 8) | static_cast<int>(cell[q].size())});
       for (auto& tj : cell[q]) term.push_back(SegTerm<T>{T(tj.second), tj.first});
     }
-    poff += (r1.dim * r3.dim + 3) / 4 * 4;
+    poff += (r1.dim * rstride + 3) / 4 * 4;
   }
   // Runs: maximal pieces of a group with one X irrep.  Groups are contiguous pieces of the
   // X-sorted list, so the runs of one X irrep are consecutive in the run table.
@@ -501,9 +505,9 @@ void build_lk(oeqb_plan& p) {
   });
   const int n = static_cast<int>(order.size());
   if (p.dtype == 2)
-    seg_tables<double>(p, order, {0, n}, p.segl);
+    seg_tables<double>(p, order, {0, n}, p.segl, true);
   else
-    seg_tables<float>(p, order, {0, n}, p.segl);
+    seg_tables<float>(p, order, {0, n}, p.segl, true);
   const size_t elem = p.dtype == 2 ? 8 : 4;
   oeqb_plan::LkCfg& c = p.lk;
   c.nch = nch;

@@ -1,7 +1,8 @@
 // Lockstep channelwise-uvu backward (BASELINE C2 shape, uniform multiplicities).
 //
 // Same mathematics as tp_bwd_seg (tp_kernels_seg.cuh): per row, P[i][k] = pw sum_j c_ijk y_j
-// is built once in shared memory, and for channel u of instruction n
+// is built once in shared memory (each row i padded to a multiple of 4 values), and for
+// channel u of instruction n
 //     h_i = sum_k P[i][k] gz[u][k];  dX[u][i] += w[u] h_i;  dW[u] = sum_i x[u][i] h_i;
 //     dY[j] += w[u] pw sum_(i,k) c_ijk x[u][i] gz[u][k].
 // Work mapping: a CTA takes RB rows at a time and its NW consumer warps (16; 12 with CPL = 2)
@@ -259,8 +260,6 @@ __global__ void __launch_bounds__((lk_warps(CPL) + 1) * 32, 1) tp_bwd_lk(const A
           if (active) {
             dispatch_bc<A>(in.bc, [&]<int Bd, int C>() {
               constexpr int D2 = 2 * Bd + 1, D3 = 2 * C + 1;
-              T P[seg_vpad<T>(D1 * D3)];
-              lds_vec(P, Pr + in.p_off);
               T gz[CPL][D3], w[CPL];
               const T* gs = sl + gz_base + ch * D3;
 #pragma unroll
@@ -269,21 +268,30 @@ __global__ void __launch_bounds__((lk_warps(CPL) + 1) * 32, 1) tp_bwd_lk(const A
                 for (int kk = 0; kk < D3; ++kk) gz[q][kk] = gs[q * 32 * D3 + kk];
                 w[q] = shared_w ? Wg[in.w_off + ch + 32 * q] : sl[w_base + 32 * q];
               }
+              // P rows are padded to R3 values (16-byte aligned): one row live at a time.
+              constexpr int R3 = seg_vpad<T>(D3);
+              T sdot[CPL];
 #pragma unroll
-              for (int q = 0; q < CPL; ++q) {
-                T sdot = T(0);
+              for (int q = 0; q < CPL; ++q) sdot[q] = T(0);
 #pragma unroll
-                for (int i = 0; i < D1; ++i) {
+              for (int i = 0; i < D1; ++i) {
+                T Pi[R3];
+                lds_vec(Pi, Pr + in.p_off + i * R3);
+#pragma unroll
+                for (int q = 0; q < CPL; ++q) {
                   T h = T(0);
 #pragma unroll
-                  for (int kk = 0; kk < D3; ++kk) h += P[i * D3 + kk] * gz[q][kk];
+                  for (int kk = 0; kk < D3; ++kk) h += Pi[kk] * gz[q][kk];
                   gx[q][i] += w[q] * h;
-                  sdot += x[q][i] * h;
+                  sdot[q] += x[q][i] * h;
                 }
+              }
+#pragma unroll
+              for (int q = 0; q < CPL; ++q) {
                 if (shared_w)
-                  atomic_add(dwrow + in.w_off + ch + 32 * q, sdot);
+                  atomic_add(dwrow + in.w_off + ch + 32 * q, sdot[q]);
                 else
-                  dwrow[in.w_off + ch + 32 * q] = sdot;
+                  dwrow[in.w_off + ch + 32 * q] = sdot[q];
               }
 #pragma unroll
               for (int q = 0; q < CPL; ++q) {
