@@ -40,6 +40,8 @@ const void* seg_kernel_ptr(int kind);
 template <class T>
 const void* lk_kernel_ptr(int cpl);
 template <class T>
+const void* lkf_kernel_ptr(int cpl);
+template <class T>
 const void* edge_kernel_ptr(int kind);
 const void* uvw_tc_kernel_ptr(int kind);
 template <class T>
@@ -125,7 +127,7 @@ struct oeqb_plan {
     int nch = 0, cpl = 1, rb = 0, nslots = 0, offY = 0, xy_elems = 0, slot_elems = 0,
         slot_w_off = 0;
     size_t smem = 0;
-  } lk;
+  } lk, lkf;  // backward, forward
   // Edge-per-lane convolution (tp_kernels_edge.cuh) for multiplicity-1 problems; edge1 = the
   // single-path variant (one instruction whose irreps are the whole rows).
   bool edge_ok = false;
@@ -481,6 +483,7 @@ void build_seg(oeqb_plan& p) {
 // channels per lane (a warp covers 64 channels) on 12 consumer warps where they divide.
 void build_lk(oeqb_plan& p) {
   p.lk = {};
+  p.lkf = {};
   p.segl = {};
   if (!p.segb.ok || p.dtype != 1) return;  // fp64 operands do not fit the register budget
   if (p.ir2.size() > static_cast<size_t>(kLMaxUnrolled) + 1) return;
@@ -531,6 +534,27 @@ void build_lk(oeqb_plan& p) {
     if (c.nslots >= 3) break;
   }
   c.ok = c.cpl >= 1 && c.nslots >= 3;
+  // Lockstep forward (every output irrep written by one instruction: the segment forward's
+  // condition): 16 consumer warps, a ring of W segments, two Z staging buffers per warp.
+  if (!p.segf.ok) return;
+  oeqb_plan::LkCfg& f = p.lkf;
+  f = {};
+  f.nch = nch;
+  f.offY = c.offY;
+  f.xy_elems = c.xy_elems;
+  f.cpl = nch % 2 == 0 && kLfWarps % (nch / 2) == 0 ? 2 : 1;
+  if (kLfWarps % (nch / f.cpl) != 0) return;
+  f.rb = kLfWarps / (nch / f.cpl);
+  f.slot_w_off = 0;
+  f.slot_elems = p.shared_w ? 0 : f.rb * nch * 32;
+  const size_t ffixed = p.segl.blob.size() + 8 * (4 + 2 * kLkMaxSlots) +
+                        elem * (size_t(2) * f.rb * f.xy_elems + size_t(f.rb) * p.segl.psize +
+                                size_t(kLfWarps) * 2 * f.cpl * 32 * kSegD);
+  for (f.nslots = kLkMaxSlots; f.nslots >= 3; --f.nslots) {
+    f.smem = ffixed + elem * size_t(f.nslots) * f.slot_elems;
+    if (f.smem <= 220 * 1024) break;
+  }
+  f.ok = f.nslots >= 3;
 }
 
 // Convolutions whose instructions all have multiplicity 1 run one edge per lane.
@@ -1086,10 +1110,12 @@ int launch_seg(oeqb_plan& p, int kind, const Args<T>& a, cudaStream_t stream) {
   return 0;
 }
 
+// fwd = true: the lockstep forward (tp_fwd_lk), else the backward (tp_bwd_lk).
 template <class T>
-int launch_lk(oeqb_plan& p, const Args<T>& a, cudaStream_t stream) {
+int launch_lk(oeqb_plan& p, const Args<T>& a, cudaStream_t stream, bool fwd = false) {
   const oeqb_plan::SegTable& t = p.segl;
-  const oeqb_plan::LkCfg& c = p.lk;
+  const oeqb_plan::LkCfg& c = fwd ? p.lkf : p.lk;
+  const int nwarps = fwd ? kLfWarps : lk_warps(c.cpl);
   ArgsLk<T> v;
   v.a = a;
   v.tables = p.dmem + t.dev_off;
@@ -1110,7 +1136,7 @@ int launch_lk(oeqb_plan& p, const Args<T>& a, cudaStream_t stream) {
   v.xy_elems = c.xy_elems;
   v.slot_elems = c.slot_elems;
   v.slot_w_off = c.slot_w_off;
-  const void* kernel = lk_kernel_ptr<T>(c.cpl);
+  const void* kernel = fwd ? lkf_kernel_ptr<T>(c.cpl) : lk_kernel_ptr<T>(c.cpl);
   {
     std::lock_guard<std::mutex> g(p.mu);
     auto it = p.occ.find(kernel);
@@ -1118,7 +1144,7 @@ int launch_lk(oeqb_plan& p, const Args<T>& a, cudaStream_t stream) {
       if (int rc = allow_max_smem(p.device, kernel)) return rc;
       int n = 0;
       OEQB_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(
-          &n, kernel, 32 * (lk_warps(c.cpl) + 1), c.smem));
+          &n, kernel, 32 * (nwarps + 1), c.smem));
       if (n <= 0) return fail(OEQB_ERR_UNSUPPORTED, "lockstep kernel does not fit on the device");
       p.occ.emplace(kernel, n);
     }
@@ -1127,7 +1153,7 @@ int launch_lk(oeqb_plan& p, const Args<T>& a, cudaStream_t stream) {
   const long long blocks = std::max<long long>(1, std::min<long long>(nblk, p.sm_count));
   void* params[] = {&v};
   OEQB_CUDA(cudaLaunchKernel(kernel, dim3(static_cast<unsigned>(blocks)),
-                             dim3(32 * (lk_warps(c.cpl) + 1)), params, c.smem, stream));
+                             dim3(32 * (nwarps + 1)), params, c.smem, stream));
   return 0;
 }
 
@@ -1433,6 +1459,7 @@ int tp_forward_t(oeqb_plan* p, int64_t B, const void* X, const void* Y, const vo
   } else {
     if (p->sw.ok && aligned16(W)) return launch_uvw_sw_fwd(*p, a, s);
   }
+  if (p->lkf.ok && lk_aligned(*p, a)) return launch_lk(*p, a, s, true);
   if (p->segf.ok) return launch_seg(*p, 0, a, s);
   if (p->row_ok) return launch_row(*p, 0, a, s);
   return launch(*p, batch_kernel_ptr<T>(0, p->uvw, false, kBatch), a, true, false, s);
@@ -1760,6 +1787,7 @@ int oeqb_tp_forward_noalloc(const void* descriptor, size_t nbytes, int device, i
   p.segb = {};
   p.segl = {};
   p.lk = {};
+  p.lkf = {};
   std::vector<unsigned char> img;
   layout_tables(p, img);
   const size_t status_off = align16(img.size());

@@ -24,6 +24,8 @@ template <class T>
 const void* seg_kernel_ptr(int kind);
 template <class T>
 const void* lk_kernel_ptr(int cpl);  // cpl = channels per lane (1 or 2)
+template <class T>
+const void* lkf_kernel_ptr(int cpl);  // lockstep forward
 // Edge-per-lane convolution for multiplicity-1 problems (tp_kernels_edge.cuh); kind 0/1 =
 // forward/backward, 2/3 = the single-path variants, 4/5/6 = single-path deterministic
 // forward, backward pass A (messages to the workspace) and pass B (sender-ordered sums).
@@ -59,6 +61,10 @@ const void* edge_kernel_ptr(int kind);
   template <>                                                                     \
   const void* lk_kernel_ptr<T>(int cpl) {                                        \
     return cpl == 2 ? (const void*)tp_bwd_lk<T, 2> : (const void*)tp_bwd_lk<T, 1>; \
+  }                                                                               \
+  template <>                                                                     \
+  const void* lkf_kernel_ptr<T>(int cpl) {                                        \
+    return cpl == 2 ? (const void*)tp_fwd_lk<T, 2> : (const void*)tp_fwd_lk<T, 1>; \
   }                                                                               \
   template <>                                                                     \
   const void* edge_kernel_ptr<T>(int kind) {                                      \

@@ -361,4 +361,211 @@ __global__ void __launch_bounds__((lk_warps(CPL) + 1) * 32, 1) tp_bwd_lk(const A
   }
 }
 
+
+// ---------------------------------------------------------------------------------------
+// Lockstep channelwise-uvu forward (same problem class, every output irrep written by exactly
+// one instruction).  Per row and instruction n, for channel u:
+//     Z[u][k] = w[u] sum_i x[u][i] P[i][k],  P[i][k] = pw sum_j c_ijk y_j.
+// Work mapping as in tp_bwd_lk: 16 consumer warps are (row, chunk of 32 x CPL channels)
+// pairs walking the instruction list in the same order; a 17th warp is the producer.  X and Y
+// are double-buffered per row block, the instruction's W segment of every row of the block
+// streams through a ring of slots.  A warp's Z segment (32 x CPL channels x d3, contiguous in
+// the row) is staged in shared memory (two buffers per warp) and written by one bulk store.
+constexpr int kLfWarps = 16;
+
+template <class T>
+__device__ __forceinline__ void lf_fill(const ArgsLk<T>& v, const SmemLk<T>& s, int n, int slot,
+                                        long long row0, int nr, int lane) {
+  const Args<T>& a = v.a;
+  const unsigned wb = a.shared_w ? 0u : static_cast<unsigned>(v.nch * 32 * sizeof(T));
+  if (lane == 0) mbar_expect_tx(&s.slot_bar[slot], nr * wb);
+  __syncwarp();
+  if (wb != 0 && lane < nr) {
+    const long long row = row0 + lane;
+    bulk_g2s(s.ring + static_cast<size_t>(slot) * v.slot_elems + lane * v.nch * 32,
+             a.W + row * a.wnumel + s.ins[n].w_off, wb, &s.slot_bar[slot]);
+  }
+}
+
+template <class T, int CPL>
+__global__ void __launch_bounds__((kLfWarps + 1) * 32, 1) tp_fwd_lk(const ArgsLk<T> v) {
+  constexpr int NW = kLfWarps, ZSLOT = CPL * 32 * kSegD;
+  extern __shared__ __align__(16) unsigned char smem[];
+  const Args<T>& a = v.a;
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  SmemLk<T> s;
+  T* zst;  // [NW][2][ZSLOT] Z staging
+  {
+    const uint4* src = reinterpret_cast<const uint4*>(v.tables);
+    uint4* dst = reinterpret_cast<uint4*>(smem);
+    for (int i = threadIdx.x; i < v.table_bytes / 16; i += blockDim.x) dst[i] = src[i];
+    s.ins = reinterpret_cast<const SegInstr*>(smem);
+    s.runs = reinterpret_cast<const SegRun*>(smem + v.off_run);
+    s.pent = reinterpret_cast<const SegPEnt*>(smem + v.off_pent);
+    s.term = reinterpret_cast<const SegTerm<T>*>(smem + v.off_term);
+    unsigned char* p = smem + v.table_bytes;
+    s.row_bar = reinterpret_cast<unsigned long long*>(p);
+    s.row_emp = s.row_bar + 2;
+    s.slot_bar = s.row_emp + 2;
+    s.slot_emp = s.slot_bar + kLkMaxSlots;
+    p += 8 * (4 + 2 * kLkMaxSlots);
+    s.rowbuf = reinterpret_cast<T*>(p);
+    s.ring = s.rowbuf + static_cast<size_t>(2) * v.rb * v.xy_elems;
+    s.P = s.ring + static_cast<size_t>(v.nslots) * v.slot_elems;
+    s.gys = nullptr;
+    zst = s.P + static_cast<size_t>(v.rb) * v.psize;
+    for (int i = threadIdx.x; i < v.rb * v.psize; i += blockDim.x) s.P[i] = T(0);
+    if (threadIdx.x == 0) {
+      for (int i = 0; i < 2; ++i) {
+        mbar_init(&s.row_bar[i], 1);
+        mbar_init(&s.row_emp[i], NW);
+      }
+      for (int i = 0; i < kLkMaxSlots; ++i) {
+        mbar_init(&s.slot_bar[i], 1);
+        mbar_init(&s.slot_emp[i], NW);
+      }
+      fence_mbar_init();
+    }
+    __syncthreads();
+  }
+  const long long B = a.nitems;
+  const long long nblk = (B + v.rb - 1) / v.rb;
+  if (wid == NW) {
+    // Producer warp: row blocks and W slots in consumption order.
+    if (blockIdx.x < nblk) {
+      const int myblk = static_cast<int>((nblk - blockIdx.x + gridDim.x - 1) / gridDim.x);
+      auto rows_of = [&](int kb, long long* row0) {
+        *row0 = (blockIdx.x + static_cast<long long>(kb) * gridDim.x) * v.rb;
+        return static_cast<int>(min(static_cast<long long>(v.rb), B - *row0));
+      };
+      long long row0;
+      int nr = rows_of(0, &row0);
+      lk_load_rows(v, s, 0, row0, nr, lane);
+      if (myblk > 1) {
+        long long r1;
+        const int n1 = rows_of(1, &r1);
+        lk_load_rows(v, s, 1, r1, n1, lane);
+      }
+      int slot = 0, wrap = 0;
+      for (int kb = 0; kb < myblk; ++kb) {
+        nr = rows_of(kb, &row0);
+        if (kb >= 2) {
+          mbar_wait(&s.row_emp[kb & 1], ((kb >> 1) - 1) & 1, a.status);
+          lk_load_rows(v, s, kb & 1, row0, nr, lane);
+        }
+        for (int n = 0; n < v.ninstr; ++n) {
+          if (wrap > 0) mbar_wait(&s.slot_emp[slot], (wrap - 1) & 1, a.status);
+          lf_fill(v, s, n, slot, row0, nr, lane);
+          if (++slot == v.nslots) {
+            slot = 0;
+            ++wrap;
+          }
+        }
+      }
+    }
+    return;
+  }
+  const int nchw = v.nch / CPL;                   // warps per row
+  const int r = wid / nchw, c = wid - r * nchw;   // this warp's row in the block and chunk
+  const int ch = c * 32 * CPL + lane;             // first channel; then + 32, ...
+  const int nslots = v.nslots;
+  const size_t slot_elems = static_cast<size_t>(v.slot_elems);
+  const int w_base = r * v.nch * 32 + ch;         // this lane's weight in a slot
+  const bool shared_w = a.shared_w != 0;
+  const T* __restrict__ Wg = a.W;
+  int* status = a.status;
+  const T* ring = s.ring;
+  unsigned long long* slot_bar = s.slot_bar;
+  unsigned long long* slot_emp = s.slot_emp;
+  const SegInstr* insv = s.ins;
+  T* const zst0 = zst + static_cast<size_t>(wid) * 2 * ZSLOT;
+  int sb = 0;
+  int slot = 0;
+  unsigned par = 0;
+  int k = 0;
+  for (long long blk = blockIdx.x; blk < nblk; blk += gridDim.x, ++k) {
+    const int b = k & 1;
+    const long long row0 = blk * v.rb;
+    const int nr = static_cast<int>(min(static_cast<long long>(v.rb), B - row0));
+    mbar_wait(&s.row_bar[b], (k >> 1) & 1, a.status);
+    const T* xyb = s.rowbuf + static_cast<size_t>(b) * v.rb * v.xy_elems;
+    for (int e = threadIdx.x; e < v.npent * nr; e += NW * 32) {
+      const int rr = e / v.npent, q = e - rr * v.npent;
+      const SegPEnt pe = s.pent[q];
+      const T* y = xyb + rr * v.xy_elems + v.offY;
+      const int t0 = pe.t0nt >> 8, nt = pe.t0nt & 255;
+      T acc = T(0);
+      for (int tt = t0; tt < t0 + nt; ++tt) acc += s.term[tt].c * y[s.term[tt].j];
+      s.P[rr * v.psize + pe.dst] = acc;
+    }
+    consumer_sync<NW>();
+    const bool active = r < nr;
+    const long long row = row0 + r;
+    const T* xr = xyb + r * v.xy_elems;
+    const T* Pr = s.P + r * v.psize;
+    T* zrow = a.out0 + row * a.L3dim;
+    for (int q = 0; q < v.nrun; ++q) {
+      const SegRun run = s.runs[q];
+      dispatch_l(run.l1, [&]<int A>() {
+        constexpr int D1 = 2 * A + 1;
+        T x[CPL][D1];
+        const T* xs = xr + run.x_off + ch * D1;
+#pragma unroll
+        for (int cq = 0; cq < CPL; ++cq)
+#pragma unroll
+          for (int i = 0; i < D1; ++i) x[cq][i] = active ? xs[cq * 32 * D1 + i] : T(0);
+        for (int n = run.n0; n < run.n1; ++n) {
+          mbar_wait(&slot_bar[slot], par, status);
+          const SegInstr in = insv[n];
+          const T* sl = ring + static_cast<size_t>(slot) * slot_elems;
+          if (active) {
+            dispatch_l(in.l3, [&]<int C>() {
+              constexpr int D3 = 2 * C + 1, R3 = seg_vpad<T>(D3);
+              T w[CPL], z[CPL][D3];
+#pragma unroll
+              for (int cq = 0; cq < CPL; ++cq) {
+                w[cq] = shared_w ? Wg[in.w_off + ch + 32 * cq] : sl[w_base + 32 * cq];
+#pragma unroll
+                for (int kk = 0; kk < D3; ++kk) z[cq][kk] = T(0);
+              }
+#pragma unroll
+              for (int i = 0; i < D1; ++i) {
+                T Pi[R3];
+                lds_vec(Pi, Pr + in.p_off + i * R3);
+#pragma unroll
+                for (int cq = 0; cq < CPL; ++cq)
+#pragma unroll
+                  for (int kk = 0; kk < D3; ++kk) z[cq][kk] += x[cq][i] * Pi[kk];
+              }
+              T* stage = zst0 + sb * ZSLOT;
+              sb ^= 1;
+              bulk_wait_read<1>();  // the store that last used this buffer has read it
+              __syncwarp();
+#pragma unroll
+              for (int cq = 0; cq < CPL; ++cq)
+#pragma unroll
+                for (int kk = 0; kk < D3; ++kk)
+                  stage[(cq * 32 + lane) * D3 + kk] = z[cq][kk] * w[cq];
+              fence_async_smem();
+              __syncwarp();
+              bulk_store_leader(lane == 0, zrow + in.z_off + c * 32 * CPL * D3, stage,
+                                CPL * 32 * D3 * sizeof(T));
+            });
+          }
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&slot_emp[slot]);
+          if (++slot == nslots) {
+            slot = 0;
+            par ^= 1u;
+          }
+        }
+      });
+    }
+    // P is rebuilt for the next block only after every warp has finished with it.
+    consumer_sync<NW>();
+    if (lane == 0) mbar_arrive(&s.row_emp[b]);
+  }
+  bulk_wait_all<0>();  // every Z store has completed before the CTA exits
+}
+
 }  // namespace oeqb

@@ -153,9 +153,10 @@ def _kernel_names(fn):
 
 
 @pytest.mark.parametrize("name", ["tp_c2_literal.npz", "tp_mace_medium_shared.npz"])
-def test_lockstep_backward_many_rows(name, cuda_device):
-    """The C2-shape backward over 997 rows (ragged for every row-block size), so the kernel's
-    ring of dZ/W slots wraps many times and both row buffers are reused, vs the fp64 oracle."""
+def test_lockstep_many_rows(name, cuda_device):
+    """The C2-shape forward and backward over 997 rows (ragged for every row-block size), so
+    the kernels' rings of W / dZ slots wrap many times and both row buffers are reused, vs the
+    fp64 oracle."""
     g = load_golden(name)
     p = oracle_problem(g)
     dtype = np.float32
@@ -170,6 +171,13 @@ def test_lockstep_backward_many_rows(name, cuda_device):
     W = rng.normal(size=(int(g["weight_numel"]),) if shared else (B, int(g["weight_numel"])))
     G = rng.normal(size=(B, g["Z"].shape[1]))
     gX, gY, gW = O.backward(p, X, Y, W[..., inv], G)
+    Zref = O.forward(p, X, Y, W[..., inv])
+    xs, ys, ws = to_dev(X, dtype), to_dev(Y, dtype), to_dev(W, dtype)
+    out = {}
+    names = _kernel_names(lambda: out.update(Z=tp(xs, ys, ws)))
+    if name == "tp_c2_literal.npz":
+        assert any("tp_fwd_lk" in n for n in names), sorted(names)
+    assert_close(out["Z"], Zref, dtype, "Z")
     x = to_dev(X, dtype).requires_grad_()
     y = to_dev(Y, dtype).requires_grad_()
     w = to_dev(W, dtype).requires_grad_()
