@@ -46,6 +46,9 @@ def _args():
     ap.add_argument("--sc-nodes", type=int, default=100000)
     ap.add_argument("--rows", type=int, default=50000)
     ap.add_argument("--e2e-steps", type=int, default=3)
+    ap.add_argument("--e2e-chunks", type=int, default=4,
+                    help="row chunks per e2e step, one CUDA stream each (copies in both "
+                         "directions overlap with each other and with the kernels)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     return ap.parse_args()
 
@@ -308,21 +311,44 @@ def bench_tp(args, world, rank, local):
     rows_total = B * world * K
     value = rows_total / (elapsed_ms * 1e-3)
 
-    # e2e: through the public module API with pinned host buffers.
+    # e2e: through the public module API with pinned host buffers.  Each step's rows are split
+    # into chunks, one CUDA stream per chunk: a chunk's host-to-device copies, its forward and
+    # backward, and its device-to-host copies run in order on its stream, so the copies of
+    # different chunks overlap in both directions (PCIe is full duplex).  Shared weights: each
+    # chunk's weight gradient is a partial sum; the step adds them on the device and reads the
+    # total back once.
     E = max(1, args.e2e_steps)
+    NC = max(1, min(args.e2e_chunks, B))
     hX, hY, hW, hG = (t.cpu().pin_memory() for t in (X, Y, W, G))
     outs_h = [torch.empty(B, d3).pin_memory(), torch.empty(B, d1).pin_memory(),
               torch.empty(B, d2).pin_memory(), torch.empty_like(hW).pin_memory()]
+    streams = [torch.cuda.Stream(dev) for _ in range(NC)]
+    cuts = [B * c // NC for c in range(NC + 1)]
 
     def e2e_step():
-        x = hX.to(dev, non_blocking=True).requires_grad_()
-        y = hY.to(dev, non_blocking=True).requires_grad_()
-        w = hW.to(dev, non_blocking=True).requires_grad_()
-        g = hG.to(dev, non_blocking=True)
-        z = tp(x, y, w)
-        z.backward(g)
-        for h, d in zip(outs_h, (z.detach(), x.grad, y.grad, w.grad)):
-            h.copy_(d, non_blocking=True)
+        main = torch.cuda.current_stream(dev)
+        parts = []
+        for c, st in enumerate(streams):
+            lo, hi = cuts[c], cuts[c + 1]
+            with torch.cuda.stream(st):
+                x = hX[lo:hi].to(dev, non_blocking=True).requires_grad_()
+                y = hY[lo:hi].to(dev, non_blocking=True).requires_grad_()
+                w = (hW if shared else hW[lo:hi]).to(dev, non_blocking=True).requires_grad_()
+                g = hG[lo:hi].to(dev, non_blocking=True)
+                z = tp(x, y, w)
+                z.backward(g)
+                for h, d in zip(outs_h[:3], (z.detach(), x.grad, y.grad)):
+                    h[lo:hi].copy_(d, non_blocking=True)
+                if shared:
+                    parts.append(w.grad)
+                else:
+                    outs_h[3][lo:hi].copy_(w.grad, non_blocking=True)
+        if shared:
+            for st in streams:
+                main.wait_stream(st)
+            for p in parts:
+                p.record_stream(main)
+            outs_h[3].copy_(torch.stack(parts).sum(0), non_blocking=True)
 
     e2e_step()
     torch.cuda.synchronize()
@@ -332,11 +358,12 @@ def bench_tp(args, world, rank, local):
         e2e_step()
     torch.cuda.synchronize()
     e2e_s = _max_over_ranks(time.perf_counter() - t0, world)
-    h2d = (hX.numel() + hY.numel() + hW.numel() + hG.numel()) * s
+    h2d = (hX.numel() + hY.numel() + hG.numel() + hW.numel() * (NC if shared else 1)) * s
     d2h = sum(h.numel() for h in outs_h) * s
     e2e = {"value": B * world * E / e2e_s, "unit": UNIT, "h2d_bytes_per_step": h2d,
            "d2h_bytes_per_step": d2h, "steps": E,
-           "path": "oeq.TensorProduct forward+backward (torch op API), pinned host buffers"}
+           "path": f"oeq.TensorProduct forward+backward (torch op API), pinned host buffers, "
+                   f"{NC} row chunks on {NC} CUDA streams per step"}
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
