@@ -375,6 +375,39 @@ struct E1Lane {
   bool valid;
 };
 
+// The index loads of a lane's edge, unchecked: the atomic kernels issue them one 32-edge block
+// ahead, so that only the dependent X / dZ row gathers wait on memory in each iteration.
+struct E1Raw {
+  long long e, row, col;
+};
+
+template <class T>
+__device__ __forceinline__ E1Raw e1_raw(const Args<T>& a, long long base, int lane) {
+  E1Raw r;
+  r.e = base + lane;
+  const bool v = r.e < a.nitems;
+  r.row = v ? a.rows[r.e] : -1;
+  r.col = v ? a.cols[r.e] : 0;
+  return r;
+}
+
+// Range check of the loaded indices (bad indices raise status 1 and drop the edge).
+template <class T>
+__device__ __forceinline__ E1Lane e1_check(const Args<T>& a, const E1Raw& r) {
+  E1Lane l;
+  l.e = r.e;
+  l.valid = r.e < a.nitems;
+  l.row = r.row;
+  l.col = r.col;
+  if (l.valid && (l.row < 0 || l.row >= a.nnodes || l.col < 0 || l.col >= a.nnodes)) {
+    flag(a.status, 1);
+    l.valid = false;
+    l.row = -1;
+    l.col = 0;
+  }
+  return l;
+}
+
 template <class T>
 __device__ __forceinline__ E1Lane e1_lane(const Args<T>& a, long long base, int lane) {
   E1Lane l;
@@ -441,9 +474,11 @@ __global__ void __launch_bounds__(kEdgeWarps * 32) conv_fwd_edge1(const Args<T> 
   dispatch_triple(p.code, [&]<int A, int B, int C>() {
     constexpr int D2 = 2 * B + 1, D3 = 2 * C + 1;
     T* ys = e1_warp_smem<T>(smem, 32 * D2);
-    for (long long base = (static_cast<long long>(blockIdx.x) * kEdgeWarps + (threadIdx.x >> 5)) * 32;
-         base < a.nitems; base += nw * 32) {
-      const E1Lane l = e1_lane(a, base, lane);
+    long long base = (static_cast<long long>(blockIdx.x) * kEdgeWarps + (threadIdx.x >> 5)) * 32;
+    E1Raw next = e1_raw(a, base, lane);
+    for (; base < a.nitems; base += nw * 32) {
+      const E1Lane l = e1_check(a, next);
+      next = e1_raw(a, base + nw * 32, lane);
       e1_stage_in<T, D2>(ys, a.Y, base, a.nitems, lane);
       __syncwarp();
       T z[D3];
@@ -517,9 +552,11 @@ __global__ void __launch_bounds__(kEdgeWarps * 32) conv_bwd_edge1(const Args<T> 
     constexpr int D1 = 2 * A + 1, D2 = 2 * B + 1;
     T* ys = e1_warp_smem<T>(smem, 64 * D2);
     T* yo = ys + 32 * D2;
-    for (long long base = (static_cast<long long>(blockIdx.x) * kEdgeWarps + (threadIdx.x >> 5)) * 32;
-         base < a.nitems; base += nw * 32) {
-      const E1Lane l = e1_lane(a, base, lane);
+    long long base = (static_cast<long long>(blockIdx.x) * kEdgeWarps + (threadIdx.x >> 5)) * 32;
+    E1Raw next = e1_raw(a, base, lane);
+    for (; base < a.nitems; base += nw * 32) {
+      const E1Lane l = e1_check(a, next);
+      next = e1_raw(a, base + nw * 32, lane);
       e1_stage_in<T, D2>(ys, a.Y, base, a.nitems, lane);
       __syncwarp();
       T h[D1];
