@@ -375,8 +375,8 @@ struct E1Lane {
   bool valid;
 };
 
-// The index loads of a lane's edge, unchecked: the backward kernels issue them one 32-edge block
-// ahead, so that only the dependent X / dZ row gathers wait on memory in each iteration (in the
+// The index loads of a lane's edge, unchecked: the backward kernels and the deterministic
+// forward issue them one 32-edge block ahead, so that only the dependent X / dZ row gathers wait on memory in each iteration (in the
 // forward the four extra registers cost more occupancy than the overlap gains: 543 vs 527 us).
 struct E1Raw {
   long long e, row, col;
@@ -651,8 +651,13 @@ __global__ void __launch_bounds__(kEdgeWarps * 32) conv_fwd_edge1_det(const Args
     long long carry_key = -2;
     // Blocks start at the 4-aligned edge at or below p0 (lanes before p0 belong to the previous
     // warp and are masked), so the Y rows of a block start 16-byte aligned.
-    for (long long base = p0 & ~3LL; base < p1; base += 32) {
-      E1Lane l = e1_lane(a, base, lane);
+    // The index loads run one block ahead; the next block's first receiver (the key that
+    // decides whether the last run continues) is lane 0's prefetched row.
+    long long base = p0 & ~3LL;
+    E1Raw next = e1_raw(a, base, lane);
+    for (; base < p1; base += 32) {
+      E1Lane l = e1_check(a, next);
+      next = e1_raw(a, base + 32, lane);
       if (l.e >= p1 || l.e < p0) {
         l.valid = false;
         l.row = -1;
@@ -663,7 +668,8 @@ __global__ void __launch_bounds__(kEdgeWarps * 32) conv_fwd_edge1_det(const Args
       e1_message<T, A, B, C>(a, p, l, ys, lane, z);
       __syncwarp();
       const bool more = base + 32 < p1;
-      const long long nk = more ? a.rows[base + 32] : -3;
+      const long long nk0 = __shfl_sync(0xffffffffu, next.row, 0);
+      const long long nk = more ? nk0 : -3;
       e1_seg_block<T, D3>(z, l.valid ? l.row : -1, nk, more, carry, carry_key, a.out0, lane);
     }
   });
