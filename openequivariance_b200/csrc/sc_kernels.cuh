@@ -385,12 +385,17 @@ __global__ void __launch_bounds__(kScWarps * 32, 2) sc_bwd_dx_kernel(const ArgsS
 
 // dcoef[e, c, m, o] = sum over nodes of element e of g[o] phi_m(x).  One CTA per (e, c);
 // thread t owns monomials t, t + blockDim, ...; nodes are consumed in chunks staged in
-// shared memory, in sorted order.
+// shared memory, in sorted order: the chunk's node indices first, then independent gathers of
+// x and g.  A staged x row has K + 1 slots, the last one 1, so every monomial is
+// x[f0] x[f1] x[f2] without branches (absent factors point at the 1); a node's DT output
+// gradients are vector loads.
 template <class T, int K, int DT>
 __global__ void __launch_bounds__(256) sc_bwd_dcoef_kernel(const ArgsSc<T> a) {
-  constexpr int CH = 64;  // nodes per chunk
-  __shared__ T xs[CH * K];
-  __shared__ T gs[CH * DT];
+  constexpr int CH = 256;     // nodes per chunk
+  constexpr int XR = K + 1;   // staged x row: K values and a 1
+  __shared__ T xs[CH * XR];
+  __shared__ __align__(16) T gs[CH * DT];
+  __shared__ long long ps[CH];  // the chunk's node indices
   __shared__ unsigned char tri[sc_monomials(K, 3)][3];
   const int e = blockIdx.x / a.channels, c = blockIdx.x - e * a.channels;
   // Monomial index -> (a, b, c) factors (K marks "absent", x[K] = 1).
@@ -413,6 +418,9 @@ __global__ void __launch_bounds__(256) sc_bwd_dcoef_kernel(const ArgsSc<T> a) {
     tri[t][1] = static_cast<unsigned char>(f1);
     tri[t][2] = static_cast<unsigned char>(f2);
   }
+  // Zero rows (and the 1 slots) once: the unrolled loop reads up to 3 rows past a short last
+  // chunk, which then hold zeros or an earlier chunk's x (finite), times zero gradients.
+  for (int t = threadIdx.x; t < CH * XR; t += blockDim.x) xs[t] = t % XR == K ? T(1) : T(0);
   constexpr int MPT = (sc_monomials(K, 3) + 255) / 256;  // monomials per thread
   T acc[MPT][DT];
 #pragma unroll
@@ -423,27 +431,48 @@ __global__ void __launch_bounds__(256) sc_bwd_dcoef_kernel(const ArgsSc<T> a) {
   for (long long base = b0; base < b1; base += CH) {
     const int n = static_cast<int>(min(static_cast<long long>(CH), b1 - base));
     __syncthreads();
+    for (int r = threadIdx.x; r < n; r += blockDim.x) ps[r] = a.perm[base + r];
+    __syncthreads();
+#pragma unroll 4
     for (int t = threadIdx.x; t < n * K; t += blockDim.x) {
       const int r = t / K, i = t - r * K;
-      xs[t] = a.x[(a.perm[base + r] * a.channels + c) * K + i];
+      xs[r * XR + i] = a.x[(ps[r] * a.channels + c) * K + i];
     }
+#pragma unroll 4
     for (int t = threadIdx.x; t < n * DT; t += blockDim.x) {
       const int r = t / DT, o = t - r * DT;
-      gs[t] = o < a.nout ? a.gout[a.perm[base + r] * a.out_dim + a.map.col[o] + c * a.map.step[o]] : T(0);
+      gs[t] = o < a.nout ? a.gout[ps[r] * a.out_dim + a.map.col[o] + c * a.map.step[o]] : T(0);
     }
+    // Rows n..CH-1 of a short last chunk: zero gradients, so the unrolled loop adds nothing.
+    for (int t = n * DT + threadIdx.x; t < CH * DT; t += blockDim.x) gs[t] = T(0);
     __syncthreads();
+    const int nr = (n + 3) & ~3;  // rows rounded up to the unroll
 #pragma unroll
     for (int j = 0; j < MPT; ++j) {
       const int mi = threadIdx.x + j * 256;
       if (mi < a.m) {
-        const int f0 = tri[mi][0], f1 = tri[mi][1], f2 = tri[mi][2];
-        for (int r = 0; r < n; ++r) {
-          const T* xr = xs + r * K;
-          T phi = xr[f0];
-          if (f1 < K) phi *= xr[f1];
-          if (f2 < K) phi *= xr[f2];
+        const T* x0 = xs + tri[mi][0];
+        const T* x1 = xs + tri[mi][1];
+        const T* x2 = xs + tri[mi][2];
+#pragma unroll 4
+        for (int r = 0; r < nr; ++r) {
+          const T phi = x0[r * XR] * x1[r * XR] * x2[r * XR];
+          T gv[DT];
+          if constexpr (sizeof(T) == 4 && DT % 4 == 0) {
 #pragma unroll
-          for (int o = 0; o < DT; ++o) acc[j][o] += phi * gs[r * DT + o];
+            for (int o4 = 0; o4 < DT; o4 += 4) {
+              const float4 q = reinterpret_cast<const float4*>(gs + r * DT + o4)[0];
+              gv[o4] = q.x;
+              gv[o4 + 1] = q.y;
+              gv[o4 + 2] = q.z;
+              gv[o4 + 3] = q.w;
+            }
+          } else {
+#pragma unroll
+            for (int o = 0; o < DT; ++o) gv[o] = gs[r * DT + o];
+          }
+#pragma unroll
+          for (int o = 0; o < DT; ++o) acc[j][o] += phi * gv[o];
         }
       }
     }
