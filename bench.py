@@ -44,7 +44,9 @@ def _args():
     ap.add_argument("--conv-nodes", type=int, default=200000)
     ap.add_argument("--conv-mode", choices=["atomic", "deterministic"], default="atomic")
     ap.add_argument("--sc-nodes", type=int, default=100000)
-    ap.add_argument("--rows", type=int, default=50000)
+    ap.add_argument("--rows", type=int, default=None,
+                    help="TP rows per GPU (default: the BASELINE config's batch, 50,000 for "
+                         "c2/c2ml, 20,000 for c4)")
     ap.add_argument("--e2e-steps", type=int, default=3)
     ap.add_argument("--e2e-chunks", type=int, default=4,
                     help="row chunks per e2e step, one CUDA stream each (copies in both "
@@ -254,7 +256,7 @@ def bench_tp(args, world, rank, local):
     dev = torch.device("cuda", local)
     problem = baseline_problem(args.workload)
     tp = oeq.TensorProduct(problem)
-    B = args.rows
+    B = args.rows or (20000 if args.workload == "c4" else 50000)
     shared = problem.shared_weights
     gen = torch.Generator(device=dev).manual_seed(1234 + rank)
     X = torch.randn(B, problem.irreps_in1.dim, device=dev, generator=gen)
