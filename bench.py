@@ -294,6 +294,10 @@ def bench_tp(args, world, rank, local):
             e[2].record()
             ops.jit_tp_backward(tp.kernel, tp.hash, X, Y, W, G)
             e[3].record()
+            # Release this step's output before the next forward allocates one: the caching
+            # allocator then reuses its block instead of (in some processes) mapping a new
+            # multi-GB segment while the GPU idles inside the timed forward.
+            del Z
         end.record()
         torch.cuda.synchronize()
     _barrier(world)
