@@ -164,10 +164,14 @@ int oeqb_group_gemm(int dtype, const void* A, const void* B, const int64_t* offs
  * implicit synchronisation and fragmentation are not acceptable.  The problem tables live
  * in a static device array of the library (OEQB_NOALLOC_BYTES, loaded on every device
  * the library is used on and kept until process exit); problems whose tables exceed it are
- * rejected with OEQB_ERR_UNSUPPORTED.  The first call on a device resolves the array's
- * address (make that first call outside any stream capture).  All calls on a device share
- * the array, so calls whose GPU work overlaps race; serialise them (one stream).  Inputs
- * and outputs are as for oeqb_tp_forward; the descriptor is parsed on every call. */
+ * rejected with OEQB_ERR_UNSUPPORTED.  The first call on a device, with that device
+ * current, resolves the array's device address (cudaGetSymbolAddress); make that first call
+ * before any stream capture.  Every call parses the descriptor and copies its tables from a
+ * host buffer of the call into the array with cudaMemcpyAsync on `stream`.  All calls on a
+ * device share the array and leave their tables in it, so calls whose GPU work overlaps race;
+ * serialise them (one stream).  The call runs the table-driven forward kernel whatever the
+ * problem, and that kernel raises no device status: the returned code is the whole error
+ * report.  Inputs and outputs are as for oeqb_tp_forward. */
 #define OEQB_NOALLOC_BYTES 65536
 int oeqb_tp_forward_noalloc(const void* descriptor, size_t nbytes, int device, int64_t batch,
                             const void* L1_in, const void* L2_in, const void* W, void* L3_out,

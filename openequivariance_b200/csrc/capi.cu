@@ -1782,16 +1782,20 @@ int oeqb_tp_forward_noalloc(const void* descriptor, size_t nbytes, int device, i
   oeqb_plan p;
   p.device = device;
   if (int rc = parse_descriptor(descriptor, nbytes, p)) return rc;
-  p.row_ok = false;  // this entry point runs the table-driven forward kernel
+  // This entry point runs the table-driven forward kernel only.  Every specialised path is
+  // switched off here, including the shared-weight uvw ones (tc, sw), whose weight images
+  // only oeqb_plan_create allocates.
+  p.row_ok = false;
   p.segf = {};
   p.segb = {};
   p.segl = {};
   p.lk = {};
   p.lkf = {};
+  p.tc = {};
+  p.sw = {};
   std::vector<unsigned char> img;
   layout_tables(p, img);
-  const size_t status_off = align16(img.size());
-  const size_t need = status_off + 16;
+  const size_t need = img.size();
   if (need > kNoAllocBytes)
     return fail(OEQB_ERR_UNSUPPORTED,
                 "problem tables need " + std::to_string(need) +
@@ -1805,13 +1809,14 @@ int oeqb_tp_forward_noalloc(const void* descriptor, size_t nbytes, int device, i
     p.sm_count = sms;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   p.dmem = base;
-  p.d_status = reinterpret_cast<int*>(base + status_off);
+  // The table kernel of the batch forward raises no device status (it indexes only rows
+  // below `batch` and its own tables), so no status word is kept: the returned code is the
+  // whole error report of this call.
+  p.d_status = nullptr;
   OEQB_CUDA(cudaMemcpyAsync(base, img.data(), img.size(), cudaMemcpyHostToDevice, s));
-  OEQB_CUDA(cudaMemsetAsync(p.d_status, 0, sizeof(int), s));
   const int rc = p.dtype == 1 ? tp_forward_t<float>(&p, batch, L1_in, L2_in, W, L3_out, s)
                               : tp_forward_t<double>(&p, batch, L1_in, L2_in, W, L3_out, s);
   p.dmem = nullptr;  // not owned
-  p.d_status = nullptr;
   return rc;
 }
 

@@ -1,8 +1,8 @@
 """Generates the golden fixtures in this directory from the reference implementation.
 
-Run in a container where the reference is mounted (default ``/root/reference``, override
-with ``OEQ_REFERENCE_ROOT``): ``python tests/golden/make_golden.py``.  The GPU box does not
-have the reference; the committed ``*.npz`` files are what the tests read.
+Run where a checkout of the reference is available, naming it in ``OEQ_REFERENCE_ROOT``:
+``OEQ_REFERENCE_ROOT=<checkout> python tests/golden/make_golden.py``.  The tests never read
+the reference; the committed ``*.npz`` files are what they read.
 
 What is taken from the reference (imported with ``OEQ_NOTORCH=1``):
 
@@ -27,7 +27,10 @@ from pathlib import Path
 import numpy as np
 
 OUT = Path(__file__).resolve().parent
-REF = Path(os.environ.get("OEQ_REFERENCE_ROOT", "/root/reference")) / "openequivariance"
+if "OEQ_REFERENCE_ROOT" not in os.environ:
+    sys.exit("set OEQ_REFERENCE_ROOT to a checkout of the reference (the directory that holds "
+             "openequivariance/openequivariance)")
+REF = Path(os.environ["OEQ_REFERENCE_ROOT"]) / "openequivariance"
 
 
 def _import_reference():

@@ -1,7 +1,7 @@
 """Generates the symmetric-contraction golden fixtures (``sc_*.npz``) from the reference.
 
-Run where the reference is mounted (default ``/root/reference``, override with
-``OEQ_REFERENCE_ROOT``): ``python tests/golden/make_golden_sc.py``.
+Run where a checkout of the reference is available, naming it in ``OEQ_REFERENCE_ROOT``:
+``OEQ_REFERENCE_ROOT=<checkout> python tests/golden/make_golden_sc.py``.
 
 The reference module ``_torch/symmetric_contraction/SymmetricContraction.py`` imports e3nn
 and the compiled extension, neither of which exists in this container.  The module file is
@@ -34,7 +34,10 @@ from pathlib import Path
 import numpy as np
 
 OUT = Path(__file__).resolve().parent
-REF = Path(os.environ.get("OEQ_REFERENCE_ROOT", "/root/reference")) / "openequivariance"
+if "OEQ_REFERENCE_ROOT" not in os.environ:
+    sys.exit("set OEQ_REFERENCE_ROOT to a checkout of the reference (the directory that holds "
+             "openequivariance/openequivariance)")
+REF = Path(os.environ["OEQ_REFERENCE_ROOT"]) / "openequivariance"
 
 os.environ["OEQ_NOTORCH"] = "1"
 sys.path.insert(0, str(REF))

@@ -21,8 +21,12 @@ def _ptr(t):
     return ctypes.c_void_p(t.data_ptr())
 
 
+# tp_c4_nequip_uvw is the shared-weight uvw class: the plan path runs its dedicated
+# kernels (tensor cores in float32), the allocation-free call runs the table kernel.
 @pytest.mark.parametrize("name,dtype", [("tp_mace_large.npz", np.float32),
-                                        ("tp_c1.npz", np.float64)])
+                                        ("tp_c1.npz", np.float64),
+                                        ("tp_c4_nequip_uvw.npz", np.float32),
+                                        ("tp_c4_nequip_uvw.npz", np.float64)])
 def test_noalloc_forward_matches_plan_forward(name, dtype, cuda_device):
     import torch
 
@@ -42,7 +46,8 @@ def test_noalloc_forward_matches_plan_forward(name, dtype, cuda_device):
             B = 300 + 77 * call
             X = torch.randn(B, prob.irreps_in1.dim, dtype=tdt, device="cuda", generator=gen)
             Y = torch.randn(B, prob.irreps_in2.dim, dtype=tdt, device="cuda", generator=gen)
-            W = torch.randn(B, prob.weight_numel, dtype=tdt, device="cuda", generator=gen)
+            wshape = (prob.weight_numel,) if prob.shared_weights else (B, prob.weight_numel)
+            W = torch.randn(*wshape, dtype=tdt, device="cuda", generator=gen)
             Z_ref = torch.empty(B, prob.irreps_out.dim, dtype=tdt, device="cuda")
             Z = torch.full_like(Z_ref, float("nan"))
             assert lib.oeqb_tp_forward(handle, ctypes.c_int64(B), _ptr(X), _ptr(Y), _ptr(W),
