@@ -72,8 +72,24 @@ size_t oeqb_conv_workspace_bytes(const oeqb_plan* plan, int64_t nnz, int64_t nod
 
 /* Synchronises `stream` and reports (then clears) the plan's device error flag:
  * 0 = clean, 1 = an edge index was out of range, 2 = a permutation entry was out of
- * range.  Kernels skip such entries instead of faulting. */
+ * range, 3 = a pipeline wait inside a kernel expired (that call's outputs are incomplete).
+ * Kernels skip bad entries instead of faulting.  Returns OEQB_ERR_DEVICE with the message
+ * when the flag was set.  (The reference has no counterpart: its kernels index unchecked.) */
 int oeqb_plan_check_status(oeqb_plan* plan, int* status, void* stream);
+
+/* Checks a convolution graph on the device before it is used, synchronously on `stream`
+ * (no counterpart in the reference, whose kernels trust their indices).  Reports, as
+ * OEQB_ERR_INVALID with the message of the most basic defect found:
+ *   rows/cols entries outside [0, node_count);
+ *   transpose_perm (if not NULL) entries outside [0, nnz), repeated entries (not a
+ *   permutation), or an order that does not sort the edges by cols (sender);
+ *   rows not sorted, when need_sorted_rows is nonzero (deterministic plans).
+ * `scratch` is device memory of at least oeqb_conv_validate_scratch_bytes(nnz) bytes,
+ * 16-byte aligned; the call clears it itself. */
+size_t oeqb_conv_validate_scratch_bytes(int64_t nnz);
+int oeqb_conv_validate(const int64_t* rows, const int64_t* cols, const int64_t* transpose_perm,
+                       int64_t nnz, int64_t node_count, int need_sorted_rows, void* scratch,
+                       size_t scratch_bytes, void* stream);
 
 /* ---- batch tensor product (replaces tensorproducts.hpp:77-88) ----
  * L1_in [batch, L1_dim], L2_in [batch, L2_dim], W [batch, weight_numel] or

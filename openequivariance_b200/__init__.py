@@ -28,6 +28,37 @@ if os.environ.get("OEQ_NOTORCH", "0") != "1":
     )
 
 
+def set_device_checks(enabled: bool) -> bool:
+    """Turns the synchronous device checks on or off; returns the previous setting.
+
+    The kernels never fault on bad graph indices: they skip them and raise a status flag.
+    With checks on, every convolution call validates rows / cols / transpose_perm on the
+    device before launching (range, receiver order in deterministic mode, permutation and
+    sender order of ``transpose_perm``) and every call reads its plan's status flag
+    afterwards; a problem raises ``RuntimeError`` naming it.  Each check synchronises the
+    stream (checks are skipped during CUDA-graph capture).  ``OEQB_DEVICE_CHECKS=1`` in the
+    environment turns them on at load time.
+    """
+    import torch
+
+    from ._ext import load_torch_ops
+
+    load_torch_ops()
+    return bool(torch.ops.oeqb200.set_device_checks(bool(enabled)))
+
+
+def check_device_status() -> None:
+    """Reads and clears the status flag of every plan on the current device and raises
+    ``RuntimeError`` if a kernel flagged a bad index or an expired pipeline wait since the
+    last check (synchronises the current stream)."""
+    import torch
+
+    from ._ext import load_torch_ops
+
+    load_torch_ops()
+    torch.ops.oeqb200.check_device_status()
+
+
 def torch_ext_so_path():
     """Path of the ``.so`` to link when using the operators from the PyTorch C++ API."""
     from ._ext import TORCH_LIB_PATH
@@ -57,4 +88,6 @@ __all__ = [
     "torch_ext_so_path",
     "jax",
     "transpose_irreps",
+    "set_device_checks",
+    "check_device_status",
 ]

@@ -1584,6 +1584,61 @@ int conv_bwd_t(oeqb_plan* p, bool db, const void* X, const void* Y, const void* 
 }  // namespace
 
 // ---------------------------------------------------------------------------------------
+// Graph validation (oeqb_conv_validate).  One thread per edge position; every defect found
+// sets its bit in report[0] (bit k = defect code k), so the host can name the most basic
+// one whatever the thread order.  seen[] is a bitmap over edge positions for the
+// permutation test.  Reads only in-range addresses: a transpose_perm entry is used as an
+// index only after its own range check.
+__global__ void conv_validate_kernel(const long long* __restrict__ rows,
+                                     const long long* __restrict__ cols,
+                                     const long long* __restrict__ perm, long long nnz,
+                                     long long nodes, int need_sorted, unsigned* report,
+                                     unsigned* seen) {
+  unsigned bits = 0;
+  const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
+  for (long long e = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; e < nnz;
+       e += stride) {
+    const long long r = rows[e], c = cols[e];
+    if (r < 0 || r >= nodes || c < 0 || c >= nodes) bits |= 1u << 1;
+    if (need_sorted && e + 1 < nnz && rows[e + 1] < r) bits |= 1u << 4;
+    if (perm) {
+      const long long q = perm[e];
+      if (q < 0 || q >= nnz) {
+        bits |= 1u << 2;
+        continue;
+      }
+      const unsigned bit = 1u << (q & 31);
+      if (atomicOr(seen + (q >> 5), bit) & bit) bits |= 1u << 5;
+      if (e + 1 < nnz) {
+        const long long q2 = perm[e + 1];
+        if (q2 >= 0 && q2 < nnz && cols[q2] < cols[q]) bits |= 1u << 6;
+      }
+    }
+  }
+  bits |= __shfl_xor_sync(0xffffffffu, bits, 16);
+  bits |= __shfl_xor_sync(0xffffffffu, bits, 8);
+  bits |= __shfl_xor_sync(0xffffffffu, bits, 4);
+  bits |= __shfl_xor_sync(0xffffffffu, bits, 2);
+  bits |= __shfl_xor_sync(0xffffffffu, bits, 1);
+  if (bits && (threadIdx.x & 31) == 0) atomicOr(report, bits);
+}
+
+namespace {
+// Messages of the device status codes (plan status flags and validation defects).
+const char* status_message(int code) {
+  switch (code) {
+    case 1: return "edge index out of range: every rows/cols entry must lie in [0, num_nodes)";
+    case 2: return "transpose_perm entry out of range: entries must lie in [0, num_edges)";
+    case 3: return "a kernel's pipeline wait expired; the outputs of that call are incomplete";
+    case 4: return "rows are not sorted: the deterministic convolution needs receiver-sorted edges";
+    case 5: return "transpose_perm is not a permutation: an edge position appears twice";
+    case 6: return "transpose_perm does not list the edges in sender (cols) order";
+    default: return "unknown device status";
+  }
+}
+}  // namespace
+
+// ---------------------------------------------------------------------------------------
 // Allocation-free forward (oeqb_tp_forward_noalloc).  The problem tables and the status
 // flag live in this file-scope device array instead of plan memory, so the call needs no
 // device allocation.  Every call on a device shares the array and leaves its contents
@@ -1670,9 +1725,38 @@ int oeqb_plan_check_status(oeqb_plan* p, int* status, void* stream) {
   OEQB_CUDA(cudaStreamSynchronize(s));
   OEQB_CUDA(cudaMemsetAsync(p->d_status, 0, sizeof(int), s));
   if (status) *status = h;
-  return h ? fail(OEQB_ERR_DEVICE, h == 2 ? "transpose_perm entry out of range"
-                                          : "edge index out of range")
-           : 0;
+  return h ? fail(OEQB_ERR_DEVICE, status_message(h)) : 0;
+}
+
+size_t oeqb_conv_validate_scratch_bytes(int64_t nnz) {
+  return nnz <= 0 ? 16 : 16 + 4 * static_cast<size_t>((nnz + 31) / 32);
+}
+
+int oeqb_conv_validate(const int64_t* rows, const int64_t* cols, const int64_t* transpose_perm,
+                       int64_t nnz, int64_t node_count, int need_sorted_rows, void* scratch,
+                       size_t scratch_bytes, void* stream) {
+  if (nnz < 0 || node_count < 0) return fail(OEQB_ERR_INVALID, "negative size");
+  if (nnz == 0) return 0;
+  if (!rows || !cols) return fail(OEQB_ERR_INVALID, "null rows/cols");
+  const size_t need = oeqb_conv_validate_scratch_bytes(nnz);
+  if (!scratch || scratch_bytes < need || (reinterpret_cast<uintptr_t>(scratch) & 15))
+    return fail(OEQB_ERR_INVALID, "validation scratch must be 16-byte aligned and hold " +
+                                      std::to_string(need) + " bytes");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  auto* report = static_cast<unsigned*>(scratch);
+  OEQB_CUDA(cudaMemsetAsync(scratch, 0, need, s));
+  const long long blocks = std::min<long long>((nnz + 255) / 256, 148LL * 8);
+  conv_validate_kernel<<<static_cast<unsigned>(blocks), 256, 0, s>>>(
+      reinterpret_cast<const long long*>(rows), reinterpret_cast<const long long*>(cols),
+      reinterpret_cast<const long long*>(transpose_perm), nnz, node_count, need_sorted_rows,
+      report, report + 4);
+  OEQB_CUDA(cudaGetLastError());
+  unsigned h = 0;
+  OEQB_CUDA(cudaMemcpyAsync(&h, report, sizeof(h), cudaMemcpyDeviceToHost, s));
+  OEQB_CUDA(cudaStreamSynchronize(s));
+  for (int code = 1; code < 32; ++code)
+    if (h & (1u << code)) return fail(OEQB_ERR_INVALID, status_message(code));
+  return 0;
 }
 
 int oeqb_tp_forward(oeqb_plan* p, int64_t batch, const void* L1_in, const void* L2_in,

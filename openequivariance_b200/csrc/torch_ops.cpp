@@ -14,6 +14,8 @@
 #include <c10/cuda/CUDAStream.h>
 #include <torch/library.h>
 
+#include <atomic>
+#include <cstdlib>
 #include <map>
 #include <mutex>
 #include <sstream>
@@ -97,6 +99,62 @@ void* stream_of(const Tensor& t) {
   return reinterpret_cast<void*>(c10::cuda::getCurrentCUDAStream(t.device().index()).stream());
 }
 
+// Device checks.  The kernels never fault on bad indices: they skip them and raise the
+// plan's status flag.  With checks on (OEQB_DEVICE_CHECKS=1 in the environment, or
+// oeqb200::set_device_checks(True)), every convolution call first validates its graph on
+// the device (oeqb_conv_validate) and raises before launching anything if it is bad, and
+// every call reads the plan's status after its launches and raises if a kernel flagged
+// something.  Both synchronise the stream, so they are skipped while the stream is being
+// captured into a CUDA graph.  With checks off, oeqb200::check_device_status() reads the
+// flags of every plan on demand.
+std::atomic<bool> g_checks{[] {
+  const char* e = std::getenv("OEQB_DEVICE_CHECKS");
+  return e != nullptr && std::string(e) == "1";
+}()};
+
+bool checks_active(void* stream) {
+  if (!g_checks.load(std::memory_order_relaxed)) return false;
+  cudaStreamCaptureStatus st = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(static_cast<cudaStream_t>(stream), &st) != cudaSuccess) return false;
+  return st == cudaStreamCaptureStatusNone;
+}
+
+void validate_graph(const Tensor& rows, const Tensor& cols, const Tensor* perm, int64_t nnz,
+                    int64_t nodes, bool sorted_rows, void* stream) {
+  const size_t need = oeqb_conv_validate_scratch_bytes(nnz);
+  Tensor scratch = at::empty({static_cast<int64_t>(need)}, rows.options().dtype(at::kByte));
+  const int rc = oeqb_conv_validate(rows.data_ptr<int64_t>(), cols.data_ptr<int64_t>(),
+                                    perm ? perm->data_ptr<int64_t>() : nullptr, nnz, nodes,
+                                    sorted_rows ? 1 : 0, scratch.data_ptr(), need, stream);
+  TORCH_CHECK(rc == 0, "OpenEquivariance-B200 input check failed: ", oeqb_last_error());
+}
+
+void check_status(const PlanInfo& k, void* stream) {
+  int st = 0;
+  const int rc = oeqb_plan_check_status(k.plan, &st, stream);
+  TORCH_CHECK(rc == 0, "OpenEquivariance-B200 device error: ", oeqb_last_error());
+}
+
+bool set_device_checks(bool enabled) { return g_checks.exchange(enabled); }
+
+// Reads (and clears) the status flag of every plan of the current device; raises on the
+// first that is set.
+void check_device_status() {
+  const int dev = c10::cuda::current_device();
+  std::vector<oeqb_plan*> plans;
+  {
+    std::lock_guard<std::mutex> g(g_mu);
+    for (auto& kv : g_plans)
+      if (kv.first.second == dev) plans.push_back(kv.second.plan);
+  }
+  void* s = reinterpret_cast<void*>(c10::cuda::getCurrentCUDAStream(dev).stream());
+  for (oeqb_plan* p : plans) {
+    int st = 0;
+    const int rc = oeqb_plan_check_status(p, &st, s);
+    TORCH_CHECK(rc == 0, "OpenEquivariance-B200 device error: ", oeqb_last_error());
+  }
+}
+
 int tensor_device(const Tensor& t) { return t.is_cuda() ? t.device().index() : 0; }
 
 void check_weights(const PlanInfo& k, const Tensor& W, int64_t rows, const char* name) {
@@ -119,8 +177,10 @@ Tensor jit_tp_forward(Tensor json_bytes, int64_t hash, Tensor L1_in, Tensor L2_i
   c10::cuda::CUDAGuard guard(L1_in.device());
   Tensor L3_out = at::empty({B, k.L3_dim}, L1_in.options());
   Tensor x = L1_in.contiguous(), y = L2_in.contiguous(), w = W.contiguous();
+  void* st = stream_of(L1_in);
   check_rc(oeqb_tp_forward(k.plan, B, x.data_ptr(), y.data_ptr(), w.data_ptr(), L3_out.data_ptr(),
-                           stream_of(L1_in)));
+                           st));
+  if (checks_active(st)) check_status(k, st);
   return L3_out;
 }
 
@@ -138,9 +198,11 @@ std::tuple<Tensor, Tensor, Tensor> jit_tp_backward(Tensor json_bytes, int64_t ha
   Tensor W_grad = at::empty_like(W, at::MemoryFormat::Contiguous);
   Tensor x = L1_in.contiguous(), y = L2_in.contiguous(), w = W.contiguous(),
          gz = L3_grad.contiguous();
+  void* st = stream_of(L1_in);
   check_rc(oeqb_tp_backward(k.plan, B, x.data_ptr(), L1_grad.data_ptr(), y.data_ptr(),
                             L2_grad.data_ptr(), w.data_ptr(), W_grad.data_ptr(), gz.data_ptr(),
-                            stream_of(L1_in)));
+                            st));
+  if (checks_active(st)) check_status(k, st);
   return {L1_grad, L2_grad, W_grad};
 }
 
@@ -198,12 +260,15 @@ std::tuple<Tensor, Tensor, Tensor, Tensor> jit_tp_double_backward(
     auto [gx1, unused_y1, gw1] = bwd(x, dy, w);
     auto [unused_x2, gy2, gw2] = bwd(dx, y, w);
     auto [gx3, gy3, unused_w3] = bwd(x, y, dw);
+    if (checks_active(st)) check_status(k, st);
     return {gx1.add_(gx3), gy2.add_(gy3), gw1.add_(gw2), L3_dgrad};
   }
+  void* st = stream_of(L1_in);
   check_rc(oeqb_tp_double_backward(k.plan, B, x.data_ptr(), y.data_ptr(), w.data_ptr(),
                                    gz.data_ptr(), dx.data_ptr(), dy.data_ptr(), dw.data_ptr(),
                                    L1_grad.data_ptr(), L2_grad.data_ptr(), W_grad.data_ptr(),
-                                   L3_dgrad.data_ptr(), stream_of(L1_in)));
+                                   L3_dgrad.data_ptr(), st));
+  if (checks_active(st)) check_status(k, st);
   return {L1_grad, L2_grad, W_grad, L3_dgrad};
 }
 
@@ -244,10 +309,13 @@ Tensor jit_conv_forward(Tensor json_bytes, int64_t hash, Tensor L1_in, Tensor L2
   Tensor L3_out = at::empty({c.nodes, k.L3_dim}, L1_in.options());
   Tensor x = L1_in.contiguous(), y = L2_in.contiguous(), w = W.contiguous(),
          r = rows.contiguous(), cl = cols.contiguous();
+  void* st = stream_of(L1_in);
+  const bool chk = checks_active(st);
+  if (chk) validate_graph(r, cl, nullptr, c.nnz, c.nodes, k.deterministic, st);
   check_rc(oeqb_conv_forward(k.plan, x.data_ptr(), y.data_ptr(), w.data_ptr(), L3_out.data_ptr(),
                              r.data_ptr<int64_t>(), cl.data_ptr<int64_t>(), c.nnz, c.nodes,
-                             workspace.data_ptr(), static_cast<size_t>(workspace.numel()),
-                             stream_of(L1_in)));
+                             workspace.data_ptr(), static_cast<size_t>(workspace.numel()), st));
+  if (chk) check_status(k, st);
   return L3_out;
 }
 
@@ -273,11 +341,15 @@ std::tuple<Tensor, Tensor, Tensor> jit_conv_backward(Tensor json_bytes, int64_t 
   const size_t need = oeqb_conv_workspace_bytes(k.plan, c.nnz, c.nodes);
   if (need > static_cast<size_t>(workspace.numel()))
     ws = at::empty({static_cast<int64_t>(need)}, workspace.options());
+  void* st = stream_of(L1_in);
+  const bool chk = checks_active(st);
+  if (chk) validate_graph(r, cl, k.deterministic ? &tp : nullptr, c.nnz, c.nodes, k.deterministic, st);
   check_rc(oeqb_conv_backward(
       k.plan, x.data_ptr(), L1_grad.data_ptr(), y.data_ptr(), L2_grad.data_ptr(), w.data_ptr(),
       W_grad.data_ptr(), gz.data_ptr(), r.data_ptr<int64_t>(), cl.data_ptr<int64_t>(), c.nnz,
       c.nodes, ws.data_ptr(), static_cast<size_t>(ws.numel()),
-      k.deterministic ? tp.data_ptr<int64_t>() : nullptr, stream_of(L1_in)));
+      k.deterministic ? tp.data_ptr<int64_t>() : nullptr, st));
+  if (chk) check_status(k, st);
   return {L1_grad, L2_grad, W_grad};
 }
 
@@ -302,12 +374,16 @@ std::tuple<Tensor, Tensor, Tensor, Tensor> jit_conv_double_backward(
          gz = L3_grad.contiguous(), dx = L1_dgrad.contiguous(), dy = L2_dgrad.contiguous(),
          dw = W_dgrad.contiguous(), r = rows.contiguous(), cl = cols.contiguous();
   Tensor tp = k.deterministic ? transpose_perm.contiguous() : Tensor();
+  void* st = stream_of(L1_in);
+  const bool chk = checks_active(st);
+  if (chk) validate_graph(r, cl, k.deterministic ? &tp : nullptr, c.nnz, c.nodes, k.deterministic, st);
   check_rc(oeqb_conv_double_backward(
       k.plan, x.data_ptr(), y.data_ptr(), w.data_ptr(), gz.data_ptr(), dx.data_ptr(),
       dy.data_ptr(), dw.data_ptr(), L1_grad.data_ptr(), L2_grad.data_ptr(), W_grad.data_ptr(),
       L3_dgrad.data_ptr(), r.data_ptr<int64_t>(), cl.data_ptr<int64_t>(), c.nnz, c.nodes,
       workspace.data_ptr(), static_cast<size_t>(workspace.numel()),
-      k.deterministic ? tp.data_ptr<int64_t>() : nullptr, stream_of(L1_in)));
+      k.deterministic ? tp.data_ptr<int64_t>() : nullptr, st));
+  if (chk) check_status(k, st);
   return {L1_grad, L2_grad, W_grad, L3_dgrad};
 }
 
@@ -391,6 +467,8 @@ std::tuple<Tensor, Tensor> sc_backward(Tensor x, Tensor perm, Tensor elem_offset
 }  // namespace
 
 TORCH_LIBRARY(oeqb200, m) {
+  m.def("set_device_checks(bool enabled) -> bool", &set_device_checks);
+  m.def("check_device_status() -> ()", &check_device_status);
   m.def("sc_forward(Tensor x, Tensor perm, Tensor elem_offsets, Tensor coef, int[] out_col, int[] out_step, int out_dim, int degree) -> Tensor");
   m.def("sc_backward(Tensor x, Tensor perm, Tensor elem_offsets, Tensor coef, Tensor grad_out, int[] out_col, int[] out_step, int degree) -> (Tensor, Tensor)");
 }

@@ -121,3 +121,28 @@ def test_torch_ops_registered():
     for name in ("jit_tp_forward", "jit_tp_backward", "jit_tp_double_backward",
                  "jit_conv_forward", "jit_conv_backward", "jit_conv_double_backward"):
         assert hasattr(torch.ops.libtorch_tp_jit, name)
+
+
+def test_refgpu_cases_match_baseline_problems():
+    """The BASELINE-size parity cases (run on the reference's kernels by
+    ``tests/golden/make_golden_refgpu.py``) are the package's BASELINE problems."""
+    import sys
+
+    from conftest import GOLDEN
+    from openequivariance_b200.problems import baseline_problem
+
+    sys.path.insert(0, str(GOLDEN))
+    import refgpu_cases as R
+
+    for case, base in (("c1", "c1"), ("c2", "c2"), ("c2ml", "c2ml"), ("c4_f32", "c4")):
+        in1, in2, out, ins, mode, shared = R.TP_CASES[case][:6]
+        p = baseline_problem(base)
+        assert (str(p.irreps_in1), str(p.irreps_in2), str(p.irreps_out)) == (in1, in2, out)
+        assert [(i.i_in1, i.i_in2, i.i_out) for i in p.instructions] == ins
+        assert {i.connection_mode for i in p.instructions} == {mode}
+        assert p.shared_weights == shared
+        assert p.weight_numel == R.weight_numel(R.TP_CASES[case])
+    rows, cols, tperm = R.c3_graph()
+    assert rows.size == R.C3_EDGES
+    assert np.all(np.diff(rows * R.C3_NODES + cols) > 0)
+    assert np.all(np.diff(cols[tperm] * R.C3_NODES + rows[tperm]) > 0)
