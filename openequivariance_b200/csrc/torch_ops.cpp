@@ -14,6 +14,7 @@
 #include <c10/cuda/CUDAStream.h>
 #include <torch/library.h>
 
+#include <algorithm>
 #include <atomic>
 #include <cstdlib>
 #include <map>
@@ -425,7 +426,22 @@ Tensor group_gemm(Tensor A, Tensor B, Tensor ragged_counts, int64_t num_W, int64
 
 std::vector<int> int_list(at::IntArrayRef v) { return std::vector<int>(v.begin(), v.end()); }
 
-// Fused symmetric contraction (this package's op; no reference schema).
+// Fused symmetric contraction (this package's op; no reference schema).  The float64
+// kernels take at most 4 padded outputs per pass; wider float64 output sets run in chunks
+// of 4 outputs, each pass writing its own columns of `out` (and its own coefficient
+// columns of the gradient), with the x gradients of the chunks summed in chunk order.
+constexpr int kF64Chunk = 4;
+
+bool chunked(const Tensor& x, const Tensor& coef) {
+  return x.scalar_type() == at::kDouble && coef.size(3) > kF64Chunk;
+}
+
+Tensor chunk_coef(const Tensor& coef, int64_t s, int64_t n) {
+  Tensor c = at::zeros({coef.size(0), coef.size(1), coef.size(2), kF64Chunk}, coef.options());
+  c.narrow(3, 0, n).copy_(coef.narrow(3, s, n));
+  return c;
+}
+
 Tensor sc_forward(Tensor x, Tensor perm, Tensor elem_offsets, Tensor coef, at::IntArrayRef out_col,
                   at::IntArrayRef out_step, int64_t out_dim, int64_t degree) {
   TORCH_CHECK(x.is_cuda() && x.dim() == 3, "sc_forward: x must be a [N, C, K] GPU tensor");
@@ -435,12 +451,23 @@ Tensor sc_forward(Tensor x, Tensor perm, Tensor elem_offsets, Tensor coef, at::I
   Tensor out = at::empty({x.size(0), out_dim}, x.options());
   const auto col = int_list(out_col), step = int_list(out_step);
   TORCH_CHECK(col.size() == step.size(), "sc_forward: out_col / out_step length mismatch");
-  check_rc(oeqb_sc_forward(dtype_code(x), x.size(0), static_cast<int>(x.size(1)),
-                           static_cast<int>(x.size(2)), static_cast<int>(degree),
-                           static_cast<int>(coef.size(3)), static_cast<int>(col.size()), col.data(),
-                           step.data(), out_dim, static_cast<int>(coef.size(0)), xc.data_ptr(),
-                           perm.data_ptr<int64_t>(), elem_offsets.data_ptr<int64_t>(),
-                           cc.data_ptr(), out.data_ptr(), stream_of(x)));
+  const int nout = static_cast<int>(col.size());
+  auto run = [&](const Tensor& cf, int dt, int s, int n) {
+    check_rc(oeqb_sc_forward(dtype_code(x), x.size(0), static_cast<int>(x.size(1)),
+                             static_cast<int>(x.size(2)), static_cast<int>(degree), dt, n,
+                             col.data() + s, step.data() + s, out_dim,
+                             static_cast<int>(coef.size(0)), xc.data_ptr(),
+                             perm.data_ptr<int64_t>(), elem_offsets.data_ptr<int64_t>(),
+                             cf.data_ptr(), out.data_ptr(), stream_of(x)));
+  };
+  if (!chunked(x, cc)) {
+    run(cc, static_cast<int>(cc.size(3)), 0, nout);
+    return out;
+  }
+  for (int s = 0; s < nout; s += kF64Chunk) {
+    const int n = std::min(kF64Chunk, nout - s);
+    run(chunk_coef(cc, s, n), kF64Chunk, s, n);
+  }
   return out;
 }
 
@@ -451,17 +478,35 @@ std::tuple<Tensor, Tensor> sc_backward(Tensor x, Tensor perm, Tensor elem_offset
   TORCH_CHECK(x.is_cuda() && x.dim() == 3, "sc_backward: x must be a [N, C, K] GPU tensor");
   const c10::cuda::CUDAGuard guard(x.device());
   Tensor xc = x.contiguous(), cc = coef.contiguous(), gc = grad_out.contiguous();
-  Tensor gx = at::empty_like(xc);
-  Tensor gcoef = at::empty_like(cc);
   const auto col = int_list(out_col), step = int_list(out_step);
-  check_rc(oeqb_sc_backward(dtype_code(x), x.size(0), static_cast<int>(x.size(1)),
-                            static_cast<int>(x.size(2)), static_cast<int>(degree),
-                            static_cast<int>(coef.size(3)), static_cast<int>(col.size()),
-                            col.data(), step.data(), gc.size(1), static_cast<int>(coef.size(0)),
-                            xc.data_ptr(), perm.data_ptr<int64_t>(),
-                            elem_offsets.data_ptr<int64_t>(), cc.data_ptr(), gc.data_ptr(),
-                            gx.data_ptr(), gcoef.data_ptr(), stream_of(x)));
-  return {gx, gcoef};
+  const int nout = static_cast<int>(col.size());
+  auto run = [&](const Tensor& cf, int dt, int s, int n, Tensor& gx, Tensor& gcoef) {
+    check_rc(oeqb_sc_backward(dtype_code(x), x.size(0), static_cast<int>(x.size(1)),
+                              static_cast<int>(x.size(2)), static_cast<int>(degree), dt, n,
+                              col.data() + s, step.data() + s, gc.size(1),
+                              static_cast<int>(coef.size(0)), xc.data_ptr(),
+                              perm.data_ptr<int64_t>(), elem_offsets.data_ptr<int64_t>(),
+                              cf.data_ptr(), gc.data_ptr(), gx.data_ptr(), gcoef.data_ptr(),
+                              stream_of(x)));
+  };
+  if (!chunked(x, cc)) {
+    Tensor gx = at::empty_like(xc);
+    Tensor gcoef = at::empty_like(cc);
+    run(cc, static_cast<int>(cc.size(3)), 0, nout, gx, gcoef);
+    return {gx, gcoef};
+  }
+  Tensor gx_sum = at::zeros_like(xc);
+  Tensor gcoef = at::zeros_like(cc);
+  for (int s = 0; s < nout; s += kF64Chunk) {
+    const int n = std::min(kF64Chunk, nout - s);
+    Tensor cf = chunk_coef(cc, s, n);
+    Tensor gx = at::empty_like(xc);
+    Tensor gcf = at::empty_like(cf);
+    run(cf, kF64Chunk, s, n, gx, gcf);
+    gx_sum.add_(gx);
+    gcoef.narrow(3, s, n).copy_(gcf.narrow(3, 0, n));
+  }
+  return {gx_sum, gcoef};
 }
 
 }  // namespace

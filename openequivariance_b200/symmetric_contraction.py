@@ -16,8 +16,9 @@ is a polynomial evaluation in registers; nothing is materialised and nothing syn
 with the host.  First-order gradients (x and the coefficients, hence the weights) come from
 ``sc_backward``; when a backward pass itself records a graph (double backward, e.g. force
 training), the gradient is recomputed with differentiable torch operations on the same
-monomial form.  Shapes outside the kernels' range (coupling dimension other than 4 or 9,
-correlation 4, CPU tensors) use that torch formulation throughout.
+monomial form.  There is no CPU path: CPU tensors and shapes outside the kernels' range
+(coupling dimension other than 4 or 9, correlation above 3, more than 16 output
+components) raise.
 """
 
 from __future__ import annotations
@@ -165,20 +166,24 @@ class SymmetricContraction(torch.nn.Module):
         return coef.permute(0, 1, 3, 2)
 
     def forward(self, x: torch.Tensor, y: torch.Tensor) -> torch.Tensor:
+        if not x.is_cuda:
+            raise RuntimeError("Tensor 'x' is not on the GPU.")
+        if not self.fused_ok:
+            raise NotImplementedError(
+                f"SymmetricContraction: coupling dimension {self.k}, correlation {self.degree} "
+                f"and {self.nout} output components are outside the fused kernels' range "
+                f"(coupling dimension 4 or 9, correlation <= 3, at most 16 output components)")
         elem = torch.argmax(y, dim=1)
         coef = self.coefficients()
-        # The 16-wide kernels are float32 only.
-        if self.fused_ok and x.is_cuda and not (x.dtype == torch.float64 and self.dt == 16):
-            from . import _ops
+        from . import _ops
 
-            _ops.ensure_registered()
-            if self.dt > self.nout:
-                coef = torch.nn.functional.pad(coef, (0, self.dt - self.nout))
-            perm = torch.argsort(elem, stable=True)
-            counts = torch.bincount(elem, minlength=self.num_elements)
-            eoff = torch.cat([counts.new_zeros(1), torch.cumsum(counts, 0)])
-            return _FusedSC.apply(x, coef.contiguous(), perm, eoff, elem, self)
-        return _torch_contraction(self, x, coef, elem)
+        _ops.ensure_registered()
+        if self.dt > self.nout:
+            coef = torch.nn.functional.pad(coef, (0, self.dt - self.nout))
+        perm = torch.argsort(elem, stable=True)
+        counts = torch.bincount(elem, minlength=self.num_elements)
+        eoff = torch.cat([counts.new_zeros(1), torch.cumsum(counts, 0)])
+        return _FusedSC.apply(x, coef.contiguous(), perm, eoff, elem, self)
 
 
 def _monomial_features(sc: SymmetricContraction, x: torch.Tensor) -> torch.Tensor:
@@ -194,7 +199,9 @@ def _monomial_features(sc: SymmetricContraction, x: torch.Tensor) -> torch.Tenso
 
 
 def _torch_contraction(sc: SymmetricContraction, x, coef, elem) -> torch.Tensor:
-    """Differentiable torch evaluation of the same polynomial (fallback and double backward)."""
+    """Differentiable torch evaluation of the same polynomial.  Used only to record the
+    double backward (on the device, inside ``_FusedSC.backward``); the forward and first
+    backward always run the fused kernels."""
     phi = _monomial_features(sc, x)                                   # [N, C, M]
     nout = sc.nout
     vals = torch.einsum("ncm,ncmo->nco", phi, coef[elem][..., :nout])  # [N, C, nout]

@@ -11,6 +11,11 @@ from pathlib import Path
 import numpy as np
 import pytest
 
+# The whole GPU session runs with the synchronous device checks on (graph validation before
+# every convolution launch, status read after every launch): any kernel that flags a bad
+# index or an expired pipeline wait fails its test.
+os.environ.setdefault("OEQB_DEVICE_CHECKS", "1")
+
 ROOT = Path(__file__).resolve().parents[1]
 GOLDEN = Path(__file__).resolve().parent / "golden"
 sys.path.insert(0, str(ROOT))

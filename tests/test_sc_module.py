@@ -40,19 +40,26 @@ def _run(mod, d, device, dtype):
     return out, grads
 
 
+def _nerr(a, b):
+    a = np.asarray(a.detach().cpu().double().numpy() if torch.is_tensor(a) else a, dtype=np.float64)
+    b = np.asarray(b, dtype=np.float64)
+    return np.abs(a - b).max() / max(np.abs(b).max(), 1e-30)
+
+
 def _check(d, out, grads, tol):
-    np.testing.assert_allclose(out.detach().cpu().double().numpy(), d["out"], atol=tol, rtol=tol)
-    np.testing.assert_allclose(grads[0].cpu().double().numpy(), d["grad_x"], atol=tol, rtol=tol)
+    """Normalised max error (max |a - b| / max |b|) of the output and every gradient."""
+    pairs = [("out", out, d["out"]), ("grad_x", grads[0], d["grad_x"])]
     corr = int(d["meta"][0])
     gi = 1
     for ci in range((len(grads) - 1) // corr):
-        np.testing.assert_allclose(grads[gi].cpu().double().numpy(), d[f"c{ci}_grad_weights_max"],
-                                   atol=tol, rtol=tol)
+        pairs.append((f"c{ci}.weights_max", grads[gi], d[f"c{ci}_grad_weights_max"]))
         gi += 1
         for i in range(corr - 1):
-            np.testing.assert_allclose(grads[gi].cpu().double().numpy(),
-                                       d[f"c{ci}_grad_weights_{i}"], atol=tol, rtol=tol)
+            pairs.append((f"c{ci}.weights[{i}]", grads[gi], d[f"c{ci}_grad_weights_{i}"]))
             gi += 1
+    for what, got, want in pairs:
+        e = _nerr(got, want)
+        assert e <= tol, f"{what}: normalised max error {e:.3e} > {tol:.0e}"
 
 
 @pytest.mark.parametrize("path", FIXTURES, ids=IDS)
@@ -68,10 +75,34 @@ def test_seeded_weights_and_buffers_match_reference(path):
 
 
 @pytest.mark.parametrize("path", FIXTURES, ids=IDS)
-def test_cpu_torch_formulation_matches_reference(path):
+def test_cpu_monomial_formulation_matches_reference(path):
+    """The weight folding onto monomials (``coefficients``), evaluated by the differentiable
+    torch form of the polynomial on the CPU, reproduces the reference module's outputs and
+    every gradient.  (The module itself runs only the fused GPU kernels.)"""
+    from openequivariance_b200.symmetric_contraction import _torch_contraction
+
     d = np.load(path)
-    out, grads = _run(_module(d), d, "cpu", torch.float64)
+    mod = _module(d)
+    x = torch.tensor(d["x"], dtype=torch.float64, requires_grad=True)
+    ne = int(d["meta"][1])
+    elem = torch.tensor(d["labels"])
+    out = _torch_contraction(mod, x, mod.coefficients(), elem)
+    params = []
+    for c in mod.contractions:
+        params += [c.weights_max] + list(c.weights)
+    g = torch.tensor(d["grad_out"], dtype=torch.float64)
+    grads = torch.autograd.grad((out * g).sum(), [x] + params)
+    assert ne == mod.num_elements
     _check(d, out, grads, 1e-10)
+
+
+def test_module_refuses_cpu_tensors():
+    d = np.load(FIXTURES[0])
+    mod = _module(d)
+    x = torch.tensor(d["x"], dtype=torch.float64)
+    y = torch.nn.functional.one_hot(torch.tensor(d["labels"]), num_classes=int(d["meta"][1]))
+    with pytest.raises(RuntimeError, match="is not on the GPU"):
+        mod(x, y.double())
 
 
 # ------------------------------------------------------------------------------- GPU
@@ -90,7 +121,7 @@ def test_gpu_fused_matches_reference(path, dtype):
     mod = _module(d, torch.float64).to(dtype).cuda()
     assert mod.fused_ok, "fixture shapes are in the fused kernels' range"
     out, grads = _run(mod, d, "cuda", dtype)
-    tol = 1e-10 if dtype == torch.float64 else 2e-5
+    tol = 1e-10 if dtype == torch.float64 else 1e-5
     _check(d, out, grads, tol)
 
 
@@ -98,7 +129,7 @@ def test_gpu_fused_matches_reference(path, dtype):
 @pytest.mark.parametrize("dtype", [torch.float64, torch.float32], ids=["f64", "f32"])
 def test_gpu_mace_shape_against_oracle(dtype):
     """128x0e+128x1o+128x2e -> 128x0e+128x1o, correlation 3, 10 elements (C5 shape)."""
-    n, ne = 3000, 10
+    n, ne = 2000, 10
     prob = SO.ScProblem("128x0e+128x1o+128x2e", "128x0e+128x1o", 3, ne)
     torch.manual_seed(7)
     mod = oeq.SymmetricContraction("128x0e+128x1o+128x2e", "128x0e+128x1o", correlation=3,
@@ -106,14 +137,27 @@ def test_gpu_mace_shape_against_oracle(dtype):
     g = torch.Generator().manual_seed(11)
     x = torch.randn(n, 128, 9, dtype=torch.float64, generator=g)
     labels = torch.randint(0, ne, (n,), generator=g)
-    weights = [[c.weights_max.detach()] + [w.detach() for w in c.weights] for c in mod.contractions]
-    want = SO.forward(prob, weights, x, labels).numpy()
+    weights = [[c.weights_max.detach().clone().requires_grad_(True)] +
+               [w.detach().clone().requires_grad_(True) for w in c.weights]
+               for c in mod.contractions]
+    xo = x.clone().requires_grad_(True)
+    want = SO.forward(prob, weights, xo, labels)
+    G = torch.randn(want.shape, dtype=torch.float64, generator=g)
+    flat = [w for ws in weights for w in ws]
+    want_grads = torch.autograd.grad((want * G).sum(), [xo] + flat)
     modg = mod.to(dtype).cuda()
     y = torch.nn.functional.one_hot(labels, ne).to(dtype).cuda()
-    with torch.no_grad():
-        got = modg(x.to(dtype).cuda(), y).cpu().numpy()
+    xg = x.to(dtype).cuda().requires_grad_(True)
+    got = modg(xg, y)
+    params = [p for c in modg.contractions for p in [c.weights_max] + list(c.weights)]
+    got_grads = torch.autograd.grad((got * G.to(dtype).cuda()).sum(), [xg] + params)
     tol = 1e-12 if dtype == torch.float64 else 1e-5
-    assert _normalized_err(got, want) <= tol
+    assert _normalized_err(got.detach().cpu().numpy(), want.detach().numpy()) <= tol
+    # Gradients of x and of every weight tensor (weights_max and the lower correlations of
+    # both output irreps) at the C5 shape.
+    for i, (a, b) in enumerate(zip(got_grads, want_grads)):
+        e = _normalized_err(a.cpu().numpy(), b.numpy())
+        assert e <= tol, f"gradient {i}: normalised max error {e:.3e}"
 
 
 @pytest.mark.gpu
