@@ -1,19 +1,25 @@
 #!/usr/bin/env python
 """Benchmark of the Clebsch-Gordan tensor-product hot path on B200.
 
-Default workload ("C2"): MACE-style batch uvu tensor product,
-X = 128x0e+128x1o+128x2e, Y = real spherical harmonics (l <= 3) of random unit vectors,
-Z = every parity-allowed output up to l = 3 (24 paths), 50,000 rows per GPU, float32,
-forward + backward per step.  A row is the tensor product of one edge, so the metric is
-edges (rows) per second.  With --gpus N every rank processes its own 50,000-row shard
-(weak scaling, no data-path collective: batch rows are independent).
+Default workload (``--workload conv``): the fused graph convolution that BASELINE.json's
+metric names at 1/2/4/8 GPUs, with C3's irreps (1x2e (x) 1x3e -> 1x2e, per-edge weights) on
+the C5 graph: 200,000 nodes uniform in a periodic cube at C3's density (side 85.5 A, 5 A
+cutoff), 33,514,104 directed edges, forward + backward per step, float32.  Nodes are numbered
+along a Morton curve and partitioned into contiguous receiver ranges over the ranks; the halo
+rows of X (forward) and dX (backward) cross NVLink with NCCL ``all_to_all_single``, overlapped
+with each rank's interior edges (strong scaling: the graph is fixed as N grows).  The metric
+is directed edges per second of the whole job.
+
+At N=1 the line also carries the batch-TP headline of BASELINE configs[1] (``tp_c2``: MACE
+uvu, 24 paths, 50,000 rows, fwd+bwd) and the symmetric contraction (``sc_c5``), each with its
+own roofline.  Other workloads: ``--workload c2 | c2ml | c4 | sc``.
 
 Timing: W warm-up steps, then K steps between barriers + device syncs, CUDA events on the
 launching stream, max over ranks.  Inputs are larger than L2 (126 MB) so no flush is
-needed.  ``e2e`` repeats the step through the public operator API with pinned host
-buffers, host->device copies of the inputs and device->host copies of every output inside
-the timed region.  ``--impl reference`` times the CPU port of the reference's e3nn path
-(the reference ships no CPU implementation) on the host cores.
+needed.  ``e2e`` repeats the step through the public module API with pinned host buffers,
+host->device copies of the inputs and device->host copies of every output inside the timed
+region.  ``--impl reference`` times the CPU port of the reference's e3nn-backed path (the
+reference ships no CPU implementation of its own) on the host cores.
 """
 
 from __future__ import annotations
@@ -40,7 +46,7 @@ def _args():
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["c2", "c2ml", "c4", "conv", "sc"], default="c2")
+    ap.add_argument("--workload", choices=["c2", "c2ml", "c4", "conv", "sc"], default="conv")
     ap.add_argument("--conv-nodes", type=int, default=200000)
     ap.add_argument("--conv-mode", choices=["atomic", "deterministic"], default="atomic")
     ap.add_argument("--sc-nodes", type=int, default=100000)
@@ -52,6 +58,8 @@ def _args():
                     help="row chunks per e2e step, one CUDA stream each (copies in both "
                          "directions overlap with each other and with the kernels)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-extras", action="store_true",
+                    help="at N=1, skip the extra C2 TP and symmetric-contraction lines")
     return ap.parse_args()
 
 
@@ -446,9 +454,62 @@ def cpu_baseline_tp(problem, budget_s=10.0, rows=None):
 # ----------------------------------------------------------------------------- reference
 
 
+def bench_reference_conv(args, world):
+    """The conv workload's reference arm: the CPU port of the reference's e3nn-backed
+    convolution (gather, per-edge tensor product, scatter-add; ``E3NNConv.forward``) on all
+    host threads, each step a bounded sample of the same graph family (the C3 graph: C5's
+    density and degree, 5,000 nodes, 839,872 edges, built on the CPU)."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import cpu_baseline as CB
+    import tp_oracle as O
+
+    import torch
+
+    from openequivariance_b200.graph import radius_graph
+
+    gen = torch.Generator().manual_seed(0)
+    pos = torch.rand(5000, 3, generator=gen, dtype=torch.float64) * 25.0
+    rows, cols, _, _ = radius_graph(pos, 25.0, 5.0)
+    p = O.make_problem("1x2e", "1x3e", "1x2e", [(0, 0, 0, "uvu", True)])
+    X = torch.randn(5000, 5, generator=gen)
+    G = torch.randn(5000, 5, generator=gen)
+    ne = 1 << 17
+    Y = torch.randn(ne, 7, generator=gen)
+    W = torch.randn(ne, 1, generator=gen)
+    r, c = rows[:ne], cols[:ne]
+    for _ in range(args.warmup):
+        CB.time_conv_fwd_bwd(p, X, Y, W, G, r, c)
+    times, threads = [], None
+    for _ in range(args.steps):
+        t, threads = CB.time_conv_fwd_bwd(p, X, Y, W, G, r, c)
+        times.append(t)
+    total = sum(times)
+    value = ne * args.steps / total
+    return {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": 1e3 * total / args.steps, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "impl": "reference",
+        "config": {"workload": _conv_desc(args.conv_nodes, C5_EDGES.get(args.conv_nodes),
+                                          args.conv_mode),
+                   "edges_per_step": ne,
+                   "implementation": "CPU port of the reference's e3nn-backed convolution "
+                                     "(torch-CPU gather / einsum / scatter-add)"},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
+                         "sample": f"{ne} edges of the C3 graph per step, forward+backward, "
+                                   f"float32"},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+
+
 def bench_reference(args, world, rank):
     if rank != 0:
         return None
+    if args.workload == "conv":
+        return bench_reference_conv(args, world)
+    if args.workload == "sc":
+        return {"impl": "reference", "unavailable": "no CPU port of the symmetric contraction "
+                                                    "is timed; use the TP or conv workloads"}
     from openequivariance_b200.problems import baseline_problem
 
     problem = baseline_problem(args.workload)
@@ -517,39 +578,84 @@ def _time_steps(step, K, world, local):
     return _max_over_ranks(start.elapsed_time(end), world), clk.summary()
 
 
-def bench_conv(args, world, rank, local):
-    """C3 irreps on the C5 graph (200,000 nodes, same density as C3: periodic box of side
-    25 * 40^(1/3) A, 5 A cutoff), receiver-range partitioned over the ranks (strong scaling)."""
-    import numpy as np
+def _conv_graph(n, dev):
+    """The C5 graph: n nodes uniform in a periodic cube of side 25 * (n / 5000)^(1/3) A (C3's
+    density), 5 A cutoff, nodes numbered along a Morton curve, receiver-sorted edges."""
     import torch
+
+    from openequivariance_b200.graph import morton_order, radius_graph
+
+    box = 25.0 * (n / 5000.0) ** (1.0 / 3.0)
+    gen = torch.Generator().manual_seed(0)
+    pos = (torch.rand(n, 3, generator=gen, dtype=torch.float64) * box).to(dev)
+    pos = pos[morton_order(pos, box)]
+    rows, cols, tperm, vec = radius_graph(pos, box, 5.0)
+    return rows, cols, vec
+
+
+# Directed edge counts of the C5-family graphs (seed 0), by node count.
+C5_EDGES = {200000: 33514104}
+
+
+def _conv_desc(n, E, mode):
+    return (f"conv: C3 irreps (1x2e x 1x3e -> 1x2e, uvu, per-edge weights) fused conv fwd+bwd "
+            f"on the C5 graph: periodic radius graph, {n} nodes (Morton-numbered), {E} directed "
+            f"edges, {mode}")
+
+
+def _ev_ms(fn, reps=10, warm=3):
+    """Average device time of fn() on the current stream (CUDA events)."""
+    import torch
+
+    for _ in range(warm):
+        fn()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(reps):
+        fn()
+    b.record()
+    torch.cuda.synchronize()
+    return a.elapsed_time(b) / reps
+
+
+def conv_bytes(edges, nodes, fwd, det):
+    """Algorithmic bytes of one C3-irreps convolution launch (float32): each input read once,
+    each output written once; per edge Y (7) and W (1) values and two int64 indices, per node
+    X (5) and Z (5) values; the backward reads Y, W, X, dZ and writes dY, dW, dX (plus the
+    int64 transpose permutation when deterministic)."""
+    if fwd:
+        return edges * ((7 + 1) * 4 + 16) + nodes * (5 + 5) * 4
+    return edges * (2 * (7 + 1) * 4 + 16 + (8 if det else 0)) + nodes * (5 + 5 + 5) * 4
+
+
+def bench_conv(args, world, rank, local):
+    """C3 irreps on the C5 graph (200,000 nodes, 33.5 M directed edges, C3's density),
+    receiver-range partitioned over the ranks with halo exchange (strong scaling)."""
+    import torch
+    import torch.distributed as dist
 
     import openequivariance_b200 as oeq
     from openequivariance_b200.distributed import PartitionedConv, ReceiverPartition
-    from openequivariance_b200.graph import radius_graph
     from openequivariance_b200.problems import baseline_problem, real_spherical_harmonics
 
     dev = torch.device("cuda", local)
     n = args.conv_nodes
-    box = 25.0 * (n / 5000.0) ** (1.0 / 3.0)
-    gen = torch.Generator().manual_seed(0)
-    pos = (torch.rand(n, 3, generator=gen, dtype=torch.float64) * box).to(dev)
-    rows, cols, tperm, vec = radius_graph(pos, box, 5.0)
+    rows, cols, vec = _conv_graph(n, dev)
     E = rows.numel()
     det = args.conv_mode == "deterministic"
     problem = baseline_problem("c1")
     conv = oeq.TensorProductConv(problem, deterministic=det)
     part = ReceiverPartition.build(rows, cols, n, world, rank)
-    group = None
-    pc = PartitionedConv(conv, part, group)
+    pc = PartitionedConv(conv, part)
     g2 = torch.Generator(device=dev).manual_seed(1)
     X = torch.randn(n, 5, device=dev, generator=g2)[part.node_lo:part.node_hi].contiguous()
-    Y = real_spherical_harmonics(vec[part.edge_lo:part.edge_hi], 3)[:, 9:16].float().contiguous()
-    W = torch.randn(part.edge_hi - part.edge_lo, 1, device=dev, generator=g2)
-    G = torch.randn(part.n_local, 5, device=dev, generator=g2)
+    Y = real_spherical_harmonics(vec[part.edge_index], 3)[:, 9:16].float().contiguous()
+    W = torch.randn(part.n_edges, 1, device=dev, generator=g2)
+    G = torch.randn(part.n_own, 5, device=dev, generator=g2)
     X.requires_grad_()
     Y.requires_grad_()
     W.requires_grad_()
-    del pos, vec
+    del vec
 
     def step():
         Z = pc(X, Y, W)
@@ -561,32 +667,55 @@ def bench_conv(args, world, rank, local):
     launches = _launches_per_step(step)
     K = args.steps
     elapsed_ms, clocks = _time_steps(step, K, world, local)
-    # Kernel-only timing of this rank's fused backward (the dominant pass), CUDA events.
-    ops = torch.ops.libtorch_tp_jit
-    Xf = torch.randn(world * part.n_max, 5, device=dev)
-    Gf = torch.randn(world * part.n_max, 5, device=dev)
-    tp = part.transpose_perm if det else conv.dummy_transpose_perm
-    ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
-    for _ in range(3):
-        ops.jit_conv_backward(conv.kernel, conv.hash, Xf, Y.detach(), W.detach(), Gf, part.rows,
-                              part.cols, conv.workspace_buffer, tp)
-    ev[0].record()
-    for _ in range(10):
-        ops.jit_conv_backward(conv.kernel, conv.hash, Xf, Y.detach(), W.detach(), Gf, part.rows,
-                              part.cols, conv.workspace_buffer, tp)
-    ev[1].record()
-    torch.cuda.synchronize()
-    t_bwd = ev[0].elapsed_time(ev[1]) / 10
-    El = part.edge_hi - part.edge_lo
-    Np = world * part.n_max
-    bytes_bwd = El * (2 * 7 + 2 * 1) * 4 + El * 16 + (El * 8 if det else 0) + Np * (5 + 5 + 5) * 4
-    peak, peak_src = _peaks()
-    achieved = bytes_bwd / (t_bwd * 1e-3) / 1e9
     value = E * K / (elapsed_ms * 1e-3)
+
+    # Per-rank breakdown (untimed diagnostic pass, CUDA events): each kernel block alone, and
+    # each halo exchange alone (blocking all_to_all_single, every rank in the same order).
+    nl, ni = part.n_local_nodes, part.n_interior
+    Xl = torch.randn(nl, 5, device=dev)
+    Gl = torch.randn(nl, 5, device=dev)
+    Yd, Wd = Y.detach(), W.detach()
+    gX, gY, gW = torch.empty_like(Xl), torch.empty_like(Yd), torch.empty_like(Wd)
+    blocks = {"int": (slice(0, ni), part.rows_int, part.cols_int, part.tperm_int),
+              "bnd": (slice(ni, part.n_edges), part.rows_bnd, part.cols_bnd, part.tperm_bnd)}
+    comp = {}
+    for name, (sl, r_, c_, t_) in blocks.items():
+        if sl.stop > sl.start:
+            comp[f"fwd_{name}"] = _ev_ms(lambda: pc.fwd(Xl, Yd[sl], Wd[sl], r_, c_, t_))
+            comp[f"bwd_{name}"] = _ev_ms(lambda: pc.bwd(Xl, Yd[sl], Wd[sl], Gl, r_, c_, t_, gX,
+                                                          gY[sl], gW[sl]))
+        else:
+            comp[f"fwd_{name}"] = comp[f"bwd_{name}"] = 0.0
+    if world > 1:
+        send = torch.randn(int(part.send_idx.numel()), 5, device=dev)
+        halo = torch.empty(part.n_halo, 5, device=dev)
+        comp["exchange_x"] = _ev_ms(lambda: dist.all_to_all_single(
+            halo, send, part.recv_counts, part.send_counts))
+        comp["exchange_dx"] = _ev_ms(lambda: dist.all_to_all_single(
+            send, halo, part.send_counts, part.recv_counts))
+    keys = sorted(comp)
+    vals = torch.tensor([comp[k] for k in keys], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(vals, op=dist.ReduceOp.MAX)
+    breakdown = {k: float(v) for k, v in zip(keys, vals.tolist())}
+    kern_ms = sum(v for k, v in breakdown.items() if not k.startswith("exchange"))
+    halo_tot = torch.tensor([part.n_halo, part.n_boundary], dtype=torch.int64, device=dev)
+    if world > 1:
+        dist.all_reduce(halo_tot)
+
+    # Roofline of the dominant kernel: the interior-block backward of this rank.
+    t_bwd = comp["bwd_int"]
+    bytes_bwd = conv_bytes(ni, nl, False, det)
+    peak, peak_src = _peaks()
+    achieved = bytes_bwd / (t_bwd * 1e-3) / 1e9 if t_bwd else 0.0
+    t_fwd = comp["fwd_int"]
+    bytes_fwd = conv_bytes(ni, nl, True, det)
+    tr = _traffic(f"conv_{args.conv_mode}:conv_bwd_per_edge")
+    traffic = tr * ni if tr else None
 
     # e2e: host buffers of this rank's inputs and outputs through the same module.
     hX, hY, hW, hG = (t.detach().cpu().pin_memory() for t in (X, Y, W, G))
-    outs = [torch.empty(part.n_local, 5).pin_memory(), torch.empty(part.n_local, 5).pin_memory(),
+    outs = [torch.empty(part.n_own, 5).pin_memory(), torch.empty(part.n_own, 5).pin_memory(),
             torch.empty_like(hY).pin_memory(), torch.empty_like(hW).pin_memory()]
 
     def e2e_step():
@@ -614,19 +743,24 @@ def bench_conv(args, world, rank, local):
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": K,
         "warmup": args.warmup, "ms_per_step": elapsed_ms / K, "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": f"conv: C3 irreps (1x2e x 1x3e -> 1x2e, uvu) fused conv fwd+bwd on a "
-                               f"periodic radius graph, {n} nodes, {E} directed edges, "
-                               f"{args.conv_mode}",
-                   "parallelism": f"receiver-range partition over {world} GPU(s): all-gather X, "
-                                  f"reduce-scatter dX (NCCL)",
+        "config": {"workload": _conv_desc(n, E, args.conv_mode),
+                   "global_edges": E, "nodes": n,
+                   "parallelism": f"receiver-range partition over {world} GPU(s); halo X / dX "
+                                  f"exchanged with NCCL all_to_all_single, overlapped with the "
+                                  f"interior edges",
+                   "halo_nodes_total": int(halo_tot[0]), "boundary_edges_total": int(halo_tot[1]),
                    "l2": "edge arrays larger than L2 (no flush needed)"},
-        "kernels_ms": {"conv_bwd_rank0": t_bwd},
-        "roofline": {"bound": "hbm", "kernel": "conv_bwd", "achieved": achieved, "peak": peak,
-                     "peak_source": peak_src, "unit": "GB/s", "frac": achieved / peak,
-                     "traffic": None, "algorithmic_bytes_per_launch": bytes_bwd},
+        "breakdown_ms_max_over_ranks": breakdown,
+        "kernels_ms_per_step_max_rank": kern_ms,
+        "roofline": {"bound": "hbm", "kernel": "conv_bwd (interior block, rank 0)",
+                     "achieved": achieved, "peak": peak, "peak_source": peak_src, "unit": "GB/s",
+                     "frac": achieved / peak, "traffic": traffic,
+                     "algorithmic_bytes_per_launch": bytes_bwd,
+                     "fwd_frac": bytes_fwd / (t_fwd * 1e-3) / 1e9 / peak if t_fwd else None},
         "e2e": {"value": E * E2 / e2e_s, "unit": UNIT, "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "steps": E2,
-                "path": "PartitionedConv forward+backward, pinned host buffers per rank"},
+                "path": "PartitionedConv forward+backward (public module API), pinned host "
+                        "buffers per rank"},
         "gpu_launches": launches * K,
         "clocks": clocks,
     }
@@ -700,6 +834,34 @@ def bench_sc(args, world, rank, local):
     launches = _launches_per_step(step)
     K = args.steps
     elapsed_ms, clocks = _time_steps(step, K, world, local)
+    # FLOP roofline of the three kernels (CUDA-core FP32; no tensor cores involved): per
+    # (node, channel), M = 219 monomials of degree <= 3 in the 9 components (45 + 165 of them
+    # formed with one multiply each) and 4 padded output components.
+    from torch.profiler import ProfilerActivity, profile
+
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        step()
+        torch.cuda.synchronize()
+    kt = {}
+    names = ("sc_fwd_kernel", "sc_bwd_dx_kernel", "sc_bwd_dcoef_kernel")
+    for e in prof.events():
+        if e.device_type != torch.autograd.DeviceType.CUDA:
+            continue
+        for k in names:
+            if k in e.name:
+                kt[k] = kt.get(k, 0.0) + e.time_range.elapsed_us() / 1e3
+    per_nc = {"sc_fwd_kernel": 2 * 219 * 4 + 210,
+              "sc_bwd_dx_kernel": 9 * (8 + 2) + 45 * (8 + 4 + 2) + 165 * (8 + 6 + 6),
+              "sc_bwd_dcoef_kernel": 2 * 219 * 4 + 210}
+    props = torch.cuda.get_device_properties(dev)
+    mhz = clocks.get("sm_max_mhz") or 1965.0
+    fp32_peak = props.multi_processor_count * 128 * 2 * mhz * 1e6 / 1e12
+    roof = {}
+    for k, f in per_nc.items():
+        if k in kt and kt[k] > 0:
+            tf = f * n * 128 / (kt[k] * 1e-3) / 1e12
+            roof[k] = {"ms": kt[k], "tflops": tf, "frac": tf / fp32_peak,
+                       "flops_per_launch": f * n * 128}
     return {
         "metric": "symmetric contraction fwd+bwd nodes/sec", "value": n * world * K / (elapsed_ms * 1e-3),
         "unit": "nodes/s", "n_gpus": world, "steps": K, "warmup": args.warmup,
@@ -709,7 +871,15 @@ def bench_sc(args, world, rank, local):
                                "128x0e+128x1o, correlation 3, 10 elements",
                    "nodes_per_gpu": n, "parallelism": f"dp{world} (independent node shards)"},
         "gpu_launches": launches * K, "clocks": clocks,
+        "roofline": {"bound": "fp32 FMA (CUDA cores)", "unit": "TFLOP/s", "peak": fp32_peak,
+                     "peak_source": "nominal: SMs x 128 FP32 lanes x 2 x max SM clock",
+                     "kernels": roof},
     }
+
+
+def _extra(line, keys=("value", "unit", "ms_per_step", "kernels_ms", "roofline",
+                       "tensor_roofline", "e2e", "cpu_baseline", "config", "metric")):
+    return {k: line[k] for k in keys if k in line}
 
 
 def main():
@@ -719,6 +889,19 @@ def main():
         line = bench_reference(args, world, rank)
     elif args.workload == "conv":
         line = bench_conv(args, world, rank, local)
+        if world == 1 and not args.no_extras:
+            # The batch-TP headline (C2) and the symmetric contraction,
+            # each with its own roofline, as extra keys of the N=1 line.
+            import torch
+
+            torch.cuda.empty_cache()
+            a2 = argparse.Namespace(**vars(args))
+            a2.workload = "c2"
+            line["tp_c2"] = _extra(bench_tp(a2, world, rank, local))
+            torch.cuda.empty_cache()
+            a3 = argparse.Namespace(**vars(args))
+            a3.workload = "sc"
+            line["sc_c5"] = _extra(bench_sc(a3, world, rank, local))
     elif args.workload == "sc":
         line = bench_sc(args, world, rank, local)
     else:

@@ -202,6 +202,11 @@ def _register_sc():
     def _fake_scb(x, perm, elem_offsets, coef, grad_out, out_col, out_step, degree):
         return torch.empty_like(x), torch.empty_like(coef)
 
+    @torch.library.register_fake("oeqb200::conv_backward_into")
+    def _fake_cbi(kernel, hash, L1_in, L2_in, W, L3_grad, rows, cols, workspace, perm,
+                  L1_grad, L2_grad, W_grad):
+        return None
+
 
 def _register_autocast():
     for name in ("jit_tp_forward", "jit_tp_backward", "jit_tp_double_backward",

@@ -320,6 +320,12 @@ Tensor jit_conv_forward(Tensor json_bytes, int64_t hash, Tensor L1_in, Tensor L2
   return L3_out;
 }
 
+// Convolution backward into caller-provided gradient tensors (contiguous; e.g. row slices
+// of larger buffers).  Shared by jit_conv_backward and oeqb200::conv_backward_into.
+void conv_backward_impl(const PlanInfo& k, const ConvIdx& c, Tensor L1_in, Tensor L2_in,
+                        Tensor W, Tensor L3_grad, Tensor rows, Tensor cols, Tensor workspace,
+                        Tensor transpose_perm, Tensor& L1_grad, Tensor& L2_grad, Tensor& W_grad);
+
 std::tuple<Tensor, Tensor, Tensor> jit_conv_backward(Tensor json_bytes, int64_t hash,
                                                      Tensor L1_in, Tensor L2_in, Tensor W,
                                                      Tensor L3_grad, Tensor rows, Tensor cols,
@@ -333,6 +339,32 @@ std::tuple<Tensor, Tensor, Tensor> jit_conv_backward(Tensor json_bytes, int64_t 
   Tensor L1_grad = at::empty_like(L1_in, at::MemoryFormat::Contiguous);
   Tensor L2_grad = at::empty_like(L2_in, at::MemoryFormat::Contiguous);
   Tensor W_grad = at::empty_like(W, at::MemoryFormat::Contiguous);
+  conv_backward_impl(k, c, L1_in, L2_in, W, L3_grad, rows, cols, workspace, transpose_perm,
+                     L1_grad, L2_grad, W_grad);
+  return {L1_grad, L2_grad, W_grad};
+}
+
+void conv_backward_into(Tensor json_bytes, int64_t hash, Tensor L1_in, Tensor L2_in, Tensor W,
+                        Tensor L3_grad, Tensor rows, Tensor cols, Tensor workspace,
+                        Tensor transpose_perm, Tensor L1_grad, Tensor L2_grad, Tensor W_grad) {
+  const PlanInfo& k = get_plan(json_bytes, hash, tensor_device(L1_in));
+  ConvIdx c = check_conv_common(k, L1_in, L2_in, rows, cols, workspace, transpose_perm,
+                                "OpenEquivariance_conv_atomic_backward");
+  check_tensor(L3_grad, {c.nodes, k.L3_dim}, k.dtype, "L3_grad");
+  check_weights(k, W, c.nnz, "W");
+  check_tensor(L1_grad, {c.nodes, k.L1_dim}, k.dtype, "L1_grad");
+  check_tensor(L2_grad, {c.nnz, k.L2_dim}, k.dtype, "L2_grad");
+  check_weights(k, W_grad, c.nnz, "W_grad");
+  TORCH_CHECK(L1_grad.is_contiguous() && L2_grad.is_contiguous() && W_grad.is_contiguous(),
+              "conv_backward_into: gradient outputs must be contiguous");
+  c10::cuda::CUDAGuard guard(L1_in.device());
+  conv_backward_impl(k, c, L1_in, L2_in, W, L3_grad, rows, cols, workspace, transpose_perm,
+                     L1_grad, L2_grad, W_grad);
+}
+
+void conv_backward_impl(const PlanInfo& k, const ConvIdx& c, Tensor L1_in, Tensor L2_in,
+                        Tensor W, Tensor L3_grad, Tensor rows, Tensor cols, Tensor workspace,
+                        Tensor transpose_perm, Tensor& L1_grad, Tensor& L2_grad, Tensor& W_grad) {
   Tensor x = L1_in.contiguous(), y = L2_in.contiguous(), w = W.contiguous(),
          gz = L3_grad.contiguous(), r = rows.contiguous(), cl = cols.contiguous();
   Tensor tp = k.deterministic ? transpose_perm.contiguous() : Tensor();
@@ -351,7 +383,6 @@ std::tuple<Tensor, Tensor, Tensor> jit_conv_backward(Tensor json_bytes, int64_t 
       c.nodes, ws.data_ptr(), static_cast<size_t>(ws.numel()),
       k.deterministic ? tp.data_ptr<int64_t>() : nullptr, st));
   if (chk) check_status(k, st);
-  return {L1_grad, L2_grad, W_grad};
 }
 
 std::tuple<Tensor, Tensor, Tensor, Tensor> jit_conv_double_backward(
@@ -514,12 +545,14 @@ std::tuple<Tensor, Tensor> sc_backward(Tensor x, Tensor perm, Tensor elem_offset
 TORCH_LIBRARY(oeqb200, m) {
   m.def("set_device_checks(bool enabled) -> bool", &set_device_checks);
   m.def("check_device_status() -> ()", &check_device_status);
+  m.def("conv_backward_into(Tensor json_bytes, int hash, Tensor L1_in, Tensor L2_in, Tensor W, Tensor L3_grad, Tensor rows, Tensor cols, Tensor workspace, Tensor transpose_perm, Tensor(a!) L1_grad, Tensor(b!) L2_grad, Tensor(c!) W_grad) -> ()");
   m.def("sc_forward(Tensor x, Tensor perm, Tensor elem_offsets, Tensor coef, int[] out_col, int[] out_step, int out_dim, int degree) -> Tensor");
   m.def("sc_backward(Tensor x, Tensor perm, Tensor elem_offsets, Tensor coef, Tensor grad_out, int[] out_col, int[] out_step, int degree) -> (Tensor, Tensor)");
 }
 
 TORCH_LIBRARY_IMPL(oeqb200, CUDA, m) {
   m.impl("sc_forward", &sc_forward);
+  m.impl("conv_backward_into", &conv_backward_into);
   m.impl("sc_backward", &sc_backward);
 }
 

@@ -1,28 +1,35 @@
-"""Multi-GPU fused convolution: receiver-range node partitions over ``torch.distributed``.
+"""Multi-GPU fused convolution: receiver-range node partitions with halo exchange.
 
 Each rank owns a contiguous range of receiver nodes (ranges balanced by edge count) and every
-edge whose receiver it owns; with receiver-sorted edges (``graph.coord_graph``) that is a
-contiguous slice of the edge list.  Edge data (Y, W) and the rank's node data (X, Z rows) stay
-local.  One pass exchanges node data only:
+edge whose receiver it owns.  With nodes numbered in a spatial order (``graph.morton_order``)
+a contiguous range is a compact region of space, so only the senders near its surface (the
+*halo*) belong to other ranks.  A rank's edges fall into two blocks, each receiver-sorted:
 
-* forward: ``all_gather`` of X (each rank's senders may live anywhere), then the fused
-  convolution of the local edges into the rank's Z rows;
-* backward: dY and dW are local per edge; each rank's dX contributions to every sender are
-  summed onto the owners with ``reduce_scatter``.
+* interior edges, whose sender the rank owns;
+* boundary edges, whose sender is a halo node (plus up to three edges with an owned sender,
+  so that the boundary block starts at a multiple of 4 edges).
 
-Node ranges are padded to a common size so the collectives are the fixed-size
-``all_gather_into_tensor`` / ``reduce_scatter_tensor``; the local edges index that padded
-global space (rank r's node v sits at row ``r * n_max + (v - lo_r)``), so the single-GPU
-kernels run unchanged.  Every rank issues the same collectives in the same order.  Sums
-over ranks use the backend's fixed reduction order, so deterministic mode stays reproducible
-run to run.  The reference has no multi-GPU path; this follows the receiver-range plan for
-its convolution (``TensorProductConv.forward``, ``_torch/TensorProductConv.py:145-200``).
+Per pass, node data crosses NVLink once each way, overlapped with the interior edges:
+
+* forward: the rank sends the X rows its neighbours need (``all_to_all_single``, NCCL,
+  started asynchronously) and meanwhile runs the fused convolution of its interior edges;
+  once the halo rows have arrived it runs the boundary edges and adds their messages;
+* backward: the boundary edges go first (their dX contributions belong to halo nodes), the
+  contributions travel back to their owners while the interior edges run, and each owner
+  adds what it received in rank order (deterministic: one writer per row and call).
+
+dY and dW stay local per edge.  Node ids are local: ``[0, n_own)`` the owned nodes,
+``[n_own, n_own + n_halo)`` the halo nodes grouped by owning rank (ascending global id), so the
+single-GPU kernels run unchanged on a node space of ``n_own + n_halo`` rows.  Every rank issues
+the same collectives in the same order.  The reference has no multi-GPU path (its
+``tests/multidevice_test.py:14-30`` runs independent replicas); this partitions its fused
+convolution (``TensorProductConv.forward``, ``_torch/TensorProductConv.py:145-200``).
 """
 
 from __future__ import annotations
 
-from dataclasses import dataclass
-from typing import Callable, Optional
+from dataclasses import dataclass, field
+from typing import Callable, List, Optional
 
 import torch
 import torch.distributed as dist
@@ -30,122 +37,235 @@ import torch.distributed as dist
 
 @dataclass
 class ReceiverPartition:
-    """This rank's share of a receiver-sorted graph."""
+    """This rank's share of a receiver-sorted graph (see the module docstring)."""
 
     rank: int
     world: int
     num_nodes: int
-    node_lo: int                 # owned receiver nodes [node_lo, node_hi)
+    node_lo: int                   # owned nodes [node_lo, node_hi) (global ids)
     node_hi: int
-    n_max: int                   # padded node-range size (all ranks)
-    edge_lo: int                 # owned edges [edge_lo, edge_hi) of the global edge list
-    edge_hi: int
-    rows: torch.Tensor           # local edges, receivers in padded global index space
-    cols: torch.Tensor           # local edges, senders in padded global index space
-    transpose_perm: torch.Tensor  # local edges in (sender, receiver) order
+    halo_nodes: torch.Tensor       # [n_halo] global ids of the halo, grouped by owner rank
+    recv_counts: List[int]         # halo rows arriving from each rank
+    send_idx: torch.Tensor         # owned local ids sent to the other ranks, by destination
+    send_counts: List[int]         # rows sent to each rank
+    edge_index: torch.Tensor       # [E_local] global edge ids in local order (interior first)
+    n_interior: int
+    rows_int: torch.Tensor         # interior edges: local receiver / sender ids
+    cols_int: torch.Tensor
+    rows_bnd: torch.Tensor         # boundary edges: local receiver / sender (halo) ids
+    cols_bnd: torch.Tensor
+    tperm_int: torch.Tensor        # each block's edges in (sender, receiver) order
+    tperm_bnd: torch.Tensor
+    send_splits: List[torch.Tensor] = field(default_factory=list)  # send_idx per destination
+    n_boundary_local: int = 0      # boundary-block edges whose sender is owned (0..3)
 
     @property
-    def n_local(self) -> int:
+    def n_own(self) -> int:
         return self.node_hi - self.node_lo
+
+    @property
+    def n_halo(self) -> int:
+        return int(self.halo_nodes.numel())
+
+    @property
+    def n_local_nodes(self) -> int:
+        return self.n_own + self.n_halo
+
+    @property
+    def n_edges(self) -> int:
+        return int(self.edge_index.numel())
+
+    @property
+    def n_boundary(self) -> int:
+        return self.n_edges - self.n_interior
 
     @staticmethod
     def build(rows: torch.Tensor, cols: torch.Tensor, num_nodes: int, world: int, rank: int
               ) -> "ReceiverPartition":
-        """Partition of receiver-sorted (rows, cols); node ranges balance the edge counts."""
+        """Partition of the receiver-sorted global graph (rows, cols), on their device.
+
+        Every rank calls this with the whole graph and computes the same node ranges; no
+        communication is needed.  Node ranges balance the edge counts.
+        """
         rows = rows.to(torch.int64)
         cols = cols.to(torch.int64)
+        dev = rows.device
         E = rows.numel()
-        # Node boundaries at equal edge quantiles, snapped to receiver boundaries.
-        deg_cum = torch.searchsorted(rows, torch.arange(num_nodes + 1, device=rows.device))
-        targets = torch.tensor([E * r // world for r in range(world + 1)], device=rows.device)
+        deg_cum = torch.searchsorted(rows, torch.arange(num_nodes + 1, device=dev))
+        targets = torch.tensor([E * r // world for r in range(world + 1)], device=dev)
         bounds = torch.searchsorted(deg_cum, targets).clamp(max=num_nodes)
         bounds[0], bounds[-1] = 0, num_nodes
         bounds = torch.cummax(bounds, 0).values
         b = bounds.tolist()
-        n_max = max(1, max(b[r + 1] - b[r] for r in range(world)))
+        ecut = deg_cum[bounds].tolist()
+        owner = torch.searchsorted(bounds[1:], torch.arange(num_nodes, device=dev), right=True)
         lo, hi = b[rank], b[rank + 1]
-        e_lo, e_hi = int(deg_cum[lo]), int(deg_cum[hi])
-        owner = torch.searchsorted(bounds[1:], torch.arange(num_nodes, device=rows.device),
-                                   right=True)
-        padded = owner * n_max + (torch.arange(num_nodes, device=rows.device) - bounds[owner])
-        r_loc = padded[rows[e_lo:e_hi]]
-        c_loc = padded[cols[e_lo:e_hi]]
-        # Local transpose permutation: local edges in (sender, receiver) order.
-        tperm = torch.argsort(c_loc * (world * n_max) + r_loc, stable=True)
-        return ReceiverPartition(rank, world, num_nodes, lo, hi, n_max, e_lo, e_hi,
-                                 r_loc, c_loc, tperm)
+        e_lo, e_hi = ecut[rank], ecut[rank + 1]
+        n_own = hi - lo
+        r_g, c_g = rows[e_lo:e_hi], cols[e_lo:e_hi]
+        local_src = owner[c_g] == rank
+        halo = torch.unique(c_g[~local_src])  # sorted global ids, hence grouped by owner
+        # The boundary block starts at a multiple of 4 edges, so that its Y / dY rows are
+        # 16-byte aligned whenever the caller's arrays are (the vectorised edge kernels need
+        # that): the last (count % 4) edges with a local sender join the boundary block.
+        inner = local_src.clone()
+        extra = int(inner.sum()) % 4 if halo.numel() else 0
+        if extra:
+            inner[torch.nonzero(inner).flatten()[-extra:]] = False
+        idx = torch.arange(e_lo, e_hi, device=dev)
+        recv_counts = torch.bincount(owner[halo], minlength=world).tolist() if halo.numel() \
+            else [0] * world
+        rows_int, cols_int = r_g[inner] - lo, c_g[inner] - lo
+        rows_bnd = r_g[~inner] - lo
+        cb = c_g[~inner]
+        in_halo = n_own + torch.searchsorted(halo, cb).clamp(max=max(halo.numel() - 1, 0))
+        cols_bnd = torch.where(owner[cb] == rank, cb - lo, in_halo)
+        # What every other rank needs from this one: the senders of its edges that this rank
+        # owns, in ascending global id (the order that rank expects them in its halo).
+        send_splits, send_counts = [], []
+        for r in range(world):
+            if r == rank:
+                send_splits.append(torch.empty(0, dtype=torch.int64, device=dev))
+            else:
+                cr = cols[ecut[r]:ecut[r + 1]]
+                send_splits.append(torch.unique(cr[owner[cr] == rank]) - lo)
+            send_counts.append(int(send_splits[-1].numel()))
+        n_loc = n_own + int(halo.numel())
+
+        def tperm(rr, cc):
+            return torch.argsort(cc * max(n_loc, 1) + rr, stable=True)
+
+        return ReceiverPartition(
+            rank, world, num_nodes, lo, hi, halo, recv_counts, torch.cat(send_splits),
+            send_counts, torch.cat([idx[inner], idx[~inner]]), int(inner.sum()),
+            rows_int, cols_int, rows_bnd, cols_bnd, tperm(rows_int, cols_int),
+            tperm(rows_bnd, cols_bnd), send_splits, extra)
 
 
 def _local_conv_ops(conv):
-    """Forward / backward of the fused convolution module on padded global node arrays."""
+    """(forward, backward-into) of the fused convolution module on a local node space.
+
+    ``fwd(X, Y, W, rows, cols, tperm) -> Z`` with Z of X's row count;
+    ``bwd(X, Y, W, G, rows, cols, tperm, gX, gY, gW)`` writes the gradients into the given
+    tensors (contiguous row slices of the callers' buffers).
+    """
     ops = torch.ops.libtorch_tp_jit
 
-    def fwd(X, Y, W, part):
-        perm = part.transpose_perm if conv.deterministic else conv.dummy_transpose_perm
-        return ops.jit_conv_forward(conv.kernel, conv.hash, X, Y, W, conv.L3_dim, part.rows,
-                                    part.cols, conv.workspace_buffer, perm)
+    def fwd(X, Y, W, rows, cols, tperm):
+        perm = tperm if conv.deterministic else conv.dummy_transpose_perm
+        return ops.jit_conv_forward(conv.kernel, conv.hash, X, Y, W, conv.L3_dim, rows, cols,
+                                    conv.workspace_buffer, perm)
 
-    def bwd(X, Y, W, G, part):
-        perm = part.transpose_perm if conv.deterministic else conv.dummy_transpose_perm
-        return ops.jit_conv_backward(conv.kernel, conv.hash, X, Y, W, G, part.rows, part.cols,
-                                     conv.workspace_buffer, perm)
+    def bwd(X, Y, W, G, rows, cols, tperm, gX, gY, gW):
+        perm = tperm if conv.deterministic else conv.dummy_transpose_perm
+        torch.ops.oeqb200.conv_backward_into(conv.kernel, conv.hash, X, Y, W, G, rows, cols,
+                                             conv.workspace_buffer, perm, gX, gY, gW)
 
     return fwd, bwd
 
 
-class _PartitionedConvFn(torch.autograd.Function):
+class _HaloConvFn(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, X_local, Y, W, part, fwd, bwd, group):
-        n_max, world, rank = part.n_max, part.world, part.rank
-        X_pad = X_local.new_zeros(n_max, X_local.shape[1])
-        X_pad[: part.n_local] = X_local
-        if world == 1:
-            X_full = X_pad
+    def forward(ctx, X_own, Y, W, pc):
+        part = pc.part
+        n_own, n_loc, ni = part.n_own, part.n_local_nodes, part.n_interior
+        shared = pc.shared_weights
+        exchange = part.world > 1
+        if part.n_halo == 0:
+            X_loc = X_own.contiguous()
         else:
-            X_full = X_local.new_empty(world * n_max, X_local.shape[1])
-            dist.all_gather_into_tensor(X_full, X_pad, group=group)
-        Z_full = fwd(X_full, Y, W, part)
-        ctx.save_for_backward(X_full, Y, W)
-        ctx.part, ctx.bwd, ctx.group = part, bwd, group
-        return Z_full[rank * n_max: rank * n_max + part.n_local].clone()
+            X_loc = X_own.new_empty(n_loc, X_own.shape[1])
+            X_loc[:n_own].copy_(X_own)
+        work = None
+        if exchange:
+            send = X_own.index_select(0, part.send_idx)
+            work = dist.all_to_all_single(X_loc[n_own:], send, part.recv_counts,
+                                          part.send_counts, group=pc.group, async_op=True)
+        Wi = W if shared else W[:ni]
+        Z = pc.fwd(X_loc, Y[:ni], Wi, part.rows_int, part.cols_int, part.tperm_int)
+        if work is not None:
+            work.wait()
+        if part.n_boundary:
+            Wb = W if shared else W[ni:]
+            Z.add_(pc.fwd(X_loc, Y[ni:], Wb, part.rows_bnd, part.cols_bnd, part.tperm_bnd))
+        ctx.save_for_backward(X_loc, Y, W)
+        ctx.pc = pc
+        return Z[:n_own]
 
     @staticmethod
-    def backward(ctx, gZ_local):
+    def backward(ctx, gZ):
         if torch.is_grad_enabled():
             raise RuntimeError("double backward through PartitionedConv is not supported")
-        X_full, Y, W = ctx.saved_tensors
-        part = ctx.part
-        n_max, rank = part.n_max, part.rank
-        gZ_full = gZ_local.new_zeros(part.world * n_max, gZ_local.shape[1])
-        gZ_full[rank * n_max: rank * n_max + part.n_local] = gZ_local
-        gX_full, gY, gW = ctx.bwd(X_full, Y, W, gZ_full, part)
-        if part.world == 1:
-            gX_pad = gX_full
+        X_loc, Y, W = ctx.saved_tensors
+        pc = ctx.pc
+        part = pc.part
+        n_own, n_loc, ni = part.n_own, part.n_local_nodes, part.n_interior
+        shared = pc.shared_weights
+        if part.n_halo == 0:
+            gZ_loc = gZ.contiguous()
         else:
-            gX_pad = gX_full.new_empty(n_max, gX_full.shape[1])
-            dist.reduce_scatter_tensor(gX_pad, gX_full.contiguous(), op=dist.ReduceOp.SUM,
-                                       group=ctx.group)
-        return gX_pad[: part.n_local], gY, gW, None, None, None, None
+            gZ_loc = gZ.new_zeros(n_loc, gZ.shape[1])
+            gZ_loc[:n_own].copy_(gZ)
+        gY = torch.empty_like(Y)
+        gW = torch.empty_like(W)
+        d1 = X_loc.shape[1]
+        work, back = None, None
+        if part.n_boundary or part.world > 1:
+            gX_b = X_loc.new_empty(n_loc, d1)
+            gW_b = torch.empty_like(W) if shared else gW[ni:]
+            if part.n_boundary:
+                pc.bwd(X_loc, Y[ni:], W if shared else W[ni:], gZ_loc, part.rows_bnd,
+                       part.cols_bnd, part.tperm_bnd, gX_b, gY[ni:], gW_b)
+            else:
+                gX_b.zero_()
+                if shared:
+                    gW_b.zero_()
+            if part.world > 1:
+                back = X_loc.new_empty(int(part.send_idx.numel()), d1)
+                work = dist.all_to_all_single(back, gX_b[n_own:], part.send_counts,
+                                              part.recv_counts, group=pc.group, async_op=True)
+        gX_i = X_loc.new_empty(n_loc, d1)
+        gW_i = torch.empty_like(W) if shared else gW[:ni]
+        pc.bwd(X_loc, Y[:ni], W if shared else W[:ni], gZ_loc, part.rows_int, part.cols_int,
+               part.tperm_int, gX_i, gY[:ni], gW_i)
+        gX = gX_i[:n_own]
+        if part.n_boundary_local:
+            gX.add_(gX_b[:n_own])  # the boundary block's edges with an owned sender
+        if work is not None:
+            work.wait()
+            off = 0
+            for r, cnt in enumerate(part.send_counts):
+                if cnt:
+                    gX.index_add_(0, part.send_splits[r], back[off:off + cnt])
+                off += cnt
+        if shared:
+            gW = gW_i + gW_b if (part.n_boundary or part.world > 1) else gW_i
+            if part.world > 1:
+                dist.all_reduce(gW, group=pc.group)
+        return gX, gY, gW, None
 
 
 class PartitionedConv(torch.nn.Module):
     """Fused convolution of a receiver-partitioned graph (one rank per GPU).
 
-    ``forward(X_local, Y_local, W_local)`` takes this rank's node rows of X and its edges' Y
-    and W (rows ``part.edge_lo:part.edge_hi`` of the receiver-sorted edge arrays) and returns
-    this rank's rows of Z.  ``conv`` is a ``TensorProductConv`` (atomic or deterministic);
-    ``local_ops`` replaces its kernels with another (forward, backward) pair of the same
-    signature, e.g. a CPU implementation for host-side tests.
+    ``forward(X_own, Y_local, W_local)`` takes this rank's node rows of X
+    (``X[part.node_lo:part.node_hi]``) and its edges' Y and W in the partition's local edge
+    order (``Y[part.edge_index]``: interior edges first) and returns this rank's rows of Z.
+    ``conv`` is a ``TensorProductConv`` (atomic or deterministic).  ``local_ops`` replaces its
+    kernels with another (forward, backward-into) pair of the same signature (e.g. a CPU
+    implementation for host-side tests); ``shared_weights`` must then be given.
     """
 
     def __init__(self, conv, part: ReceiverPartition, group=None,
-                 local_ops: Optional[tuple[Callable, Callable]] = None):
+                 local_ops: Optional[tuple[Callable, Callable]] = None,
+                 shared_weights: Optional[bool] = None):
         super().__init__()
         self.conv = conv
         self.part = part
         self.group = group
         self.fwd, self.bwd = local_ops if local_ops is not None else _local_conv_ops(conv)
+        self.shared_weights = (bool(conv.config.shared_weights) if shared_weights is None
+                               else shared_weights)
 
-    def forward(self, X_local, Y_local, W_local):
-        return _PartitionedConvFn.apply(X_local, Y_local, W_local, self.part, self.fwd, self.bwd,
-                                        self.group)
+    def forward(self, X_own, Y_local, W_local):
+        return _HaloConvFn.apply(X_own, Y_local, W_local, self)

@@ -11,7 +11,11 @@ step never leave the GPU:
   distance below the cutoff in a periodic cubic box, found through a cell list (cells of
   side >= cutoff, the 27 neighbouring cells of each node's cell);
 * ``coord_graph``: receiver-sorted rows/cols plus the transpose permutation, as
-  ``CoordGraph``.
+  ``CoordGraph``;
+* ``morton_order``: a spatial node numbering (Z-order curve of the positions), so that
+  contiguous node ranges, which the multi-GPU convolution assigns to ranks, are compact
+  regions with small halos.  The reference has no counterpart (its graphs are partitioned
+  by nobody).
 """
 
 from __future__ import annotations
@@ -19,6 +23,31 @@ from __future__ import annotations
 from typing import Tuple
 
 import torch
+
+
+def _spread_bits(v: torch.Tensor) -> torch.Tensor:
+    """Inserts two zero bits after each of the 21 low bits of v (int64)."""
+    v = v & 0x1FFFFF
+    v = (v | (v << 32)) & 0x1F00000000FFFF
+    v = (v | (v << 16)) & 0x1F0000FF0000FF
+    v = (v | (v << 8)) & 0x100F00F00F00F00F
+    v = (v | (v << 4)) & 0x10C30C30C30C30C3
+    v = (v | (v << 2)) & 0x1249249249249249
+    return v
+
+
+def morton_order(pos: torch.Tensor, box: float, bits: int = 16) -> torch.Tensor:
+    """Permutation listing the nodes along a Z-order (Morton) curve of their positions.
+
+    Positions are wrapped into the periodic box and quantised to ``2**bits`` cells per axis;
+    node ``order[k]`` gets the new id ``k``.  Renumber with ``pos = pos[order]`` (and every
+    per-node array alike) before building the graph.
+    """
+    assert 1 <= bits <= 21
+    scale = float(1 << bits) / box
+    q = torch.clamp((torch.remainder(pos, box) * scale).to(torch.int64), 0, (1 << bits) - 1)
+    code = _spread_bits(q[:, 0]) | (_spread_bits(q[:, 1]) << 1) | (_spread_bits(q[:, 2]) << 2)
+    return torch.argsort(code, stable=True)
 
 
 def coord_graph(rows: torch.Tensor, cols: torch.Tensor, num_nodes: int

@@ -1,0 +1,121 @@
+"""Kernels launch on the caller's current stream, with the expected kernels per pass.
+
+Adapts the reference's ``tests/stream_test.py:98-379``: every operator (batch TP forward,
+backward, double backward; atomic and deterministic convolution forward, backward, double
+backward) runs repeatedly on two user streams of different priority under the profiler.  This
+library's kernels (namespace ``oeqb``) must run on exactly those two streams, the same number
+of times on each, and with the kernel names the pass is expected to launch.  The reference pins
+its JIT kernel names (``forward``, ``backward``, ``double_backward_A/B``, ``fixup_*``); the
+names here are this library's, matched by the pass they belong to.
+"""
+
+import json
+
+import numpy as np
+import pytest
+import torch
+from torch.profiler import ProfilerActivity, profile
+
+pytestmark = pytest.mark.gpu
+
+COUNT = 5
+
+
+def _problem():
+    import openequivariance_b200 as oeq
+
+    return oeq.TPProblem("1x2e", "1x3e", "1x2e", [(0, 0, 0, "uvu", True)],
+                         shared_weights=False, internal_weights=False,
+                         irrep_dtype=np.float32, weight_dtype=np.float32)
+
+
+def _executables():
+    import openequivariance_b200 as oeq
+
+    prob = _problem()
+    g = torch.Generator(device="cuda").manual_seed(0)
+    N = 1000
+    X, Y, W = (torch.rand(N, d, device="cuda", generator=g)
+               for d in (prob.irreps_in1.dim, prob.irreps_in2.dim, prob.weight_numel))
+    rows = torch.tensor([0, 1, 1, 2], device="cuda")
+    cols = torch.tensor([1, 0, 2, 1], device="cuda")
+    perm = torch.argsort(cols * 3 + rows)
+    Xc, Yc, Wc = (torch.rand(n, d, device="cuda", generator=g)
+                  for n, d in ((3, prob.irreps_in1.dim), (4, prob.irreps_in2.dim),
+                               (4, prob.weight_numel)))
+    tp = oeq.TensorProduct(prob)
+    conv_a = oeq.TensorProductConv(prob, deterministic=False)
+    conv_d = oeq.TensorProductConv(prob, deterministic=True)
+
+    def passes(fn, args):
+        leaf = [a.clone().requires_grad_(True) for a in args[:3]]
+
+        def fwd():
+            with torch.no_grad():
+                fn(*args)
+
+        def bwd():
+            z = fn(*leaf, *args[3:])
+            torch.autograd.grad(z, leaf, torch.ones_like(z))
+
+        def dbl():
+            z = fn(*leaf, *args[3:])
+            g = torch.autograd.grad(z, leaf, torch.ones_like(z), create_graph=True)
+            torch.autograd.grad(sum(t.sum() for t in g), leaf, allow_unused=True)
+
+        return fwd, bwd, dbl
+
+    out = {}
+    for name, fn, args in (("tp", tp, (X, Y, W)),
+                           ("conv_atomic", conv_a, (Xc, Yc, Wc, rows, cols)),
+                           ("conv_det", conv_d, (Xc, Yc, Wc, rows, cols, perm))):
+        f, b, d = passes(fn, args)
+        # Expected kernels of one call, by the pass whose name they carry: the forward pass
+        # launches forward kernels only; a backward call re-runs the forward (autograd) and
+        # then backward kernels; a double-backward call adds the double-backward kernels,
+        # which are forward- and backward-shaped.
+        out[f"{name}_fwd"] = (f, {"fwd"})
+        out[f"{name}_bwd"] = (b, {"fwd", "bwd"})
+        out[f"{name}_double_bwd"] = (d, {"fwd", "bwd"})
+    return out
+
+
+EXEC_NAMES = [f"{m}_{p}" for m in ("tp", "conv_atomic", "conv_det")
+              for p in ("fwd", "bwd", "double_bwd")]
+
+
+def _kernel_events(trace_path):
+    with open(trace_path) as f:
+        trace = json.load(f)
+    return [e for e in trace["traceEvents"]
+            if e.get("cat") == "kernel" and "oeqb::" in e.get("name", "")]
+
+
+@pytest.mark.parametrize("which", EXEC_NAMES)
+def test_separate_streams(which, tmp_path, cuda_device):
+    fn, passes = _executables()[which]
+    fn()  # plans built and kernels loaded outside the profile
+    torch.cuda.synchronize()
+    streams = [torch.cuda.Stream(priority=p) for p in (-1, 0)]
+    with profile(activities=[ProfilerActivity.CPU, ProfilerActivity.CUDA]) as prof:
+        for s in streams:
+            with torch.cuda.stream(s):
+                for _ in range(COUNT):
+                    fn()
+        torch.cuda.synchronize()
+    prof.export_chrome_trace(str(tmp_path / "trace.json"))
+    ev = _kernel_events(tmp_path / "trace.json")
+    assert ev, "no kernel of this library ran"
+    by_stream = {}
+    for e in ev:
+        by_stream.setdefault(e["args"]["stream"], []).append(e["name"])
+    assert len(by_stream) == 2, f"kernels ran on {sorted(by_stream)} instead of two user streams"
+    counts = [len(v) for v in by_stream.values()]
+    assert counts[0] == counts[1] and counts[0] % COUNT == 0, counts
+    seen = set()
+    for names in by_stream.values():
+        for n in names:
+            tags = {t for t in ("fwd", "bwd") if t in n}
+            assert tags, f"unexpected kernel {n}"
+            seen |= tags
+    assert seen == passes, f"{which}: kernels of passes {sorted(seen)}, expected {sorted(passes)}"
