@@ -58,6 +58,8 @@ def _args():
                     help="row chunks per e2e step, one CUDA stream each (copies in both "
                          "directions overlap with each other and with the kernels)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-graph", action="store_true",
+                    help="conv: time the eager step instead of its CUDA-graph replay")
     ap.add_argument("--no-extras", action="store_true",
                     help="at N=1, skip the extra C2 TP and symmetric-contraction lines")
     return ap.parse_args()
@@ -659,14 +661,36 @@ def bench_conv(args, world, rank, local):
 
     def step():
         Z = pc(X, Y, W)
-        torch.autograd.grad(Z, (X, Y, W), G)
+        return torch.autograd.grad(Z, (X, Y, W), G)
 
     for _ in range(args.warmup):
         step()
     torch.cuda.synchronize()
     launches = _launches_per_step(step)
+    # The whole step (forward, autograd backward, both NCCL exchanges and every small torch
+    # op) is captured once into a CUDA graph and replayed: one launch per step instead of ~25,
+    # so the ranks stay in step with each other (at 8 GPUs the eager step needs more host
+    # time than device time).  Every replay runs every kernel of the step.
+    graph = None
+    run = step
+    if not args.no_graph:
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            for _ in range(2):
+                step()
+        torch.cuda.current_stream(dev).wait_stream(side)
+        torch.cuda.synchronize()
+        _barrier(world)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            static_out = step()  # noqa: F841  (outputs live in the graph's pool)
+        run = graph.replay
+        for _ in range(args.warmup):
+            run()
+        torch.cuda.synchronize()
     K = args.steps
-    elapsed_ms, clocks = _time_steps(step, K, world, local)
+    elapsed_ms, clocks = _time_steps(run, K, world, local)
     value = E * K / (elapsed_ms * 1e-3)
 
     # Per-rank breakdown (untimed diagnostic pass, CUDA events): each kernel block alone, and
@@ -749,9 +773,11 @@ def bench_conv(args, world, rank, local):
                                   f"exchanged with NCCL all_to_all_single, overlapped with the "
                                   f"interior edges",
                    "halo_nodes_total": int(halo_tot[0]), "boundary_edges_total": int(halo_tot[1]),
+                   "cuda_graph": graph is not None,
                    "l2": "edge arrays larger than L2 (no flush needed)"},
         "breakdown_ms_max_over_ranks": breakdown,
         "kernels_ms_per_step_max_rank": kern_ms,
+        "exposed_non_kernel_ms_per_step": elapsed_ms / K - kern_ms,
         "roofline": {"bound": "hbm", "kernel": "conv_bwd (interior block, rank 0)",
                      "achieved": achieved, "peak": peak, "peak_source": peak_src, "unit": "GB/s",
                      "frac": achieved / peak, "traffic": traffic,
@@ -766,6 +792,7 @@ def bench_conv(args, world, rank, local):
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline_conv(rows, cols)
+    del graph, run  # release the captured NCCL work before the process group goes
     return line
 
 

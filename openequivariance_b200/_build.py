@@ -32,7 +32,7 @@ ARCH = "-gencode=arch=compute_100a,code=sm_100a"
 LMAX_UNROLLED = int(os.environ.get("OEQB_LMAX_UNROLLED", "3"))
 CU_SOURCES = ["capi.cu", "kern_f32_batch.cu", "kern_f64_batch.cu", "kern_f32_det.cu",
               "kern_f64_det.cu", "kern_sc.cu",
-              "kern_uvw_tc.cu", "kern_uvw_sw.cu"]
+              "kern_uvw_tc.cu", "kern_uvw_sw.cu", "kern_edge_pipe.cu"]
 
 
 def _nvcc() -> str:

@@ -13,6 +13,7 @@
 
 #include <algorithm>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <set>
@@ -47,6 +48,7 @@ const void* uvw_tc_kernel_ptr(int kind);
 template <class T>
 const void* uvw_sw_kernel_ptr(int kind);
 int set_error(int code, const std::string& msg);
+const void* edge1_pipe_kernel(int kind);  // kern_edge_pipe.cu: 0 / 1 = atomic forward / backward
 }  // namespace oeqb
 
 using namespace oeqb;
@@ -1384,6 +1386,58 @@ int launch_edge1(oeqb_plan& p, int kind, const Args<T>& a, T* ws, cudaStream_t s
 }
 
 // Workspace of the single-path deterministic backward: one record per edge.
+// Pipelined single-path kernels (tp_kernels_edge_pipe.cuh): float32, one weight per edge,
+// 16-byte aligned streams.  OEQB_EDGE_PIPE=0 selects the unpipelined kernels instead.
+bool edge1_pipe_enabled() {
+  static const bool on = [] {
+    const char* e = std::getenv("OEQB_EDGE_PIPE");
+    return !(e && std::string(e) == "0");
+  }();
+  return on;
+}
+
+template <class T>
+bool edge1_pipe_ok(const oeqb_plan& p, const Args<T>& a) {
+  if constexpr (!std::is_same_v<T, float>) {
+    return false;
+  } else {
+    return edge1_pipe_enabled() && p.edge1_ok && !p.shared_w && p.wnumel == 1 &&
+           aligned16(a.rows) && aligned16(a.cols) && aligned16(a.W) && aligned16(a.Y);
+  }
+}
+
+template <class T>
+int launch_edge1_pipe(oeqb_plan& p, int kind, const Args<T>& a, cudaStream_t stream) {
+  if (a.nitems <= 0) return 0;
+  const void* kernel = edge1_pipe_kernel(kind);
+  if (!kernel) return fail(OEQB_ERR_UNSUPPORTED, "no pipelined kernel of this kind");
+  const int d2 = 2 * ((p.edge1.code >> 4) & 15) + 1;
+  const size_t stage = 2 * 32 * sizeof(long long) + 32 * sizeof(float) * (1 + d2);
+  const size_t per_warp = 3 * stage + (kind == 1 ? 32 * sizeof(float) * (d2 + 1) : 0);
+  const size_t smem = size_t(kEdgeWarps) * per_warp;
+  int per_sm;
+  {
+    std::lock_guard<std::mutex> g(p.mu);
+    auto it = p.occ.find(kernel);
+    if (it == p.occ.end()) {
+      if (int rc = allow_max_smem(p.device, kernel)) return rc;
+      int n = 0;
+      OEQB_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kernel, kEdgeWarps * 32, smem));
+      if (n <= 0) return fail(OEQB_ERR_UNSUPPORTED, "pipelined edge kernel does not fit");
+      it = p.occ.emplace(kernel, n).first;
+    }
+    per_sm = it->second;
+  }
+  const long long cap = (long long)p.sm_count * per_sm;
+  const long long warps = (a.nitems + 31) / 32;
+  const long long blocks = std::max<long long>(1, std::min<long long>((warps + kEdgeWarps - 1) / kEdgeWarps, cap));
+  Edge1 e = p.edge1;
+  void* params[] = {const_cast<Args<T>*>(&a), &e};
+  OEQB_CUDA(cudaLaunchKernel(kernel, dim3(static_cast<unsigned>(blocks)), dim3(kEdgeWarps * 32),
+                             params, smem, stream));
+  return 0;
+}
+
 size_t edge1_det_ws_bytes(const oeqb_plan& p, int64_t nnz) {
   if (!(p.edge1_ok && p.det && !p.kahan) || nnz <= 0) return 0;
   return size_t(nnz) * kE1Rec * p.elem();
@@ -1537,6 +1591,7 @@ int conv_fwd_t(oeqb_plan* p, bool db, const void* X, const void* Y, const void* 
       return launch_edge1<T>(*p, 4, a, nullptr, s);
     return launch(*p, det_kernel_ptr<T>(0, p->uvw, db, p->kahan), a, true, true, s);
   }
+  if (!db && edge1_pipe_ok(*p, a)) return launch_edge1_pipe<T>(*p, 0, a, s);
   if (!db && p->edge1_ok && aligned16(Y)) return launch_edge1<T>(*p, 2, a, nullptr, s);
   if (!db && p->edge_ok) return launch_edge(*p, 0, a, s);
   return launch(*p, batch_kernel_ptr<T>(0, p->uvw, db, kConvAtomic), a, true, false, s);
@@ -1575,6 +1630,8 @@ int conv_bwd_t(oeqb_plan* p, bool db, const void* X, const void* Y, const void* 
     OEQB_CUDA(cudaMemsetAsync(gY, 0, sizeof(T) * size_t(nnz) * p->L2dim, s));
     return launch(*p, det_kernel_ptr<T>(1, p->uvw, db, p->kahan), a, false, true, s);
   }
+  if (!db && edge1_pipe_ok(*p, a) && aligned16(gY) && aligned16(gW))
+    return launch_edge1_pipe<T>(*p, 1, a, s);
   if (!db && p->edge1_ok && aligned16(Y) && aligned16(gY))
     return launch_edge1<T>(*p, 3, a, nullptr, s);
   if (!db && p->edge_ok) return launch_edge(*p, 1, a, s);

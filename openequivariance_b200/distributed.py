@@ -58,6 +58,11 @@ class ReceiverPartition:
     tperm_bnd: torch.Tensor
     send_splits: List[torch.Tensor] = field(default_factory=list)  # send_idx per destination
     n_boundary_local: int = 0      # boundary-block edges whose sender is owned (0..3)
+    # Fixed-order sums of the dX rows that come back from the other ranks: the positions of
+    # send_idx sorted by (node, rank), the distinct nodes, and each node's count.
+    back_order: Optional[torch.Tensor] = None
+    back_nodes: Optional[torch.Tensor] = None
+    back_counts: Optional[torch.Tensor] = None
 
     @property
     def n_own(self) -> int:
@@ -135,11 +140,16 @@ class ReceiverPartition:
         def tperm(rr, cc):
             return torch.argsort(cc * max(n_loc, 1) + rr, stable=True)
 
+        send_idx = torch.cat(send_splits)
+        # send_idx is grouped by destination rank, so a stable sort by node keeps rank order.
+        back_order = torch.argsort(send_idx, stable=True)
+        back_nodes, back_counts = torch.unique_consecutive(send_idx[back_order],
+                                                           return_counts=True)
         return ReceiverPartition(
-            rank, world, num_nodes, lo, hi, halo, recv_counts, torch.cat(send_splits),
+            rank, world, num_nodes, lo, hi, halo, recv_counts, send_idx,
             send_counts, torch.cat([idx[inner], idx[~inner]]), int(inner.sum()),
             rows_int, cols_int, rows_bnd, cols_bnd, tperm(rows_int, cols_int),
-            tperm(rows_bnd, cols_bnd), send_splits, extra)
+            tperm(rows_bnd, cols_bnd), send_splits, extra, back_order, back_nodes, back_counts)
 
 
 def _local_conv_ops(conv):
@@ -233,11 +243,14 @@ class _HaloConvFn(torch.autograd.Function):
             gX.add_(gX_b[:n_own])  # the boundary block's edges with an owned sender
         if work is not None:
             work.wait()
-            off = 0
-            for r, cnt in enumerate(part.send_counts):
-                if cnt:
-                    gX.index_add_(0, part.send_splits[r], back[off:off + cnt])
-                off += cnt
+            if back.shape[0]:
+                if pc.deterministic:
+                    # Each node's contributions summed in rank order, then one add per node.
+                    sums = torch.segment_reduce(back[part.back_order], "sum",
+                                                lengths=part.back_counts)
+                    gX.index_add_(0, part.back_nodes, sums)
+                else:
+                    gX.index_add_(0, part.send_idx, back)
         if shared:
             gW = gW_i + gW_b if (part.n_boundary or part.world > 1) else gW_i
             if part.world > 1:
@@ -253,12 +266,17 @@ class PartitionedConv(torch.nn.Module):
     order (``Y[part.edge_index]``: interior edges first) and returns this rank's rows of Z.
     ``conv`` is a ``TensorProductConv`` (atomic or deterministic).  ``local_ops`` replaces its
     kernels with another (forward, backward-into) pair of the same signature (e.g. a CPU
-    implementation for host-side tests); ``shared_weights`` must then be given.
+    implementation for host-side tests); ``shared_weights`` and ``deterministic`` must then
+    be given.
+
+    Nothing in a pass synchronises with the host, so a whole training or MD step that uses the
+    module (forward, autograd backward, the NCCL exchanges) can be captured in one CUDA graph
+    and replayed, which removes the per-step launch cost of its ~20 small operations.
     """
 
     def __init__(self, conv, part: ReceiverPartition, group=None,
                  local_ops: Optional[tuple[Callable, Callable]] = None,
-                 shared_weights: Optional[bool] = None):
+                 shared_weights: Optional[bool] = None, deterministic: Optional[bool] = None):
         super().__init__()
         self.conv = conv
         self.part = part
@@ -266,6 +284,8 @@ class PartitionedConv(torch.nn.Module):
         self.fwd, self.bwd = local_ops if local_ops is not None else _local_conv_ops(conv)
         self.shared_weights = (bool(conv.config.shared_weights) if shared_weights is None
                                else shared_weights)
+        self.deterministic = (bool(conv.deterministic) if deterministic is None
+                              else deterministic)
 
     def forward(self, X_own, Y_local, W_local):
         return _HaloConvFn.apply(X_own, Y_local, W_local, self)

@@ -58,7 +58,7 @@ def _graph(n=300, box=10.0, cutoff=2.5, spatial=True):
     return rows, cols
 
 
-def _worker(rank, world, port, results, spatial):
+def _worker(rank, world, port, results, spatial, det):
     import tp_oracle as O
 
     from openequivariance_b200.distributed import PartitionedConv, ReceiverPartition
@@ -76,7 +76,8 @@ def _worker(rank, world, port, results, spatial):
         W = rng.normal(size=(E, p.weight_numel))
         G = rng.normal(size=(n, 8))
         part = ReceiverPartition.build(rows, cols, n, world, rank)
-        conv = PartitionedConv(None, part, local_ops=_oracle_ops(p), shared_weights=False)
+        conv = PartitionedConv(None, part, local_ops=_oracle_ops(p), shared_weights=False,
+                               deterministic=det)
         lo, hi = part.node_lo, part.node_hi
         ei = part.edge_index.numpy()
         x = torch.tensor(X[lo:hi], requires_grad=True)
@@ -110,12 +111,13 @@ def _worker(rank, world, port, results, spatial):
         dist.destroy_process_group()
 
 
+@pytest.mark.parametrize("det", [False, True], ids=["atomic", "deterministic"])
 @pytest.mark.parametrize("world", [2, 3])
-def test_partitioned_conv_gloo(world):
-    port = 29600 + world
+def test_partitioned_conv_gloo(world, det):
+    port = 29600 + 2 * world + det
     ctx = mp.get_context("spawn")
     results = ctx.Manager().dict()
-    mp.start_processes(_worker, args=(world, port, results, True), nprocs=world,
+    mp.start_processes(_worker, args=(world, port, results, True, det), nprocs=world,
                        start_method="spawn")
     assert sorted(results.keys()) == list(range(world))
 
@@ -154,7 +156,8 @@ def _stalled_worker(rank, world, port, results):
                 time.sleep(0.1)
             results[1] = "idle"
             return
-        conv = PartitionedConv(None, part, local_ops=_oracle_ops(p), shared_weights=False)
+        conv = PartitionedConv(None, part, local_ops=_oracle_ops(p), shared_weights=False,
+                               deterministic=False)
         rng = np.random.default_rng(0)
         x = torch.tensor(rng.normal(size=(part.n_own, 8)))
         y = torch.tensor(rng.normal(size=(part.n_edges, 4)))

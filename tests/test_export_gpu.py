@@ -8,6 +8,7 @@ uvu, and the same three module kinds: batch, deterministic conv, atomic conv),
 built with g++ against libtorch and ``libtorch_oeqb200.so``.
 """
 
+import functools
 import os
 import subprocess
 import sys
@@ -92,6 +93,31 @@ def test_torch_export(tp_and_inputs):
     want = tp(*inputs)
     ep = torch.export.export(tp, args=inputs, strict=False)
     torch.testing.assert_close(ep.module()(*inputs), want, atol=1e-5, rtol=0)
+
+
+@functools.lru_cache(maxsize=None)
+def _cxx_has_openmp():
+    import shutil
+
+    cxx = shutil.which("g++") or "g++"
+    with tempfile.TemporaryDirectory() as d:
+        src = os.path.join(d, "t.cpp")
+        with open(src, "w") as f:
+            f.write("int main() { return 0; }\n")
+        r = subprocess.run([cxx, "-fopenmp", src, "-o", os.path.join(d, "t")],
+                           capture_output=True)
+    return r.returncode == 0
+
+
+@pytest.fixture(autouse=True)
+def _inductor_without_openmp(monkeypatch):
+    """AOTInductor always asks the host compiler for OpenMP on Linux.  The package's CUDA
+    wrapper does not use it, so where the compiler cannot provide it (no libgomp), the flags
+    are left out rather than failing the build."""
+    if not _cxx_has_openmp():
+        import torch._inductor.cpp_builder as cb
+
+        monkeypatch.setattr(cb, "_get_openmp_args", lambda cpp_compiler: ([], [], [], [], [], []))
 
 
 def test_aoti_python(tp_and_inputs):
