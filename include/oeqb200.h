@@ -63,11 +63,13 @@ const char* oeqb_last_error(void);
 int oeqb_plan_create(const void* descriptor, size_t nbytes, int device, oeqb_plan** out);
 int oeqb_plan_destroy(oeqb_plan* plan);
 
-/* Bytes of workspace oeqb_conv_backward needs for `nnz` edges (replaces the reference's
- * workspace sizing, core/LoopUnrollConv.py:138-170).  Nonzero only for deterministic plans of
- * single-path multiplicity-1 problems, whose fast backward keeps one 8-value record per edge;
- * with a smaller workspace those plans fall back to the generic deterministic kernels.  The
- * forward and the double backward need none. */
+/* Bytes of workspace oeqb_conv_forward / oeqb_conv_backward use for `nnz` edges and
+ * `node_count` nodes (replaces the reference's workspace sizing,
+ * core/LoopUnrollConv.py:138-170).  Nonzero only for single-path multiplicity-1 problems
+ * (BASELINE C3's class): deterministic plans keep one 8-value record per edge in the
+ * backward; float32 atomic plans with one weight per edge keep X, dZ and the dX accumulator in
+ * 32-byte rows (3 x 32 x node_count bytes + 256).  With a smaller (or not 16-byte aligned)
+ * workspace those plans run slower kernels that need none.  The double backward needs none. */
 size_t oeqb_conv_workspace_bytes(const oeqb_plan* plan, int64_t nnz, int64_t node_count);
 
 /* Synchronises `stream` and reports (then clears) the plan's device error flag:

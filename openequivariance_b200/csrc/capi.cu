@@ -48,7 +48,9 @@ const void* uvw_tc_kernel_ptr(int kind);
 template <class T>
 const void* uvw_sw_kernel_ptr(int kind);
 int set_error(int code, const std::string& msg);
-const void* edge1_pipe_kernel(int kind);  // kern_edge_pipe.cu: 0 / 1 = atomic forward / backward
+// kern_edge_pipe.cu: 0 / 1 = pipelined atomic forward / backward of triple `code`, 2 = pad
+// rows, 3 = unpad rows
+const void* edge1_pipe_kernel(int kind, int code);
 }  // namespace oeqb
 
 using namespace oeqb;
@@ -1396,21 +1398,75 @@ bool edge1_pipe_enabled() {
   return on;
 }
 
+// The plan class of the pipelined kernels (pointer alignment is checked per call).
+bool edge1_pipe_class(const oeqb_plan& p) {
+  const int d1 = 2 * ((p.edge1.code >> 8) & 15) + 1, d3 = 2 * (p.edge1.code & 15) + 1;
+  return edge1_pipe_enabled() && p.dtype == 1 && !p.det && p.edge1_ok && !p.shared_w &&
+         p.wnumel == 1 && d1 <= 8 && d3 <= 8 && edge1_pipe_kernel(0, p.edge1.code) != nullptr;
+}
+
+// Workspace of the pipelined kernels: X, dZ and the dX accumulator in 32-byte rows.
+constexpr size_t kPadRowBytes = 32;
+size_t edge1_pipe_ws_bytes(int64_t nodes) { return 3 * kPadRowBytes * size_t(nodes) + 256; }
+
 template <class T>
-bool edge1_pipe_ok(const oeqb_plan& p, const Args<T>& a) {
+bool edge1_pipe_ok(const oeqb_plan& p, const Args<T>& a, const void* ws, size_t ws_bytes) {
   if constexpr (!std::is_same_v<T, float>) {
     return false;
   } else {
-    return edge1_pipe_enabled() && p.edge1_ok && !p.shared_w && p.wnumel == 1 &&
-           aligned16(a.rows) && aligned16(a.cols) && aligned16(a.W) && aligned16(a.Y);
+    return edge1_pipe_class(p) && ws && aligned16(ws) &&
+           ws_bytes >= edge1_pipe_ws_bytes(a.nnodes) && aligned16(a.rows) &&
+           aligned16(a.cols) && aligned16(a.W) && aligned16(a.Y);
   }
 }
 
+// conv_pad_rows over `nodes` rows: a (width da) -> pa, optionally b (width db) -> pb, and
+// optionally zero[] cleared.
+int launch_pad(const oeqb_plan& p, const float* a, int da, float* pa, const float* b, int db,
+               float* pb, float* zero, long long nodes, cudaStream_t stream) {
+  if (nodes <= 0) return 0;
+  const long long work = nodes * 8;
+  const unsigned blocks = static_cast<unsigned>(
+      std::min<long long>((work + 255) / 256, static_cast<long long>(p.sm_count) * 8));
+  void* params[] = {&a, &da, &pa, &b, &db, &pb, &zero, &nodes};
+  OEQB_CUDA(cudaLaunchKernel(edge1_pipe_kernel(2, 0), dim3(blocks), dim3(256), params, 0, stream));
+  return 0;
+}
+
+int launch_unpad(const oeqb_plan& p, const float* src, float* dst, int d, long long nodes,
+                 cudaStream_t stream) {
+  if (nodes <= 0) return 0;
+  const long long work = nodes * d;
+  const unsigned blocks = static_cast<unsigned>(
+      std::min<long long>((work + 255) / 256, static_cast<long long>(p.sm_count) * 8));
+  void* params[] = {&src, &dst, &d, &nodes};
+  OEQB_CUDA(cudaLaunchKernel(edge1_pipe_kernel(3, 0), dim3(blocks), dim3(256), params, 0, stream));
+  return 0;
+}
+
+// kind 0: forward (pads X into the workspace first); kind 1: backward (pads X and dZ, clears
+// the dX accumulator, runs, then writes dX).
 template <class T>
-int launch_edge1_pipe(oeqb_plan& p, int kind, const Args<T>& a, cudaStream_t stream) {
-  if (a.nitems <= 0) return 0;
-  const void* kernel = edge1_pipe_kernel(kind);
-  if (!kernel) return fail(OEQB_ERR_UNSUPPORTED, "no pipelined kernel of this kind");
+int launch_edge1_pipe(oeqb_plan& p, int kind, const Args<T>& a, void* ws, cudaStream_t stream) {
+  if (a.nitems <= 0) {
+    if (kind == 1) OEQB_CUDA(cudaMemsetAsync(a.out0, 0, sizeof(T) * size_t(a.nnodes) * p.L1dim, stream));
+    return 0;
+  }
+  const void* kernel = edge1_pipe_kernel(kind, p.edge1.code);
+  if (!kernel) return fail(OEQB_ERR_UNSUPPORTED, "no pipelined kernel for this degree triple");
+  const int d1 = 2 * ((p.edge1.code >> 8) & 15) + 1, d3 = 2 * (p.edge1.code & 15) + 1;
+  float* xp = static_cast<float*>(ws);
+  float* gp = xp + 8 * size_t(a.nnodes);
+  float* dxp = gp + 8 * size_t(a.nnodes);
+  if (kind == 0) {
+    if (int rc = launch_pad(p, reinterpret_cast<const float*>(a.X), d1, xp, nullptr, 0, nullptr,
+                            nullptr, a.nnodes, stream))
+      return rc;
+  } else {
+    if (int rc = launch_pad(p, reinterpret_cast<const float*>(a.X), d1, xp,
+                            reinterpret_cast<const float*>(a.Gz), d3, gp, dxp, a.nnodes, stream))
+      return rc;
+  }
   const int d2 = 2 * ((p.edge1.code >> 4) & 15) + 1;
   const size_t stage = 2 * 32 * sizeof(long long) + 32 * sizeof(float) * (1 + d2);
   const size_t per_warp = 3 * stage + (kind == 1 ? 32 * sizeof(float) * (d2 + 1) : 0);
@@ -1432,9 +1488,14 @@ int launch_edge1_pipe(oeqb_plan& p, int kind, const Args<T>& a, cudaStream_t str
   const long long warps = (a.nitems + 31) / 32;
   const long long blocks = std::max<long long>(1, std::min<long long>((warps + kEdgeWarps - 1) / kEdgeWarps, cap));
   Edge1 e = p.edge1;
-  void* params[] = {const_cast<Args<T>*>(&a), &e};
+  const float* cxp = xp;
+  const float* cgp = gp;
+  void* params_f[] = {const_cast<Args<T>*>(&a), &e, &cxp};
+  void* params_b[] = {const_cast<Args<T>*>(&a), &e, &cxp, &cgp, &dxp};
   OEQB_CUDA(cudaLaunchKernel(kernel, dim3(static_cast<unsigned>(blocks)), dim3(kEdgeWarps * 32),
-                             params, smem, stream));
+                             kind == 0 ? params_f : params_b, smem, stream));
+  if (kind == 1)
+    return launch_unpad(p, dxp, reinterpret_cast<float*>(a.out0), d1, a.nnodes, stream);
   return 0;
 }
 
@@ -1572,7 +1633,7 @@ int tp_double_backward_t(oeqb_plan* p, int64_t B, const void* X, const void* Y, 
 template <class T>
 int conv_fwd_t(oeqb_plan* p, bool db, const void* X, const void* Y, const void* W, const void* ddX,
                const void* ddY, const void* ddW, void* Z, const int64_t* rows, const int64_t* cols,
-               int64_t nnz, int64_t nodes, cudaStream_t s) {
+               int64_t nnz, int64_t nodes, void* ws, size_t ws_bytes, cudaStream_t s) {
   OEQB_CUDA(cudaMemsetAsync(Z, 0, sizeof(T) * size_t(nodes) * p->L3dim, s));
   Args<T> a = base_args<T>(*p, true);
   a.nitems = nnz;
@@ -1591,7 +1652,7 @@ int conv_fwd_t(oeqb_plan* p, bool db, const void* X, const void* Y, const void* 
       return launch_edge1<T>(*p, 4, a, nullptr, s);
     return launch(*p, det_kernel_ptr<T>(0, p->uvw, db, p->kahan), a, true, true, s);
   }
-  if (!db && edge1_pipe_ok(*p, a)) return launch_edge1_pipe<T>(*p, 0, a, s);
+  if (!db && edge1_pipe_ok(*p, a, ws, ws_bytes)) return launch_edge1_pipe<T>(*p, 0, a, ws, s);
   if (!db && p->edge1_ok && aligned16(Y)) return launch_edge1<T>(*p, 2, a, nullptr, s);
   if (!db && p->edge_ok) return launch_edge(*p, 0, a, s);
   return launch(*p, batch_kernel_ptr<T>(0, p->uvw, db, kConvAtomic), a, true, false, s);
@@ -1602,8 +1663,6 @@ int conv_bwd_t(oeqb_plan* p, bool db, const void* X, const void* Y, const void* 
                const void* ddX, const void* ddY, const void* ddW, void* gX, void* gY, void* gW,
                const int64_t* rows, const int64_t* cols, const int64_t* perm, int64_t nnz,
                int64_t nodes, void* ws, size_t ws_bytes, cudaStream_t s) {
-  OEQB_CUDA(cudaMemsetAsync(gX, 0, sizeof(T) * size_t(nodes) * p->L1dim, s));
-  if (p->shared_w) OEQB_CUDA(cudaMemsetAsync(gW, 0, sizeof(T) * p->wnumel, s));
   Args<T> a = base_args<T>(*p, false);
   a.nitems = nnz;
   a.nnodes = nodes;
@@ -1620,6 +1679,11 @@ int conv_bwd_t(oeqb_plan* p, bool db, const void* X, const void* Y, const void* 
   a.rows = reinterpret_cast<const long long*>(rows);
   a.cols = reinterpret_cast<const long long*>(cols);
   a.perm = reinterpret_cast<const long long*>(perm);
+  // The pipelined backward writes every dX row itself (through its padded accumulator).
+  if (!db && edge1_pipe_ok(*p, a, ws, ws_bytes) && aligned16(gY) && aligned16(gW))
+    return launch_edge1_pipe<T>(*p, 1, a, ws, s);
+  OEQB_CUDA(cudaMemsetAsync(gX, 0, sizeof(T) * size_t(nodes) * p->L1dim, s));
+  if (p->shared_w) OEQB_CUDA(cudaMemsetAsync(gW, 0, sizeof(T) * p->wnumel, s));
   if (p->det) {
     if (!perm) return fail(OEQB_ERR_INVALID, "deterministic convolution needs transpose_perm");
     const size_t need = edge1_det_ws_bytes(*p, nnz);
@@ -1630,8 +1694,6 @@ int conv_bwd_t(oeqb_plan* p, bool db, const void* X, const void* Y, const void* 
     OEQB_CUDA(cudaMemsetAsync(gY, 0, sizeof(T) * size_t(nnz) * p->L2dim, s));
     return launch(*p, det_kernel_ptr<T>(1, p->uvw, db, p->kahan), a, false, true, s);
   }
-  if (!db && edge1_pipe_ok(*p, a) && aligned16(gY) && aligned16(gW))
-    return launch_edge1_pipe<T>(*p, 1, a, s);
   if (!db && p->edge1_ok && aligned16(Y) && aligned16(gY))
     return launch_edge1<T>(*p, 3, a, nullptr, s);
   if (!db && p->edge_ok) return launch_edge(*p, 1, a, s);
@@ -1769,8 +1831,9 @@ int oeqb_plan_destroy(oeqb_plan* p) {
 }
 
 size_t oeqb_conv_workspace_bytes(const oeqb_plan* p, int64_t nnz, int64_t node_count) {
-  (void)node_count;
-  return p ? edge1_det_ws_bytes(*p, nnz) : 0;
+  if (!p) return 0;
+  if (edge1_pipe_class(*p)) return edge1_pipe_ws_bytes(node_count);
+  return edge1_det_ws_bytes(*p, nnz);
 }
 
 int oeqb_plan_check_status(oeqb_plan* p, int* status, void* stream) {
@@ -1856,16 +1919,16 @@ int oeqb_tp_double_backward(oeqb_plan* p, int64_t batch, const void* L1_in, cons
 int oeqb_conv_forward(oeqb_plan* p, const void* L1_in, const void* L2_in, const void* W,
                       void* L3_out, const int64_t* rows, const int64_t* cols, int64_t nnz,
                       int64_t node_count, void* workspace, size_t workspace_bytes, void* stream) {
-  (void)workspace;
-  (void)workspace_bytes;
   if (nnz < 0 || node_count < 0) return fail(OEQB_ERR_INVALID, "negative size");
   if (int rc = check_plan(p)) return rc;
   DeviceGuard g(p->device);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   return p->dtype == 1 ? conv_fwd_t<float>(p, false, L1_in, L2_in, W, nullptr, nullptr, nullptr,
-                                           L3_out, rows, cols, nnz, node_count, s)
+                                           L3_out, rows, cols, nnz, node_count, workspace,
+                                           workspace_bytes, s)
                        : conv_fwd_t<double>(p, false, L1_in, L2_in, W, nullptr, nullptr, nullptr,
-                                            L3_out, rows, cols, nnz, node_count, s);
+                                            L3_out, rows, cols, nnz, node_count, workspace,
+                                            workspace_bytes, s);
 }
 
 int oeqb_conv_backward(oeqb_plan* p, const void* L1_in, void* L1_grad, const void* L2_in,
@@ -1901,14 +1964,14 @@ int oeqb_conv_double_backward(oeqb_plan* p, const void* L1_in, const void* L2_in
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (p->dtype == 1) {
     if (int rc = conv_fwd_t<float>(p, true, L1_in, L2_in, W, L1_dgrad, L2_dgrad, W_dgrad, L3_dgrad,
-                                   rows, cols, nnz, node_count, s))
+                                   rows, cols, nnz, node_count, nullptr, 0, s))
       return rc;
     return conv_bwd_t<float>(p, true, L1_in, L2_in, W, L3_grad, L1_dgrad, L2_dgrad, W_dgrad,
                              L1_grad, L2_grad, W_grad, rows, cols, transpose_perm, nnz, node_count,
                              nullptr, 0, s);
   }
   if (int rc = conv_fwd_t<double>(p, true, L1_in, L2_in, W, L1_dgrad, L2_dgrad, W_dgrad, L3_dgrad,
-                                  rows, cols, nnz, node_count, s))
+                                  rows, cols, nnz, node_count, nullptr, 0, s))
     return rc;
   return conv_bwd_t<double>(p, true, L1_in, L2_in, W, L3_grad, L1_dgrad, L2_dgrad, W_dgrad,
                             L1_grad, L2_grad, W_grad, rows, cols, transpose_perm, nnz, node_count,

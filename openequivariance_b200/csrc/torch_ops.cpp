@@ -313,9 +313,15 @@ Tensor jit_conv_forward(Tensor json_bytes, int64_t hash, Tensor L1_in, Tensor L2
   void* st = stream_of(L1_in);
   const bool chk = checks_active(st);
   if (chk) validate_graph(r, cl, nullptr, c.nnz, c.nodes, k.deterministic, st);
+  // Some kernels keep node rows in a padded layout in the workspace; a module's buffer that is
+  // too small is replaced for this call (torch's caching allocator).
+  Tensor ws = workspace;
+  const size_t need = oeqb_conv_workspace_bytes(k.plan, c.nnz, c.nodes);
+  if (need > static_cast<size_t>(workspace.numel()))
+    ws = at::empty({static_cast<int64_t>(need)}, workspace.options());
   check_rc(oeqb_conv_forward(k.plan, x.data_ptr(), y.data_ptr(), w.data_ptr(), L3_out.data_ptr(),
                              r.data_ptr<int64_t>(), cl.data_ptr<int64_t>(), c.nnz, c.nodes,
-                             workspace.data_ptr(), static_cast<size_t>(workspace.numel()), st));
+                             ws.data_ptr(), static_cast<size_t>(ws.numel()), st));
   if (chk) check_status(k, st);
   return L3_out;
 }
@@ -368,8 +374,9 @@ void conv_backward_impl(const PlanInfo& k, const ConvIdx& c, Tensor L1_in, Tenso
   Tensor x = L1_in.contiguous(), y = L2_in.contiguous(), w = W.contiguous(),
          gz = L3_grad.contiguous(), r = rows.contiguous(), cl = cols.contiguous();
   Tensor tp = k.deterministic ? transpose_perm.contiguous() : Tensor();
-  // The single-path deterministic backward keeps one record per edge in the workspace; a
-  // module's buffer that is too small is replaced for this call (torch's caching allocator).
+  // The single-path kernels keep one record per edge (deterministic) or padded node rows
+  // (atomic) in the workspace; a module's buffer that is too small is replaced for this call
+  // (torch's caching allocator).
   Tensor ws = workspace;
   const size_t need = oeqb_conv_workspace_bytes(k.plan, c.nnz, c.nodes);
   if (need > static_cast<size_t>(workspace.numel()))

@@ -16,8 +16,13 @@
 // The kernels this replaces waited on the index loads, then on the dependent gathers, once
 // per 32 edges, with nothing else in flight (long-scoreboard stalls of ~11 per issue).
 //
-// Requirements (checked by the host): float32 rows/cols/W/Y/dY/dW pointers 16-byte aligned;
-// per-edge weights with weight_numel == 1.  Bad indices are dropped and raise status 1.
+// Node arrays (X, dZ, and the dX accumulator) are read and written in a padded layout of
+// 32-byte rows (workspace, filled by conv_pad_rows / emptied by conv_unpad_rows), so every
+// gather and every reduction touches one aligned sector.
+//
+// Requirements (checked by the host): float32; rows/cols/W/Y/dY/dW pointers 16-byte aligned;
+// per-edge weights with weight_numel == 1; D1, D3 <= 8.  Bad indices are dropped and raise
+// status 1.
 #pragma once
 
 #include "tp_kernels_edge.cuh"
@@ -89,64 +94,82 @@ __device__ __forceinline__ void pipe_stage_in(PipeStage<D2>& st, const long long
   for (int i = lane; i < r * D2; i += 32) st.y[i] = Y[base * D2 + i];
 }
 
-// Register image of a gathered D-value row: the 16-byte aligned window that holds it
-// (NW float4 loads) and the row's offset in it.  Rows whose window would pass the end of the
-// tensor are loaded element by element at offset 0.
+// Node rows in the padded layout of these kernels: row n of a [nodes, D] tensor (D <= 8) at
+// n * 8 floats, 32-byte aligned, so a gather is one 16-byte load and D - 4 more (one sector),
+// with no alignment arithmetic on the lane.
+constexpr int kPadRow = 8;
+
 template <int D>
-struct GatherWin {
-  static constexpr int NW = (D + 6) / 4;
-  float w[4 * NW];
-  int o;
-
-  __device__ __forceinline__ void load(const float* src, long long node, long long nodes, bool valid) {
-    o = 0;
-    if (!valid) {
+__device__ __forceinline__ void load_row8(float (&v)[D], const float* src, long long node) {
+  static_assert(D <= kPadRow, "row wider than the padded layout");
+  const float* r = src + node * kPadRow;
+  if constexpr (D >= 4) {
+    const float4 t = __ldg(reinterpret_cast<const float4*>(r));
+    v[0] = t.x;
+    v[1] = t.y;
+    v[2] = t.z;
+    v[3] = t.w;
 #pragma unroll
-      for (int i = 0; i < 4 * NW; ++i) w[i] = 0.f;
-      return;
-    }
-    const long long f = node * D;
-    const int off = static_cast<int>(f & 3);
-    const long long b4 = f - off;
-    if (b4 + 4 * NW <= nodes * D) {
-      o = off;
+    for (int i = 4; i < D; ++i) v[i] = __ldg(r + i);
+  } else {
 #pragma unroll
-      for (int q = 0; q < NW; ++q) {
-        const float4 t = __ldg(reinterpret_cast<const float4*>(src + b4) + q);
-        w[4 * q] = t.x;
-        w[4 * q + 1] = t.y;
-        w[4 * q + 2] = t.z;
-        w[4 * q + 3] = t.w;
-      }
-    } else {
-#pragma unroll
-      for (int i = 0; i < D; ++i) w[i] = src[f + i];
-#pragma unroll
-      for (int i = D; i < 4 * NW; ++i) w[i] = 0.f;
-    }
+    for (int i = 0; i < D; ++i) v[i] = __ldg(r + i);
   }
+}
 
-  __device__ __forceinline__ void get(float (&v)[D]) const {
-    switch (o) {
-      case 0:
+template <int D>
+__device__ __forceinline__ void zero_row(float (&v)[D]) {
 #pragma unroll
-        for (int i = 0; i < D; ++i) v[i] = w[i];
-        break;
-      case 1:
-#pragma unroll
-        for (int i = 0; i < D; ++i) v[i] = w[i + 1];
-        break;
-      case 2:
-#pragma unroll
-        for (int i = 0; i < D; ++i) v[i] = w[i + 2];
-        break;
-      default:
-#pragma unroll
-        for (int i = 0; i < D; ++i) v[i] = w[i + 3];
-        break;
-    }
+  for (int i = 0; i < D; ++i) v[i] = 0.f;
+}
+
+// Copies [nodes, D] rows into the padded layout (zero tails).  The backward pads X and dZ and
+// clears the padded dX accumulator in one launch.
+__global__ void conv_pad_rows(const float* __restrict__ a, int da, float* __restrict__ pa,
+                              const float* __restrict__ b, int db, float* __restrict__ pb,
+                              float* __restrict__ zero, long long nodes) {
+  const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
+  for (long long t = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+       t < nodes * kPadRow; t += stride) {
+    const long long n = t / kPadRow;
+    const int i = static_cast<int>(t - n * kPadRow);
+    pa[t] = i < da ? a[n * da + i] : 0.f;
+    if (pb) pb[t] = i < db ? b[n * db + i] : 0.f;
+    if (zero) zero[t] = 0.f;
   }
-};
+}
+
+// dX [nodes, D] from the padded accumulator.
+__global__ void conv_unpad_rows(const float* __restrict__ src, float* __restrict__ dst, int d,
+                                long long nodes) {
+  const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
+  for (long long t = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+       t < nodes * d; t += stride) {
+    const long long n = t / d;
+    dst[t] = src[n * kPadRow + (t - n * d)];
+  }
+}
+
+// Adds D values into a padded (32-byte aligned) row: one 16-byte vector reduction and the
+// rest in the same sector.
+template <int D>
+__device__ __forceinline__ void red_row8(float* dst, const float (&v)[D]) {
+  if constexpr (D >= 4) {
+    asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};\n" ::"l"(dst), "f"(v[0]),
+                 "f"(v[1]), "f"(v[2]), "f"(v[3])
+                 : "memory");
+    if constexpr (D >= 6) {
+      asm volatile("red.global.add.v2.f32 [%0], {%1, %2};\n" ::"l"(dst + 4), "f"(v[4]), "f"(v[5])
+                   : "memory");
+      if constexpr (D == 7) atomic_add(dst + 6, v[6]);
+    } else if constexpr (D == 5) {
+      atomic_add(dst + 4, v[4]);
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < D; ++i) atomic_add(dst + i, v[i]);
+  }
+}
 
 constexpr int kPipeStages = 3;
 
@@ -166,15 +189,18 @@ __device__ __forceinline__ bool pipe_valid(long long row, long long col, long lo
   return true;
 }
 
-template <class T>
-__global__ void __launch_bounds__(kEdgeWarps * 32) conv_fwd_edge1_pipe(const Args<T> a, const Edge1 p) {
-  static_assert(sizeof(T) == 4, "float32 only");
+// Forward.  xp: X in the padded layout.
+// One instantiation per degree triple (A, B, C), each with its own register allocation; the
+// host picks the plan's (edge1_pipe_kernel).
+template <int A, int B, int C>
+__global__ void __launch_bounds__(kEdgeWarps * 32) conv_fwd_edge1_pipe(const Args<float> a, const Edge1 p,
+                                                                       const float* __restrict__ xp) {
   extern __shared__ __align__(16) unsigned char smem[];
   const int lane = threadIdx.x & 31;
   const long long nw = static_cast<long long>(gridDim.x) * kEdgeWarps;
   const long long n = a.nitems;
   const float pw = static_cast<float>(p.pw);
-  dispatch_triple(p.code, [&]<int A, int B, int C>() {
+  {
     constexpr int D1 = 2 * A + 1, D2 = 2 * B + 1, D3 = 2 * C + 1;
     auto* ring = reinterpret_cast<PipeStage<D2>*>(smem + (threadIdx.x >> 5) * pipe_warp_bytes<D2>());
     const long long step = nw * 32;
@@ -188,8 +214,8 @@ __global__ void __launch_bounds__(kEdgeWarps * 32) conv_fwd_edge1_pipe(const Arg
     cp_async_wait<1>();
     __syncwarp();
     bool vc = pipe_valid(ring[0].rows[lane], ring[0].cols[lane], a.nnodes, a.status);
-    GatherWin<D1> xc;
-    xc.load(a.X, ring[0].cols[lane], a.nnodes, vc);
+    float xc[D1];
+    if (vc) load_row8<D1>(xc, xp, ring[0].cols[lane]); else zero_row(xc);
     int s = 0;
     for (; base < n; base += step) {
       const int s1 = s == kPipeStages - 1 ? 0 : s + 1;
@@ -199,11 +225,10 @@ __global__ void __launch_bounds__(kEdgeWarps * 32) conv_fwd_edge1_pipe(const Arg
       cp_async_commit();
       cp_async_wait<1>();
       __syncwarp();
-      const bool more = base + step < n;
       bool vn = false;
-      GatherWin<D1> xn;
-      if (more) vn = pipe_valid(ring[s1].rows[lane], ring[s1].cols[lane], a.nnodes, a.status);
-      xn.load(a.X, more ? ring[s1].cols[lane] : 0, a.nnodes, vn);
+      if (base + step < n) vn = pipe_valid(ring[s1].rows[lane], ring[s1].cols[lane], a.nnodes, a.status);
+      float xn[D1];
+      if (vn) load_row8<D1>(xn, xp, ring[s1].cols[lane]); else zero_row(xn);
       // Block k.
       const PipeStage<D2>& st = ring[s];
       const long long row = vc ? st.rows[lane] : -1;
@@ -212,10 +237,9 @@ __global__ void __launch_bounds__(kEdgeWarps * 32) conv_fwd_edge1_pipe(const Arg
       for (int k = 0; k < D3; ++k) z[k] = 0.f;
       if (vc) {
         float x[D1], y[D2];
-        xc.get(x);
         const float w = st.w[lane] * pw;
 #pragma unroll
-        for (int i = 0; i < D1; ++i) x[i] *= w;
+        for (int i = 0; i < D1; ++i) x[i] = xc[i] * w;
 #pragma unroll
         for (int j = 0; j < D2; ++j) y[j] = st.y[lane * D2 + j];
         CG<A, B, C>::fwd(x, y, z);
@@ -226,31 +250,37 @@ __global__ void __launch_bounds__(kEdgeWarps * 32) conv_fwd_edge1_pipe(const Arg
       e1_seg_sum<float, D3>(z, r32, lane);
       if (head) red_vec(a.out0 + row * D3, z);
       __syncwarp();  // every lane is done with stage s before it is refilled
-      xc = xn;
+#pragma unroll
+      for (int i = 0; i < D1; ++i) xc[i] = xn[i];
       vc = vn;
       s = s1;
     }
     cp_async_wait<0>();
-  });
+  }
 }
 
 // Backward: per edge dY = w evec(g, x), dW = x . hvec(g, y), dX[col] += w hvec(g, y), with
-// g = pw dZ[row].  dY and dW leave through a per-warp staging buffer as coalesced 16-byte
-// stores; dX is one vector reduction per edge.
+// g = pw dZ[row].  xp, gp: X and dZ in the padded layout; dxp: the padded dX accumulator
+// (zeroed by the caller).  dY and dW leave through a per-warp staging buffer as coalesced
+// 16-byte stores; dX is one vector reduction into a 32-byte row per edge.  dZ rows are
+// gathered at the start of the block's iteration (edges are receiver-sorted, so a block's dZ
+// rows are one or two rows, served by L1); X rows one block ahead.
 template <int D2>
 __host__ __device__ constexpr size_t pipe_bwd_warp_bytes() {
   return pipe_warp_bytes<D2>() + sizeof(float) * 32 * (D2 + 1);
 }
 
-template <class T>
-__global__ void __launch_bounds__(kEdgeWarps * 32) conv_bwd_edge1_pipe(const Args<T> a, const Edge1 p) {
-  static_assert(sizeof(T) == 4, "float32 only");
+template <int A, int B, int C>
+__global__ void __launch_bounds__(kEdgeWarps * 32) conv_bwd_edge1_pipe(const Args<float> a, const Edge1 p,
+                                                                       const float* __restrict__ xp,
+                                                                       const float* __restrict__ gp,
+                                                                       float* __restrict__ dxp) {
   extern __shared__ __align__(16) unsigned char smem[];
   const int lane = threadIdx.x & 31;
   const long long nw = static_cast<long long>(gridDim.x) * kEdgeWarps;
   const long long n = a.nitems;
   const float pw = static_cast<float>(p.pw);
-  dispatch_triple(p.code, [&]<int A, int B, int C>() {
+  {
     constexpr int D1 = 2 * A + 1, D2 = 2 * B + 1, D3 = 2 * C + 1;
     unsigned char* wbase = smem + (threadIdx.x >> 5) * pipe_bwd_warp_bytes<D2>();
     auto* ring = reinterpret_cast<PipeStage<D2>*>(wbase);
@@ -266,10 +296,8 @@ __global__ void __launch_bounds__(kEdgeWarps * 32) conv_bwd_edge1_pipe(const Arg
     cp_async_wait<1>();
     __syncwarp();
     bool vc = pipe_valid(ring[0].rows[lane], ring[0].cols[lane], a.nnodes, a.status);
-    GatherWin<D1> xc;
-    GatherWin<D3> gc;
-    xc.load(a.X, ring[0].cols[lane], a.nnodes, vc);
-    gc.load(a.Gz, ring[0].rows[lane], a.nnodes, vc);
+    float xc[D1];
+    if (vc) load_row8<D1>(xc, xp, ring[0].cols[lane]); else zero_row(xc);
     int s = 0;
     for (; base < n; base += step) {
       const int s1 = s == kPipeStages - 1 ? 0 : s + 1;
@@ -278,15 +306,16 @@ __global__ void __launch_bounds__(kEdgeWarps * 32) conv_bwd_edge1_pipe(const Arg
       cp_async_commit();
       cp_async_wait<1>();
       __syncwarp();
-      const bool more = base + step < n;
-      bool vn = false;
-      if (more) vn = pipe_valid(ring[s1].rows[lane], ring[s1].cols[lane], a.nnodes, a.status);
-      GatherWin<D1> xn;
-      GatherWin<D3> gn;
-      xn.load(a.X, more ? ring[s1].cols[lane] : 0, a.nnodes, vn);
-      gn.load(a.Gz, more ? ring[s1].rows[lane] : 0, a.nnodes, vn);
-      // Block k.
+      // Block k's dZ rows first (receiver-sorted: one or two rows per block, L1 hits), so that
+      // their latency overlaps the next block's checks and X gathers issued below.
       const PipeStage<D2>& st = ring[s];
+      float g[D3];
+      if (vc) load_row8<D3>(g, gp, st.rows[lane]); else zero_row(g);
+      bool vn = false;
+      if (base + step < n) vn = pipe_valid(ring[s1].rows[lane], ring[s1].cols[lane], a.nnodes, a.status);
+      float xn[D1];
+      if (vn) load_row8<D1>(xn, xp, ring[s1].cols[lane]); else zero_row(xn);
+      // Block k.
       float h[D1], ev[D2];
       float sdot = 0.f;
 #pragma unroll
@@ -295,19 +324,17 @@ __global__ void __launch_bounds__(kEdgeWarps * 32) conv_bwd_edge1_pipe(const Arg
       for (int j = 0; j < D2; ++j) ev[j] = 0.f;
       const long long col = st.cols[lane];
       if (vc) {
-        float x[D1], y[D2], g[D3];
-        xc.get(x);
-        gc.get(g);
+        float y[D2];
 #pragma unroll
         for (int k = 0; k < D3; ++k) g[k] *= pw;
 #pragma unroll
         for (int j = 0; j < D2; ++j) y[j] = st.y[lane * D2 + j];
         CG<A, B, C>::hvec(g, y, h);
-        CG<A, B, C>::evec(g, x, ev);
+        CG<A, B, C>::evec(g, xc, ev);
         const float w = st.w[lane];
 #pragma unroll
         for (int i = 0; i < D1; ++i) {
-          sdot += x[i] * h[i];
+          sdot += xc[i] * h[i];
           h[i] *= w;
         }
 #pragma unroll
@@ -319,15 +346,15 @@ __global__ void __launch_bounds__(kEdgeWarps * 32) conv_bwd_edge1_pipe(const Arg
       __syncwarp();
       e1_stage_out<float, D2>(a.out1, yo, base, n, lane);
       e1_stage_out<float, 1>(a.out2, wo, base, n, lane);
-      if (vc) red_vec(a.out0 + col * D1, h);
+      if (vc) red_row8<D1>(dxp + col * kPadRow, h);
       __syncwarp();  // stage s and the output buffer are free again
-      xc = xn;
-      gc = gn;
+#pragma unroll
+      for (int i = 0; i < D1; ++i) xc[i] = xn[i];
       vc = vn;
       s = s1;
     }
     cp_async_wait<0>();
-  });
+  }
 }
 
 }  // namespace oeqb

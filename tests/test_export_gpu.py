@@ -96,10 +96,7 @@ def test_torch_export(tp_and_inputs):
 
 
 @functools.lru_cache(maxsize=None)
-def _cxx_has_openmp():
-    import shutil
-
-    cxx = shutil.which("g++") or "g++"
+def _has_openmp(cxx):
     with tempfile.TemporaryDirectory() as d:
         src = os.path.join(d, "t.cpp")
         with open(src, "w") as f:
@@ -110,14 +107,20 @@ def _cxx_has_openmp():
 
 
 @pytest.fixture(autouse=True)
-def _inductor_without_openmp(monkeypatch):
-    """AOTInductor always asks the host compiler for OpenMP on Linux.  The package's CUDA
-    wrapper does not use it, so where the compiler cannot provide it (no libgomp), the flags
-    are left out rather than failing the build."""
-    if not _cxx_has_openmp():
-        import torch._inductor.cpp_builder as cb
+def _inductor_compiler(monkeypatch):
+    """AOTInductor builds its wrapper with OpenMP.  Where the host compiler it finds first
+    cannot link OpenMP, it is pointed at the system g++ if that one can; without any such
+    compiler the tests that need it are skipped (a build without OpenMP loads incorrectly)."""
+    import torch._inductor.config as ic
+    import torch._inductor.cpp_builder as cb
 
-        monkeypatch.setattr(cb, "_get_openmp_args", lambda cpp_compiler: ([], [], [], [], [], []))
+    if _has_openmp(cb.get_cpp_compiler()):
+        return
+    alt = "/usr/bin/g++"
+    if os.path.exists(alt) and _has_openmp(alt):
+        monkeypatch.setattr(ic.cpp, "cxx", (None, alt))
+    else:
+        pytest.skip("no host C++ compiler with OpenMP for AOTInductor")
 
 
 def test_aoti_python(tp_and_inputs):
