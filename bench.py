@@ -53,7 +53,7 @@ def _args():
     ap.add_argument("--rows", type=int, default=None,
                     help="TP rows per GPU (default: the BASELINE config's batch, 50,000 for "
                          "c2/c2ml, 20,000 for c4)")
-    ap.add_argument("--e2e-steps", type=int, default=3)
+    ap.add_argument("--e2e-steps", type=int, default=6)
     ap.add_argument("--e2e-chunks", type=int, default=4,
                     help="row chunks per e2e step, one CUDA stream each (copies in both "
                          "directions overlap with each other and with the kernels)")
@@ -737,30 +737,70 @@ def bench_conv(args, world, rank, local):
     tr = _traffic(f"conv_{args.conv_mode}:conv_bwd_per_edge")
     traffic = tr * ni if tr else None
 
-    # e2e: host buffers of this rank's inputs and outputs through the same module.
+    # e2e: host buffers of this rank's inputs and outputs through the same module.  Every step
+    # copies its inputs in from pinned host memory and all four outputs back out.  Steps are
+    # software-pipelined over three streams: the copies in of step i + 1 and the copies out of
+    # step i - 1 run while step i computes (PCIe is full duplex), with two device buffer sets
+    # so that a copy never overwrites data a kernel still reads.
     hX, hY, hW, hG = (t.detach().cpu().pin_memory() for t in (X, Y, W, G))
-    outs = [torch.empty(part.n_own, 5).pin_memory(), torch.empty(part.n_own, 5).pin_memory(),
-            torch.empty_like(hY).pin_memory(), torch.empty_like(hW).pin_memory()]
+    outs = [[torch.empty(part.n_own, 5).pin_memory(), torch.empty(part.n_own, 5).pin_memory(),
+             torch.empty_like(hY).pin_memory(), torch.empty_like(hW).pin_memory()]
+            for _ in range(2)]
+    s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    s_cmp = torch.cuda.current_stream(dev)
+    dbuf = [[torch.empty(t.shape, device=dev) for t in (hX, hY, hW, hG)] for _ in range(2)]
+    ev_in = [torch.cuda.Event() for _ in range(2)]     # inputs of a set landed
+    ev_used = [torch.cuda.Event() for _ in range(2)]   # compute done with a set's inputs
+    ev_done = [torch.cuda.Event() for _ in range(2)]   # a set's outputs computed
+    ev_out = [torch.cuda.Event() for _ in range(2)]    # a set's outputs copied out
+    for e_ in ev_used + ev_out:
+        e_.record(s_cmp)
 
-    def e2e_step():
-        x = hX.to(dev, non_blocking=True).requires_grad_()
-        y = hY.to(dev, non_blocking=True).requires_grad_()
-        w = hW.to(dev, non_blocking=True).requires_grad_()
-        g = hG.to(dev, non_blocking=True)
+    def e2e_copy_in(i):
+        b = i & 1
+        with torch.cuda.stream(s_in):
+            s_in.wait_event(ev_used[b])
+            for d, h in zip(dbuf[b], (hX, hY, hW, hG)):
+                d.copy_(h, non_blocking=True)
+            ev_in[b].record(s_in)
+
+    def e2e_compute(i):
+        b = i & 1
+        s_cmp.wait_event(ev_in[b])
+        s_cmp.wait_event(ev_out[b])
+        x, y, w = (t.detach().requires_grad_() for t in dbuf[b][:3])
         z = pc(x, y, w)
-        gx, gy, gw = torch.autograd.grad(z, (x, y, w), g)
-        for h, d in zip(outs, (z.detach(), gx, gy, gw)):
-            h.copy_(d, non_blocking=True)
+        gx, gy, gw = torch.autograd.grad(z, (x, y, w), dbuf[b][3])
+        ev_used[b].record(s_cmp)
+        res = (z.detach(), gx, gy, gw)
+        ev_done[b].record(s_cmp)
+        return res
 
-    e2e_step()
+    def e2e_copy_out(i, res):
+        b = i & 1
+        with torch.cuda.stream(s_out):
+            s_out.wait_event(ev_done[b])
+            for h, d in zip(outs[b], res):
+                d.record_stream(s_out)
+                h.copy_(d, non_blocking=True)
+            ev_out[b].record(s_out)
+
+    def e2e_run(steps):
+        e2e_copy_in(0)
+        for i in range(steps):
+            if i + 1 < steps:
+                e2e_copy_in(i + 1)
+            e2e_copy_out(i, e2e_compute(i))
+
+    e2e_run(2)
     torch.cuda.synchronize()
     E2 = max(1, args.e2e_steps)
     _barrier(world)
     t0 = time.perf_counter()
-    for _ in range(E2):
-        e2e_step()
+    e2e_run(E2)
     torch.cuda.synchronize()
     e2e_s = _max_over_ranks(time.perf_counter() - t0, world)
+    outs = outs[0]
     h2d = sum(t.numel() for t in (hX, hY, hW, hG)) * 4
     d2h = sum(t.numel() for t in outs) * 4
     line = {
@@ -786,7 +826,8 @@ def bench_conv(args, world, rank, local):
         "e2e": {"value": E * E2 / e2e_s, "unit": UNIT, "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "steps": E2,
                 "path": "PartitionedConv forward+backward (public module API), pinned host "
-                        "buffers per rank"},
+                        "buffers per rank; copies in of the next step and out of the previous "
+                        "step overlap each step's compute (three streams)"},
         "gpu_launches": launches * K,
         "clocks": clocks,
     }

@@ -6,7 +6,8 @@ backward) runs repeatedly on two user streams of different priority under the pr
 library's kernels (namespace ``oeqb``) must run on exactly those two streams, the same number
 of times on each, and with the kernel names the pass is expected to launch.  The reference pins
 its JIT kernel names (``forward``, ``backward``, ``double_backward_A/B``, ``fixup_*``); the
-names here are this library's, matched by the pass they belong to.
+names here are this library's, matched by the pass they belong to (plus the node-row layout
+copies ``conv_pad_rows`` / ``conv_unpad_rows`` of the single-path kernels).
 """
 
 import json
@@ -115,6 +116,8 @@ def test_separate_streams(which, tmp_path, cuda_device):
     seen = set()
     for names in by_stream.values():
         for n in names:
+            if "pad_rows" in n:
+                continue  # node-row layout copies of the single-path kernels (either pass)
             tags = {t for t in ("fwd", "bwd") if t in n}
             assert tags, f"unexpected kernel {n}"
             seen |= tags
