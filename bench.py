@@ -831,6 +831,31 @@ def bench_conv(args, world, rank, local):
         "gpu_launches": launches * K,
         "clocks": clocks,
     }
+    line["conv_kernels"] = {
+        args.conv_mode: {"fwd_ms": t_fwd, "bwd_ms": t_bwd, "fwd_frac": line["roofline"]["fwd_frac"],
+                         "bwd_frac": line["roofline"]["frac"]}}
+    if world == 1:
+        # The other mode's kernels on the same graph (the deterministic forward writes each
+        # receiver row once; its backward is two passes over per-edge records).
+        other = "atomic" if det else "deterministic"
+        conv2 = oeq.TensorProductConv(problem, deterministic=not det)
+        ops = torch.ops.libtorch_tp_jit
+        tp2 = part.tperm_int if not det else conv2.dummy_transpose_perm
+        Gl2 = torch.randn(nl, 5, device=dev)
+
+        def f2():
+            return ops.jit_conv_forward(conv2.kernel, conv2.hash, Xl, Yd, Wd, 5, part.rows_int,
+                                        part.cols_int, conv2.workspace_buffer, tp2)
+
+        def b2():
+            return ops.jit_conv_backward(conv2.kernel, conv2.hash, Xl, Yd, Wd, Gl2, part.rows_int,
+                                         part.cols_int, conv2.workspace_buffer, tp2)
+
+        tf2, tb2 = _ev_ms(f2), _ev_ms(b2)
+        line["conv_kernels"][other] = {
+            "fwd_ms": tf2, "bwd_ms": tb2,
+            "fwd_frac": conv_bytes(ni, nl, True, not det) / (tf2 * 1e-3) / 1e9 / peak,
+            "bwd_frac": conv_bytes(ni, nl, False, not det) / (tb2 * 1e-3) / 1e9 / peak}
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline_conv(rows, cols)
     del graph, run  # release the captured NCCL work before the process group goes

@@ -1398,16 +1398,22 @@ bool edge1_pipe_enabled() {
   return on;
 }
 
-// The plan class of the pipelined kernels (pointer alignment is checked per call).
+// The plan class of the pipelined kernels, atomic or deterministic (without Kahan); pointer
+// alignment is checked per call.
 bool edge1_pipe_class(const oeqb_plan& p) {
   const int d1 = 2 * ((p.edge1.code >> 8) & 15) + 1, d3 = 2 * (p.edge1.code & 15) + 1;
-  return edge1_pipe_enabled() && p.dtype == 1 && !p.det && p.edge1_ok && !p.shared_w &&
+  return edge1_pipe_enabled() && p.dtype == 1 && !p.kahan && p.edge1_ok && !p.shared_w &&
          p.wnumel == 1 && d1 <= 8 && d3 <= 8 && edge1_pipe_kernel(0, p.edge1.code) != nullptr;
 }
 
-// Workspace of the pipelined kernels: X, dZ and the dX accumulator in 32-byte rows.
+// Workspace of the pipelined kernels, in 32-byte node rows: X | dZ | then the dX accumulator
+// (atomic) or one 32-byte record per edge (deterministic backward pass A).
 constexpr size_t kPadRowBytes = 32;
-size_t edge1_pipe_ws_bytes(int64_t nodes) { return 3 * kPadRowBytes * size_t(nodes) + 256; }
+size_t edge1_pipe_ws_bytes(const oeqb_plan& p, int64_t nnz, int64_t nodes) {
+  const size_t rows = 2 * kPadRowBytes * size_t(std::max<int64_t>(nodes, 0));
+  return rows + (p.det ? kPadRowBytes * size_t(std::max<int64_t>(nnz, 0))
+                       : kPadRowBytes * size_t(std::max<int64_t>(nodes, 0))) + 256;
+}
 
 template <class T>
 bool edge1_pipe_ok(const oeqb_plan& p, const Args<T>& a, const void* ws, size_t ws_bytes) {
@@ -1415,7 +1421,7 @@ bool edge1_pipe_ok(const oeqb_plan& p, const Args<T>& a, const void* ws, size_t 
     return false;
   } else {
     return edge1_pipe_class(p) && ws && aligned16(ws) &&
-           ws_bytes >= edge1_pipe_ws_bytes(a.nnodes) && aligned16(a.rows) &&
+           ws_bytes >= edge1_pipe_ws_bytes(p, a.nitems, a.nnodes) && aligned16(a.rows) &&
            aligned16(a.cols) && aligned16(a.W) && aligned16(a.Y);
   }
 }
@@ -1444,12 +1450,15 @@ int launch_unpad(const oeqb_plan& p, const float* src, float* dst, int d, long l
   return 0;
 }
 
-// kind 0: forward (pads X into the workspace first); kind 1: backward (pads X and dZ, clears
-// the dX accumulator, runs, then writes dX).
+// Forward (pads X into the workspace first): kind 0 atomic, 4 deterministic.  Backward (pads
+// X and dZ): kind 1 atomic (clears the padded dX accumulator, then copies dX out), kind 5
+// deterministic (pass A writes the per-edge records, pass B, conv_bwd_edge1_gather, sums them
+// per sender).
 template <class T>
 int launch_edge1_pipe(oeqb_plan& p, int kind, const Args<T>& a, void* ws, cudaStream_t stream) {
+  const bool bwd = kind == 1 || kind == 5;
   if (a.nitems <= 0) {
-    if (kind == 1) OEQB_CUDA(cudaMemsetAsync(a.out0, 0, sizeof(T) * size_t(a.nnodes) * p.L1dim, stream));
+    if (bwd) OEQB_CUDA(cudaMemsetAsync(a.out0, 0, sizeof(T) * size_t(a.nnodes) * p.L1dim, stream));
     return 0;
   }
   const void* kernel = edge1_pipe_kernel(kind, p.edge1.code);
@@ -1457,19 +1466,21 @@ int launch_edge1_pipe(oeqb_plan& p, int kind, const Args<T>& a, void* ws, cudaSt
   const int d1 = 2 * ((p.edge1.code >> 8) & 15) + 1, d3 = 2 * (p.edge1.code & 15) + 1;
   float* xp = static_cast<float*>(ws);
   float* gp = xp + 8 * size_t(a.nnodes);
-  float* dxp = gp + 8 * size_t(a.nnodes);
-  if (kind == 0) {
+  float* tail = gp + 8 * size_t(a.nnodes);  // dX accumulator (kind 1) or records (kind 5)
+  if (!bwd) {
     if (int rc = launch_pad(p, reinterpret_cast<const float*>(a.X), d1, xp, nullptr, 0, nullptr,
                             nullptr, a.nnodes, stream))
       return rc;
   } else {
     if (int rc = launch_pad(p, reinterpret_cast<const float*>(a.X), d1, xp,
-                            reinterpret_cast<const float*>(a.Gz), d3, gp, dxp, a.nnodes, stream))
+                            reinterpret_cast<const float*>(a.Gz), d3, gp,
+                            kind == 1 ? tail : nullptr, a.nnodes, stream))
       return rc;
   }
   const int d2 = 2 * ((p.edge1.code >> 4) & 15) + 1;
   const size_t stage = 2 * 32 * sizeof(long long) + 32 * sizeof(float) * (1 + d2);
-  const size_t per_warp = 3 * stage + (kind == 1 ? 32 * sizeof(float) * (d2 + 1) : 0);
+  const size_t per_warp = 3 * stage + (bwd ? 32 * sizeof(float) * (d2 + 1) : 0) +
+                          (kind == 5 ? 32 * sizeof(float) * kE1Rec : 0);
   const size_t smem = size_t(kEdgeWarps) * per_warp;
   int per_sm;
   {
@@ -1486,16 +1497,21 @@ int launch_edge1_pipe(oeqb_plan& p, int kind, const Args<T>& a, void* ws, cudaSt
   }
   const long long cap = (long long)p.sm_count * per_sm;
   const long long warps = (a.nitems + 31) / 32;
-  const long long blocks = std::max<long long>(1, std::min<long long>((warps + kEdgeWarps - 1) / kEdgeWarps, cap));
+  // The deterministic forward's partition is fixed (its summation order must not depend on
+  // the launch); the others cover the edges with at most one resident wave.
+  const long long blocks =
+      kind == 4 ? cap
+                : std::max<long long>(1, std::min<long long>((warps + kEdgeWarps - 1) / kEdgeWarps, cap));
   Edge1 e = p.edge1;
   const float* cxp = xp;
   const float* cgp = gp;
   void* params_f[] = {const_cast<Args<T>*>(&a), &e, &cxp};
-  void* params_b[] = {const_cast<Args<T>*>(&a), &e, &cxp, &cgp, &dxp};
+  void* params_b[] = {const_cast<Args<T>*>(&a), &e, &cxp, &cgp, &tail};
   OEQB_CUDA(cudaLaunchKernel(kernel, dim3(static_cast<unsigned>(blocks)), dim3(kEdgeWarps * 32),
-                             kind == 0 ? params_f : params_b, smem, stream));
+                             bwd ? params_b : params_f, smem, stream));
   if (kind == 1)
-    return launch_unpad(p, dxp, reinterpret_cast<float*>(a.out0), d1, a.nnodes, stream);
+    return launch_unpad(p, tail, reinterpret_cast<float*>(a.out0), d1, a.nnodes, stream);
+  if (kind == 5) return launch_edge1<T>(p, 6, a, reinterpret_cast<T*>(tail), stream);
   return 0;
 }
 
@@ -1648,6 +1664,7 @@ int conv_fwd_t(oeqb_plan* p, bool db, const void* X, const void* Y, const void* 
   a.rows = reinterpret_cast<const long long*>(rows);
   a.cols = reinterpret_cast<const long long*>(cols);
   if (p->det) {
+    if (!db && edge1_pipe_ok(*p, a, ws, ws_bytes)) return launch_edge1_pipe<T>(*p, 4, a, ws, s);
     if (!db && p->edge1_ok && !p->kahan && aligned16(Y))
       return launch_edge1<T>(*p, 4, a, nullptr, s);
     return launch(*p, det_kernel_ptr<T>(0, p->uvw, db, p->kahan), a, true, true, s);
@@ -1679,9 +1696,13 @@ int conv_bwd_t(oeqb_plan* p, bool db, const void* X, const void* Y, const void* 
   a.rows = reinterpret_cast<const long long*>(rows);
   a.cols = reinterpret_cast<const long long*>(cols);
   a.perm = reinterpret_cast<const long long*>(perm);
-  // The pipelined backward writes every dX row itself (through its padded accumulator).
-  if (!db && edge1_pipe_ok(*p, a, ws, ws_bytes) && aligned16(gY) && aligned16(gW))
-    return launch_edge1_pipe<T>(*p, 1, a, ws, s);
+  // The pipelined backward writes every dX row itself (through its padded accumulator, or the
+  // per-sender sums of pass B).
+  if (!db && edge1_pipe_ok(*p, a, ws, ws_bytes) && aligned16(gY) && aligned16(gW)) {
+    if (!p->det) return launch_edge1_pipe<T>(*p, 1, a, ws, s);
+    if (!perm) return fail(OEQB_ERR_INVALID, "deterministic convolution needs transpose_perm");
+    return launch_edge1_pipe<T>(*p, 5, a, ws, s);
+  }
   OEQB_CUDA(cudaMemsetAsync(gX, 0, sizeof(T) * size_t(nodes) * p->L1dim, s));
   if (p->shared_w) OEQB_CUDA(cudaMemsetAsync(gW, 0, sizeof(T) * p->wnumel, s));
   if (p->det) {
@@ -1832,7 +1853,7 @@ int oeqb_plan_destroy(oeqb_plan* p) {
 
 size_t oeqb_conv_workspace_bytes(const oeqb_plan* p, int64_t nnz, int64_t node_count) {
   if (!p) return 0;
-  if (edge1_pipe_class(*p)) return edge1_pipe_ws_bytes(node_count);
+  if (edge1_pipe_class(*p)) return edge1_pipe_ws_bytes(*p, nnz, node_count);
   return edge1_det_ws_bytes(*p, nnz);
 }
 

@@ -4,15 +4,22 @@
 
 namespace oeqb {
 
-// kind 0 / 1: pipelined atomic forward / backward of the triple `code`; 2 / 3: the row
-// padding kernels.  nullptr for a triple without an unrolled contraction.
+// kind 0 / 1: pipelined atomic forward / backward of the triple `code`; 4 / 5: deterministic
+// forward / backward pass A; 2 / 3: the row padding kernels.  nullptr for a triple without an
+// unrolled contraction.
 const void* edge1_pipe_kernel(int kind, int code) {
   if (kind == 2) return reinterpret_cast<const void*>(conv_pad_rows);
   if (kind == 3) return reinterpret_cast<const void*>(conv_unpad_rows);
-#define OEQB_PIPE_CASE(A, B, C)                                                      \
-  if (code == triple_code(A, B, C))                                                  \
-    return kind == 0 ? reinterpret_cast<const void*>(conv_fwd_edge1_pipe<A, B, C>)   \
-                     : reinterpret_cast<const void*>(conv_bwd_edge1_pipe<A, B, C>);
+#define OEQB_PIPE_CASE(A, B, C)                                                               \
+  if (code == triple_code(A, B, C)) {                                                         \
+    switch (kind) {                                                                           \
+      case 0: return reinterpret_cast<const void*>(conv_fwd_edge1_pipe<A, B, C>);             \
+      case 1: return reinterpret_cast<const void*>(conv_bwd_edge1_pipe<A, B, C, false>);      \
+      case 4: return reinterpret_cast<const void*>(conv_fwd_edge1_det_pipe<A, B, C>);         \
+      case 5: return reinterpret_cast<const void*>(conv_bwd_edge1_pipe<A, B, C, true>);       \
+      default: return nullptr;                                                                \
+    }                                                                                         \
+  }
   OEQB_FOR_EACH_TRIPLE(OEQB_PIPE_CASE)
 #undef OEQB_PIPE_CASE
   return nullptr;

@@ -270,11 +270,20 @@ __host__ __device__ constexpr size_t pipe_bwd_warp_bytes() {
   return pipe_warp_bytes<D2>() + sizeof(float) * 32 * (D2 + 1);
 }
 
-template <int A, int B, int C>
+// REC = false: atomic mode, dX reduced into the padded accumulator `out`.  REC = true: pass A
+// of the deterministic backward, each edge's message to its sender (D1 values and the
+// sender's index in the last of 8 slots: kE1Rec) written to `out` as one 32-byte record, in
+// edge order; pass B (conv_bwd_edge1_gather) sums them per sender in transpose_perm order.
+template <int D2, bool REC>
+__host__ __device__ constexpr size_t pipe_bwd_warp_bytes_m() {
+  return pipe_bwd_warp_bytes<D2>() + (REC ? sizeof(float) * 32 * kE1Rec : 0);
+}
+
+template <int A, int B, int C, bool REC>
 __global__ void __launch_bounds__(kEdgeWarps * 32) conv_bwd_edge1_pipe(const Args<float> a, const Edge1 p,
                                                                        const float* __restrict__ xp,
                                                                        const float* __restrict__ gp,
-                                                                       float* __restrict__ dxp) {
+                                                                       float* __restrict__ out) {
   extern __shared__ __align__(16) unsigned char smem[];
   const int lane = threadIdx.x & 31;
   const long long nw = static_cast<long long>(gridDim.x) * kEdgeWarps;
@@ -282,10 +291,11 @@ __global__ void __launch_bounds__(kEdgeWarps * 32) conv_bwd_edge1_pipe(const Arg
   const float pw = static_cast<float>(p.pw);
   {
     constexpr int D1 = 2 * A + 1, D2 = 2 * B + 1, D3 = 2 * C + 1;
-    unsigned char* wbase = smem + (threadIdx.x >> 5) * pipe_bwd_warp_bytes<D2>();
+    unsigned char* wbase = smem + (threadIdx.x >> 5) * pipe_bwd_warp_bytes_m<D2, REC>();
     auto* ring = reinterpret_cast<PipeStage<D2>*>(wbase);
     float* yo = reinterpret_cast<float*>(wbase + pipe_warp_bytes<D2>());  // [32 * D2] dY
     float* wo = yo + 32 * D2;                                              // [32] dW
+    float* ho = wo + 32;                                                   // [32 * 8] records
     const long long step = nw * 32;
     long long base = (static_cast<long long>(blockIdx.x) * kEdgeWarps + (threadIdx.x >> 5)) * 32;
     if (base >= n) return;
@@ -343,11 +353,19 @@ __global__ void __launch_bounds__(kEdgeWarps * 32) conv_bwd_edge1_pipe(const Arg
 #pragma unroll
       for (int j = 0; j < D2; ++j) yo[lane * D2 + j] = ev[j];
       wo[lane] = sdot;
+      if constexpr (REC) {
+#pragma unroll
+        for (int i = 0; i < kE1Rec - 1; ++i) ho[lane * kE1Rec + i] = i < D1 ? h[i] : 0.f;
+        ho[lane * kE1Rec + kE1Rec - 1] = e1_key_bits<float>(vc ? col : -1);
+      }
       __syncwarp();
       e1_stage_out<float, D2>(a.out1, yo, base, n, lane);
       e1_stage_out<float, 1>(a.out2, wo, base, n, lane);
-      if (vc) red_row8<D1>(dxp + col * kPadRow, h);
-      __syncwarp();  // stage s and the output buffer are free again
+      if constexpr (REC)
+        e1_stage_out<float, kE1Rec>(out, ho, base, n, lane);
+      else if (vc)
+        red_row8<D1>(out + col * kPadRow, h);
+      __syncwarp();  // stage s and the output buffers are free again
 #pragma unroll
       for (int i = 0; i < D1; ++i) xc[i] = xn[i];
       vc = vn;
@@ -355,6 +373,85 @@ __global__ void __launch_bounds__(kEdgeWarps * 32) conv_bwd_edge1_pipe(const Arg
     }
     cp_async_wait<0>();
   }
+}
+
+// Deterministic forward (same mapping as conv_fwd_edge1_det): warp w owns the edges of whole
+// receivers, its nominal range [w E / W, (w+1) E / W) moved forward to receiver boundaries,
+// and walks it in consecutive 32-edge blocks starting at the 4-aligned edge at or below the
+// range start (so Y rows start 16-byte aligned; lanes before the range are masked).  Sums of
+// receivers that continue into the next block are carried in registers, and every receiver
+// row is written once with plain stores: the result does not depend on timing.  The per-edge
+// streams go through the cp.async ring, the X rows (padded layout) are gathered a block ahead.
+template <int A, int B, int C>
+__global__ void __launch_bounds__(kEdgeWarps * 32) conv_fwd_edge1_det_pipe(const Args<float> a, const Edge1 p,
+                                                                           const float* __restrict__ xp) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  const int lane = threadIdx.x & 31;
+  const long long nwarps = static_cast<long long>(gridDim.x) * kEdgeWarps;
+  const long long wg = static_cast<long long>(blockIdx.x) * kEdgeWarps + (threadIdx.x >> 5);
+  const long long n = a.nitems;
+  const float pw = static_cast<float>(p.pw);
+  auto key = [&](long long e) { return a.rows[e]; };
+  const long long p0 = e1_snap(static_cast<long long>((static_cast<__int128>(n) * wg) / nwarps), n, key, lane);
+  const long long p1 = e1_snap(static_cast<long long>((static_cast<__int128>(n) * (wg + 1)) / nwarps), n, key, lane);
+  if (p0 >= p1) return;
+  constexpr int D1 = 2 * A + 1, D2 = 2 * B + 1, D3 = 2 * C + 1;
+  auto* ring = reinterpret_cast<PipeStage<D2>*>(smem + (threadIdx.x >> 5) * pipe_warp_bytes<D2>());
+  // Validity of lane `lane` of the block at `base`: inside [p0, p1) with good indices.
+  auto valid = [&](const PipeStage<D2>& st, long long base) {
+    const long long e = base + lane;
+    if (e < p0 || e >= p1) return false;
+    return pipe_valid(st.rows[lane], st.cols[lane], a.nnodes, a.status);
+  };
+  long long base = p0 & ~3LL;
+  pipe_stage_in<D2>(ring[0], a.rows, a.cols, a.W, a.Y, base, p1, lane);
+  cp_async_commit();
+  pipe_stage_in<D2>(ring[1], a.rows, a.cols, a.W, a.Y, base + 32, p1, lane);
+  cp_async_commit();
+  cp_async_wait<1>();
+  __syncwarp();
+  bool vc = valid(ring[0], base);
+  float xc[D1];
+  if (vc) load_row8<D1>(xc, xp, ring[0].cols[lane]); else zero_row(xc);
+  float carry[D3];
+  long long carry_key = -2;
+  int s = 0;
+  for (; base < p1; base += 32) {
+    const int s1 = s == kPipeStages - 1 ? 0 : s + 1;
+    const int s2 = s1 == kPipeStages - 1 ? 0 : s1 + 1;
+    pipe_stage_in<D2>(ring[s2], a.rows, a.cols, a.W, a.Y, base + 64, p1, lane);
+    cp_async_commit();
+    cp_async_wait<1>();
+    __syncwarp();
+    const bool more = base + 32 < p1;
+    bool vn = false;
+    if (more) vn = valid(ring[s1], base + 32);
+    float xn[D1];
+    if (vn) load_row8<D1>(xn, xp, ring[s1].cols[lane]); else zero_row(xn);
+    const PipeStage<D2>& st = ring[s];
+    float z[D3];
+#pragma unroll
+    for (int k = 0; k < D3; ++k) z[k] = 0.f;
+    if (vc) {
+      float x[D1], y[D2];
+      const float w = st.w[lane] * pw;
+#pragma unroll
+      for (int i = 0; i < D1; ++i) x[i] = xc[i] * w;
+#pragma unroll
+      for (int j = 0; j < D2; ++j) y[j] = st.y[lane * D2 + j];
+      CG<A, B, C>::fwd(x, y, z);
+    }
+    // First receiver of the next block (lane 0 of its stage), to tell whether the last run
+    // continues.
+    const long long nk = more ? ring[s1].rows[0] : -3;
+    e1_seg_block<float, D3>(z, vc ? st.rows[lane] : -1, nk, more, carry, carry_key, a.out0, lane);
+    __syncwarp();
+#pragma unroll
+    for (int i = 0; i < D1; ++i) xc[i] = xn[i];
+    vc = vn;
+    s = s1;
+  }
+  cp_async_wait<0>();
 }
 
 }  // namespace oeqb
