@@ -137,6 +137,29 @@ int oeqb_conv_double_backward(oeqb_plan* plan, const void* L1_in, const void* L2
                               void* workspace, size_t workspace_bytes,
                               const int64_t* transpose_perm, void* stream);
 
+/* ---- convolution on node arrays in padded rows (no counterpart in the reference) ----
+ * For float32 atomic plans of the single-path multiplicity-1 class with one weight per edge
+ * (oeqb_conv_rows8_ok returns 1).  Node arrays are [node_count, 8] floats: row n of X (or dZ,
+ * dX) in the first L1 (L3) of its 8 slots, 32-byte aligned rows, the padding slots zero.  This
+ * is the kernels' own layout, so callers that keep node data in it for many calls (the
+ * multi-GPU partition of openequivariance_b200.distributed, whose halo rows arrive from other
+ * GPUs straight into such a buffer) skip the per-call layout copies of oeqb_conv_forward /
+ * oeqb_conv_backward.  Y, W, dY, dW, rows and cols are as there.
+ *   forward:  Z [node_count, L3_dim] (unpadded) = sum over edges (accumulate = 0), or += it
+ *             (accumulate != 0);
+ *   backward: dY, dW written; dX contributions added into the padded accumulator dxp (the
+ *             caller clears it).
+ * reserve_sms leaves that many SMs without CTAs of the launch, for work that runs beside it
+ * (e.g. a collective).  All arrays 16-byte aligned. */
+int oeqb_conv_rows8_ok(const oeqb_plan* plan);
+int oeqb_conv_forward_rows8(oeqb_plan* plan, const float* xp, const float* Y, const float* W,
+                            float* Z, const int64_t* rows, const int64_t* cols, int64_t nnz,
+                            int64_t node_count, int accumulate, int reserve_sms, void* stream);
+int oeqb_conv_backward_rows8(oeqb_plan* plan, const float* xp, const float* gp, const float* Y,
+                             const float* W, float* dY, float* dW, float* dxp,
+                             const int64_t* rows, const int64_t* cols, int64_t nnz,
+                             int64_t node_count, int reserve_sms, void* stream);
+
 /* ---- MACE symmetric contraction (replaces the group_gemm + torch pipeline of
  * _torch/symmetric_contraction/SymmetricContraction.py:124-336 and extension/group_mm.hpp) ----
  * The contraction of correlation <= 3 is a polynomial of degree <= 3 in the k components of

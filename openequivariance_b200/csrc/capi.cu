@@ -1454,6 +1454,48 @@ int launch_unpad(const oeqb_plan& p, const float* src, float* dst, int d, long l
 // X and dZ): kind 1 atomic (clears the padded dX accumulator, then copies dX out), kind 5
 // deterministic (pass A writes the per-edge records, pass B, conv_bwd_edge1_gather, sums them
 // per sender).
+// Main kernel of the pipelined single-path pass `kind` on node arrays already in the padded
+// layout (xp, gp, and out = the padded dX accumulator or the records).  reserve_sms SMs are
+// left without CTAs of this launch (so that, e.g., a collective running beside it gets SMs).
+template <class T>
+int launch_edge1_pipe_main(oeqb_plan& p, int kind, const Args<T>& a, const float* xp,
+                           const float* gp, float* out, int reserve_sms, cudaStream_t stream) {
+  const bool bwd = kind == 1 || kind == 5;
+  const void* kernel = edge1_pipe_kernel(kind, p.edge1.code);
+  if (!kernel) return fail(OEQB_ERR_UNSUPPORTED, "no pipelined kernel for this degree triple");
+  const int d2 = 2 * ((p.edge1.code >> 4) & 15) + 1;
+  const int epw = kind == 0 ? 64 : 32;  // edges per warp step (the atomic forward takes two per lane)
+  const size_t stage = 2 * epw * sizeof(long long) + epw * sizeof(float) * (1 + d2);
+  const size_t per_warp = 3 * stage + (bwd ? 32 * sizeof(float) * (d2 + 1) : 0) +
+                          (kind == 5 ? 32 * sizeof(float) * kE1Rec : 0);
+  const size_t smem = size_t(kEdgeWarps) * per_warp;
+  int per_sm;
+  {
+    std::lock_guard<std::mutex> g(p.mu);
+    auto it = p.occ.find(kernel);
+    if (it == p.occ.end()) {
+      if (int rc = allow_max_smem(p.device, kernel)) return rc;
+      int n = 0;
+      OEQB_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kernel, kEdgeWarps * 32, smem));
+      if (n <= 0) return fail(OEQB_ERR_UNSUPPORTED, "pipelined edge kernel does not fit");
+      it = p.occ.emplace(kernel, n).first;
+    }
+    per_sm = it->second;
+  }
+  const int sms = std::max(1, p.sm_count - std::max(0, reserve_sms));
+  const long long cap = (long long)sms * per_sm;
+  const long long warps = (a.nitems + epw - 1) / epw;
+  const long long blocks =
+      kind == 4 ? (long long)p.sm_count * per_sm
+                : std::max<long long>(1, std::min<long long>((warps + kEdgeWarps - 1) / kEdgeWarps, cap));
+  Edge1 e = p.edge1;
+  void* params_f[] = {const_cast<Args<T>*>(&a), &e, &xp};
+  void* params_b[] = {const_cast<Args<T>*>(&a), &e, &xp, &gp, &out};
+  OEQB_CUDA(cudaLaunchKernel(kernel, dim3(static_cast<unsigned>(blocks)), dim3(kEdgeWarps * 32),
+                             bwd ? params_b : params_f, smem, stream));
+  return 0;
+}
+
 template <class T>
 int launch_edge1_pipe(oeqb_plan& p, int kind, const Args<T>& a, void* ws, cudaStream_t stream) {
   const bool bwd = kind == 1 || kind == 5;
@@ -1477,41 +1519,32 @@ int launch_edge1_pipe(oeqb_plan& p, int kind, const Args<T>& a, void* ws, cudaSt
                             kind == 1 ? tail : nullptr, a.nnodes, stream))
       return rc;
   }
-  const int d2 = 2 * ((p.edge1.code >> 4) & 15) + 1;
-  const size_t stage = 2 * 32 * sizeof(long long) + 32 * sizeof(float) * (1 + d2);
-  const size_t per_warp = 3 * stage + (bwd ? 32 * sizeof(float) * (d2 + 1) : 0) +
-                          (kind == 5 ? 32 * sizeof(float) * kE1Rec : 0);
-  const size_t smem = size_t(kEdgeWarps) * per_warp;
-  int per_sm;
-  {
-    std::lock_guard<std::mutex> g(p.mu);
-    auto it = p.occ.find(kernel);
-    if (it == p.occ.end()) {
-      if (int rc = allow_max_smem(p.device, kernel)) return rc;
-      int n = 0;
-      OEQB_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kernel, kEdgeWarps * 32, smem));
-      if (n <= 0) return fail(OEQB_ERR_UNSUPPORTED, "pipelined edge kernel does not fit");
-      it = p.occ.emplace(kernel, n).first;
-    }
-    per_sm = it->second;
-  }
-  const long long cap = (long long)p.sm_count * per_sm;
-  const long long warps = (a.nitems + 31) / 32;
-  // The deterministic forward's partition is fixed (its summation order must not depend on
-  // the launch); the others cover the edges with at most one resident wave.
-  const long long blocks =
-      kind == 4 ? cap
-                : std::max<long long>(1, std::min<long long>((warps + kEdgeWarps - 1) / kEdgeWarps, cap));
+  if (int rc = launch_edge1_pipe_main<T>(p, kind, a, xp, gp, tail, 0, stream)) return rc;
   Edge1 e = p.edge1;
-  const float* cxp = xp;
-  const float* cgp = gp;
-  void* params_f[] = {const_cast<Args<T>*>(&a), &e, &cxp};
-  void* params_b[] = {const_cast<Args<T>*>(&a), &e, &cxp, &cgp, &tail};
-  OEQB_CUDA(cudaLaunchKernel(kernel, dim3(static_cast<unsigned>(blocks)), dim3(kEdgeWarps * 32),
-                             bwd ? params_b : params_f, smem, stream));
   if (kind == 1)
     return launch_unpad(p, tail, reinterpret_cast<float*>(a.out0), d1, a.nnodes, stream);
-  if (kind == 5) return launch_edge1<T>(p, 6, a, reinterpret_cast<T*>(tail), stream);
+  if (kind == 5) {
+    // Pass B over a fixed partition (resident CTAs of the whole device): its summation order
+    // must not depend on the launch.
+    const void* kb = edge1_pipe_kernel(6, p.edge1.code);
+    if (!kb) return launch_edge1<T>(p, 6, a, reinterpret_cast<T*>(tail), stream);
+    int nb;
+    {
+      std::lock_guard<std::mutex> g(p.mu);
+      auto it = p.occ.find(kb);
+      if (it == p.occ.end()) {
+        int m = 0;
+        OEQB_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&m, kb, kEdgeWarps * 32, 0));
+        if (m <= 0) return fail(OEQB_ERR_UNSUPPORTED, "pass B kernel does not fit");
+        it = p.occ.emplace(kb, m).first;
+      }
+      nb = it->second;
+    }
+    const float* recs = tail;
+    void* pb[] = {const_cast<Args<T>*>(&a), &e, &recs};
+    OEQB_CUDA(cudaLaunchKernel(kb, dim3(static_cast<unsigned>(p.sm_count * nb)),
+                               dim3(kEdgeWarps * 32), pb, 0, stream));
+  }
   return 0;
 }
 
@@ -1997,6 +2030,65 @@ int oeqb_conv_double_backward(oeqb_plan* p, const void* L1_in, const void* L2_in
   return conv_bwd_t<double>(p, true, L1_in, L2_in, W, L3_grad, L1_dgrad, L2_dgrad, W_dgrad,
                             L1_grad, L2_grad, W_grad, rows, cols, transpose_perm, nnz, node_count,
                             nullptr, 0, s);
+}
+
+int oeqb_conv_rows8_ok(const oeqb_plan* p) {
+  return p && !p->det && edge1_pipe_class(*p) ? 1 : 0;
+}
+
+namespace {
+int rows8_check(const oeqb_plan* p, const void* xp, const float* Y, const float* W,
+                const int64_t* rows, const int64_t* cols, int64_t nnz, int64_t nodes) {
+  if (int rc = check_plan(p)) return rc;
+  if (!oeqb_conv_rows8_ok(p))
+    return fail(OEQB_ERR_UNSUPPORTED, "the padded-row entry points take float32 atomic "
+                                      "single-path plans with one weight per edge");
+  if (nnz < 0 || nodes < 0) return fail(OEQB_ERR_INVALID, "negative size");
+  if (!aligned16(xp) || !aligned16(Y) || !aligned16(W) || !aligned16(rows) || !aligned16(cols))
+    return fail(OEQB_ERR_INVALID, "padded-row entry points need 16-byte aligned arrays");
+  return 0;
+}
+}  // namespace
+
+int oeqb_conv_forward_rows8(oeqb_plan* p, const float* xp, const float* Y, const float* W,
+                            float* Z, const int64_t* rows, const int64_t* cols, int64_t nnz,
+                            int64_t node_count, int accumulate, int reserve_sms, void* stream) {
+  if (int rc = rows8_check(p, xp, Y, W, rows, cols, nnz, node_count)) return rc;
+  DeviceGuard g(p->device);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (!accumulate) OEQB_CUDA(cudaMemsetAsync(Z, 0, sizeof(float) * size_t(node_count) * p->L3dim, s));
+  if (nnz == 0) return 0;
+  Args<float> a = base_args<float>(*p, true);
+  a.nitems = nnz;
+  a.nnodes = node_count;
+  a.Y = Y;
+  a.W = W;
+  a.out0 = Z;
+  a.rows = reinterpret_cast<const long long*>(rows);
+  a.cols = reinterpret_cast<const long long*>(cols);
+  return launch_edge1_pipe_main<float>(*p, 0, a, xp, nullptr, nullptr, reserve_sms, s);
+}
+
+int oeqb_conv_backward_rows8(oeqb_plan* p, const float* xp, const float* gp, const float* Y,
+                             const float* W, float* dY, float* dW, float* dxp,
+                             const int64_t* rows, const int64_t* cols, int64_t nnz,
+                             int64_t node_count, int reserve_sms, void* stream) {
+  if (int rc = rows8_check(p, xp, Y, W, rows, cols, nnz, node_count)) return rc;
+  if (!aligned16(gp) || !aligned16(dY) || !aligned16(dW) || !aligned16(dxp))
+    return fail(OEQB_ERR_INVALID, "padded-row entry points need 16-byte aligned arrays");
+  if (nnz == 0) return 0;
+  DeviceGuard g(p->device);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  Args<float> a = base_args<float>(*p, false);
+  a.nitems = nnz;
+  a.nnodes = node_count;
+  a.Y = Y;
+  a.W = W;
+  a.out1 = dY;
+  a.out2 = dW;
+  a.rows = reinterpret_cast<const long long*>(rows);
+  a.cols = reinterpret_cast<const long long*>(cols);
+  return launch_edge1_pipe_main<float>(*p, 1, a, xp, gp, dxp, reserve_sms, s);
 }
 
 int oeqb_tp_forward_noalloc(const void* descriptor, size_t nbytes, int device, int64_t batch,

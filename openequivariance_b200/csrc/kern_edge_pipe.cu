@@ -4,16 +4,27 @@
 
 namespace oeqb {
 
-// kind 0 / 1: pipelined atomic forward / backward of the triple `code`; 4 / 5: deterministic
+// kind 0 / 1: pipelined atomic forward (two edges per lane) / backward of the triple `code`;
+// 4 / 5: deterministic forward / backward pass A; 6: deterministic backward pass B (by l1);
+// 4 / 5: deterministic
 // forward / backward pass A; 2 / 3: the row padding kernels.  nullptr for a triple without an
 // unrolled contraction.
 const void* edge1_pipe_kernel(int kind, int code) {
   if (kind == 2) return reinterpret_cast<const void*>(conv_pad_rows);
   if (kind == 3) return reinterpret_cast<const void*>(conv_unpad_rows);
+  if (kind == 6) {
+    switch ((code >> 8) & 15) {
+      case 0: return reinterpret_cast<const void*>(conv_bwd_edge1_gather_pipe<0>);
+      case 1: return reinterpret_cast<const void*>(conv_bwd_edge1_gather_pipe<1>);
+      case 2: return reinterpret_cast<const void*>(conv_bwd_edge1_gather_pipe<2>);
+      case 3: return reinterpret_cast<const void*>(conv_bwd_edge1_gather_pipe<3>);
+      default: return nullptr;
+    }
+  }
 #define OEQB_PIPE_CASE(A, B, C)                                                               \
   if (code == triple_code(A, B, C)) {                                                         \
     switch (kind) {                                                                           \
-      case 0: return reinterpret_cast<const void*>(conv_fwd_edge1_pipe<A, B, C>);             \
+      case 0: return reinterpret_cast<const void*>(conv_fwd_edge1_pipe2<A, B, C>);            \
       case 1: return reinterpret_cast<const void*>(conv_bwd_edge1_pipe<A, B, C, false>);      \
       case 4: return reinterpret_cast<const void*>(conv_fwd_edge1_det_pipe<A, B, C>);         \
       case 5: return reinterpret_cast<const void*>(conv_bwd_edge1_pipe<A, B, C, true>);       \

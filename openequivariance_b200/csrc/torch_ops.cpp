@@ -426,6 +426,70 @@ std::tuple<Tensor, Tensor, Tensor, Tensor> jit_conv_double_backward(
   return {L1_grad, L2_grad, W_grad, L3_dgrad};
 }
 
+// Padded-row convolution (this package's ops; the multi-GPU partition's layout).
+bool conv_rows8_ok(Tensor json_bytes, int64_t hash, int64_t device) {
+  const PlanInfo& k = get_plan(json_bytes, hash, static_cast<int>(device));
+  return oeqb_conv_rows8_ok(k.plan) != 0;
+}
+
+void check_rows8(const Tensor& t, int64_t rows, const char* name) {
+  TORCH_CHECK(t.is_cuda() && t.scalar_type() == at::kFloat && t.dim() == 2 && t.size(0) == rows &&
+                  t.size(1) == 8 && t.is_contiguous(),
+              "Tensor '", name, "' must be a contiguous float32 [", rows, ", 8] GPU tensor");
+}
+
+void conv_forward_rows8(Tensor json_bytes, int64_t hash, Tensor xp, Tensor Y, Tensor W, Tensor Z,
+                        Tensor rows, Tensor cols, bool accumulate, int64_t reserve_sms) {
+  const PlanInfo& k = get_plan(json_bytes, hash, tensor_device(xp));
+  const int64_t nodes = xp.size(0), nnz = rows.size(0);
+  check_rows8(xp, nodes, "xp");
+  check_tensor(Y, {nnz, k.L2_dim}, k.dtype, "L2_in");
+  check_weights(k, W, nnz, "W");
+  check_tensor(Z, {nodes, k.L3_dim}, k.dtype, "L3_out");
+  check_tensor(rows, {nnz}, at::kLong, "rows");
+  check_tensor(cols, {nnz}, at::kLong, "cols");
+  TORCH_CHECK(Y.is_contiguous() && W.is_contiguous() && Z.is_contiguous() && rows.is_contiguous() &&
+                  cols.is_contiguous(), "conv_forward_rows8: tensors must be contiguous");
+  c10::cuda::CUDAGuard guard(xp.device());
+  void* st = stream_of(xp);
+  const bool chk = checks_active(st);
+  if (chk) validate_graph(rows, cols, nullptr, nnz, nodes, false, st);
+  check_rc(oeqb_conv_forward_rows8(k.plan, xp.data_ptr<float>(), Y.data_ptr<float>(),
+                                   W.data_ptr<float>(), Z.data_ptr<float>(), rows.data_ptr<int64_t>(),
+                                   cols.data_ptr<int64_t>(), nnz, nodes, accumulate ? 1 : 0,
+                                   static_cast<int>(reserve_sms), st));
+  if (chk) check_status(k, st);
+}
+
+void conv_backward_rows8(Tensor json_bytes, int64_t hash, Tensor xp, Tensor gp, Tensor Y, Tensor W,
+                         Tensor dY, Tensor dW, Tensor dxp, Tensor rows, Tensor cols,
+                         int64_t reserve_sms) {
+  const PlanInfo& k = get_plan(json_bytes, hash, tensor_device(xp));
+  const int64_t nodes = xp.size(0), nnz = rows.size(0);
+  check_rows8(xp, nodes, "xp");
+  check_rows8(gp, nodes, "gp");
+  check_rows8(dxp, nodes, "dxp");
+  check_tensor(Y, {nnz, k.L2_dim}, k.dtype, "L2_in");
+  check_weights(k, W, nnz, "W");
+  check_tensor(dY, {nnz, k.L2_dim}, k.dtype, "L2_grad");
+  check_weights(k, dW, nnz, "W_grad");
+  check_tensor(rows, {nnz}, at::kLong, "rows");
+  check_tensor(cols, {nnz}, at::kLong, "cols");
+  TORCH_CHECK(Y.is_contiguous() && W.is_contiguous() && dY.is_contiguous() && dW.is_contiguous() &&
+                  rows.is_contiguous() && cols.is_contiguous(),
+              "conv_backward_rows8: tensors must be contiguous");
+  c10::cuda::CUDAGuard guard(xp.device());
+  void* st = stream_of(xp);
+  const bool chk = checks_active(st);
+  if (chk) validate_graph(rows, cols, nullptr, nnz, nodes, false, st);
+  check_rc(oeqb_conv_backward_rows8(k.plan, xp.data_ptr<float>(), gp.data_ptr<float>(),
+                                    Y.data_ptr<float>(), W.data_ptr<float>(), dY.data_ptr<float>(),
+                                    dW.data_ptr<float>(), dxp.data_ptr<float>(),
+                                    rows.data_ptr<int64_t>(), cols.data_ptr<int64_t>(), nnz, nodes,
+                                    static_cast<int>(reserve_sms), st));
+  if (chk) check_status(k, st);
+}
+
 // ----------------------------- symmetric contraction ----------------------------------
 
 int dtype_code(const Tensor& t) {
@@ -552,6 +616,9 @@ std::tuple<Tensor, Tensor> sc_backward(Tensor x, Tensor perm, Tensor elem_offset
 TORCH_LIBRARY(oeqb200, m) {
   m.def("set_device_checks(bool enabled) -> bool", &set_device_checks);
   m.def("check_device_status() -> ()", &check_device_status);
+  m.def("conv_rows8_ok(Tensor json_bytes, int hash, int device) -> bool", &conv_rows8_ok);
+  m.def("conv_forward_rows8(Tensor json_bytes, int hash, Tensor xp, Tensor Y, Tensor W, Tensor(a!) Z, Tensor rows, Tensor cols, bool accumulate, int reserve_sms) -> ()");
+  m.def("conv_backward_rows8(Tensor json_bytes, int hash, Tensor xp, Tensor gp, Tensor Y, Tensor W, Tensor(a!) dY, Tensor(b!) dW, Tensor(c!) dxp, Tensor rows, Tensor cols, int reserve_sms) -> ()");
   m.def("conv_backward_into(Tensor json_bytes, int hash, Tensor L1_in, Tensor L2_in, Tensor W, Tensor L3_grad, Tensor rows, Tensor cols, Tensor workspace, Tensor transpose_perm, Tensor(a!) L1_grad, Tensor(b!) L2_grad, Tensor(c!) W_grad) -> ()");
   m.def("sc_forward(Tensor x, Tensor perm, Tensor elem_offsets, Tensor coef, int[] out_col, int[] out_step, int out_dim, int degree) -> Tensor");
   m.def("sc_backward(Tensor x, Tensor perm, Tensor elem_offsets, Tensor coef, Tensor grad_out, int[] out_col, int[] out_step, int degree) -> (Tensor, Tensor)");
@@ -560,6 +627,8 @@ TORCH_LIBRARY(oeqb200, m) {
 TORCH_LIBRARY_IMPL(oeqb200, CUDA, m) {
   m.impl("sc_forward", &sc_forward);
   m.impl("conv_backward_into", &conv_backward_into);
+  m.impl("conv_forward_rows8", &conv_forward_rows8);
+  m.impl("conv_backward_rows8", &conv_backward_rows8);
   m.impl("sc_backward", &sc_backward);
 }
 

@@ -375,6 +375,231 @@ __global__ void __launch_bounds__(kEdgeWarps * 32) conv_bwd_edge1_pipe(const Arg
   }
 }
 
+// Atomic forward with two edges per lane: a warp takes 64 consecutive edges per step, lane l
+// edges 2l and 2l+1, which nearly always share a receiver.  The lane adds its two messages
+// when they do, so one segmented shuffle sum serves 64 edges (it is a third of the one-edge
+// kernel's instructions); where the pair straddles a receiver boundary the first message goes
+// to its receiver with its own vector reduction.  The stage ring, the padded X gathers one
+// step ahead and the tail handling are as in conv_fwd_edge1_pipe, with 64-edge stages.
+template <int D2>
+struct PipeStage2 {
+  long long rows[64];
+  long long cols[64];
+  float w[64];
+  float y[64 * D2];
+};
+
+template <int D2>
+__host__ __device__ constexpr size_t pipe2_warp_bytes() {
+  return sizeof(PipeStage2<D2>) * kPipeStages;
+}
+
+template <int D2>
+__device__ __forceinline__ void pipe2_stage_in(PipeStage2<D2>& st, const long long* rows,
+                                               const long long* cols, const float* W,
+                                               const float* Y, long long base, long long n,
+                                               int lane) {
+  if (base >= n) return;
+  if (base + 64 <= n) {
+    constexpr int kIdx = 64 * 8 / 16;
+    constexpr int kW = 64 * 4 / 16;
+    constexpr int kY = 64 * D2 * 4 / 16;
+    constexpr int kAll = 2 * kIdx + kW + kY;
+    const char* src_r = reinterpret_cast<const char*>(rows + base);
+    const char* src_c = reinterpret_cast<const char*>(cols + base);
+    const char* src_w = reinterpret_cast<const char*>(W + base);
+    const char* src_y = reinterpret_cast<const char*>(Y + base * D2);
+    char* dst = reinterpret_cast<char*>(&st);
+#pragma unroll
+    for (int q0 = 0; q0 < kAll; q0 += 32) {
+      const int q = q0 + lane;
+      if (q < kAll) {
+        const char* s;
+        if (q < kIdx)
+          s = src_r + 16 * q;
+        else if (q < 2 * kIdx)
+          s = src_c + 16 * (q - kIdx);
+        else if (q < 2 * kIdx + kW)
+          s = src_w + 16 * (q - 2 * kIdx);
+        else
+          s = src_y + 16 * (q - 2 * kIdx - kW);
+        cp_async16(dst + 16 * q, s);
+      }
+    }
+    return;
+  }
+  const int r = static_cast<int>(n - base);
+  for (int i = lane; i < 64; i += 32) {
+    st.rows[i] = i < r ? rows[base + i] : -1;
+    st.cols[i] = i < r ? cols[base + i] : 0;
+    st.w[i] = i < r ? W[base + i] : 0.f;
+  }
+  for (int i = lane; i < r * D2; i += 32) st.y[i] = Y[base * D2 + i];
+}
+
+template <int A, int B, int C>
+__global__ void __launch_bounds__(kEdgeWarps * 32) conv_fwd_edge1_pipe2(const Args<float> a, const Edge1 p,
+                                                                        const float* __restrict__ xp) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  const int lane = threadIdx.x & 31;
+  const long long nw = static_cast<long long>(gridDim.x) * kEdgeWarps;
+  const long long n = a.nitems;
+  const float pw = static_cast<float>(p.pw);
+  constexpr int D1 = 2 * A + 1, D2 = 2 * B + 1, D3 = 2 * C + 1;
+  auto* ring = reinterpret_cast<PipeStage2<D2>*>(smem + (threadIdx.x >> 5) * pipe2_warp_bytes<D2>());
+  const long long step = nw * 64;
+  long long base = (static_cast<long long>(blockIdx.x) * kEdgeWarps + (threadIdx.x >> 5)) * 64;
+  if (base >= n) return;
+  const int e0 = 2 * lane, e1 = 2 * lane + 1;
+  pipe2_stage_in<D2>(ring[0], a.rows, a.cols, a.W, a.Y, base, n, lane);
+  cp_async_commit();
+  pipe2_stage_in<D2>(ring[1], a.rows, a.cols, a.W, a.Y, base + step, n, lane);
+  cp_async_commit();
+  cp_async_wait<1>();
+  __syncwarp();
+  bool v0c = pipe_valid(ring[0].rows[e0], ring[0].cols[e0], a.nnodes, a.status);
+  bool v1c = pipe_valid(ring[0].rows[e1], ring[0].cols[e1], a.nnodes, a.status);
+  float x0c[D1], x1c[D1];
+  if (v0c) load_row8<D1>(x0c, xp, ring[0].cols[e0]); else zero_row(x0c);
+  if (v1c) load_row8<D1>(x1c, xp, ring[0].cols[e1]); else zero_row(x1c);
+  int s = 0;
+  for (; base < n; base += step) {
+    const int s1 = s == kPipeStages - 1 ? 0 : s + 1;
+    const int s2 = s1 == kPipeStages - 1 ? 0 : s1 + 1;
+    pipe2_stage_in<D2>(ring[s2], a.rows, a.cols, a.W, a.Y, base + 2 * step, n, lane);
+    cp_async_commit();
+    cp_async_wait<1>();
+    __syncwarp();
+    bool v0n = false, v1n = false;
+    if (base + step < n) {
+      v0n = pipe_valid(ring[s1].rows[e0], ring[s1].cols[e0], a.nnodes, a.status);
+      v1n = pipe_valid(ring[s1].rows[e1], ring[s1].cols[e1], a.nnodes, a.status);
+    }
+    float x0n[D1], x1n[D1];
+    if (v0n) load_row8<D1>(x0n, xp, ring[s1].cols[e0]); else zero_row(x0n);
+    if (v1n) load_row8<D1>(x1n, xp, ring[s1].cols[e1]); else zero_row(x1n);
+    const PipeStage2<D2>& st = ring[s];
+    const long long r0 = v0c ? st.rows[e0] : -1, r1 = v1c ? st.rows[e1] : -1;
+    float z0[D3], z1[D3];
+#pragma unroll
+    for (int k = 0; k < D3; ++k) z0[k] = z1[k] = 0.f;
+    if (v0c) {
+      float x[D1], y[D2];
+      const float w = st.w[e0] * pw;
+#pragma unroll
+      for (int i = 0; i < D1; ++i) x[i] = x0c[i] * w;
+#pragma unroll
+      for (int j = 0; j < D2; ++j) y[j] = st.y[e0 * D2 + j];
+      CG<A, B, C>::fwd(x, y, z0);
+    }
+    if (v1c) {
+      float x[D1], y[D2];
+      const float w = st.w[e1] * pw;
+#pragma unroll
+      for (int i = 0; i < D1; ++i) x[i] = x1c[i] * w;
+#pragma unroll
+      for (int j = 0; j < D2; ++j) y[j] = st.y[e1 * D2 + j];
+      CG<A, B, C>::fwd(x, y, z1);
+    }
+    // The pair shares a receiver: one message.  Otherwise the first edge ends its receiver's
+    // run inside this lane and is reduced on its own.
+    if (r0 >= 0 && r0 == r1) {
+#pragma unroll
+      for (int k = 0; k < D3; ++k) z1[k] += z0[k];
+    } else if (r0 >= 0) {
+      red_vec(a.out0 + r0 * D3, z0);
+    }
+    const int k32 = static_cast<int>(r1);
+    const int prev = __shfl_up_sync(0xffffffffu, k32, 1);
+    const bool head = r1 >= 0 && (lane == 0 || prev != k32);
+    e1_seg_sum<float, D3>(z1, k32, lane);
+    if (head) red_vec(a.out0 + r1 * D3, z1);
+    __syncwarp();
+#pragma unroll
+    for (int i = 0; i < D1; ++i) {
+      x0c[i] = x0n[i];
+      x1c[i] = x1n[i];
+    }
+    v0c = v0n;
+    v1c = v1n;
+    s = s1;
+  }
+  cp_async_wait<0>();
+}
+
+// Deterministic backward pass B, pipelined: as conv_bwd_edge1_gather (warp ranges of whole
+// senders in transpose_perm order, runs of equal senders summed with carries across 32-edge
+// blocks, one plain store per dX row), but the transpose_perm entries are loaded two blocks
+// ahead and the 32-byte records one block ahead, so the chain perm -> record is never waited
+// on inside a block, and the next block's first sender (whether the last run continues)
+// comes from the records already in registers.
+struct PipeRec {
+  float4 u, v;
+};
+
+__device__ __forceinline__ PipeRec load_rec(const float* ws, long long e, bool ok) {
+  PipeRec r;
+  if (ok) {
+    r.u = __ldg(reinterpret_cast<const float4*>(ws + e * kE1Rec));
+    r.v = __ldg(reinterpret_cast<const float4*>(ws + e * kE1Rec) + 1);
+  } else {
+    r.u = make_float4(0.f, 0.f, 0.f, 0.f);
+    r.v = make_float4(0.f, 0.f, 0.f, __int_as_float(-1));
+  }
+  return r;
+}
+
+template <int A>
+__global__ void __launch_bounds__(kEdgeWarps * 32) conv_bwd_edge1_gather_pipe(const Args<float> a,
+                                                                              const Edge1 p,
+                                                                              const float* __restrict__ ws) {
+  (void)p;
+  constexpr int D1 = 2 * A + 1;
+  const int lane = threadIdx.x & 31;
+  const long long nwarps = static_cast<long long>(gridDim.x) * kEdgeWarps;
+  const long long wg = static_cast<long long>(blockIdx.x) * kEdgeWarps + (threadIdx.x >> 5);
+  const long long n = a.nitems;
+  auto sender = [&](long long t) -> long long {
+    const long long e = a.perm[t];
+    if (e < 0 || e >= n) return -1;
+    return __float_as_int(ws[e * kE1Rec + kE1Rec - 1]);
+  };
+  const long long p0 = e1_snap(static_cast<long long>((static_cast<__int128>(n) * wg) / nwarps), n, sender, lane);
+  const long long p1 = e1_snap(static_cast<long long>((static_cast<__int128>(n) * (wg + 1)) / nwarps), n, sender, lane);
+  if (p0 >= p1) return;
+  // Edge of position t, or -1 (past the range, or a bad permutation entry: status 2).
+  auto edge_at = [&](long long t) -> long long {
+    if (t >= p1) return -1;
+    const long long e = a.perm[t];
+    if (e < 0 || e >= n) {
+      flag(a.status, 2);
+      return -1;
+    }
+    return e;
+  };
+  long long base = p0;
+  long long e_c = edge_at(base + lane);
+  long long e_n = edge_at(base + 32 + lane);
+  PipeRec rc = load_rec(ws, e_c, e_c >= 0);
+  float carry[D1];
+  long long carry_key = -2;
+  for (; base < p1; base += 32) {
+    const long long e_nn = edge_at(base + 64 + lane);  // two blocks ahead
+    PipeRec rn = load_rec(ws, e_n, e_n >= 0);           // one block ahead
+    float rec[8] = {rc.u.x, rc.u.y, rc.u.z, rc.u.w, rc.v.x, rc.v.y, rc.v.z, rc.v.w};
+    float h[D1];
+#pragma unroll
+    for (int i = 0; i < D1; ++i) h[i] = rec[i];
+    const long long key = e_c >= 0 ? __float_as_int(rec[kE1Rec - 1]) : -1;
+    const bool more = base + 32 < p1;
+    const long long nk = more ? __shfl_sync(0xffffffffu, static_cast<long long>(__float_as_int(rn.v.w)), 0) : -3;
+    e1_seg_block<float, D1>(h, key < 0 ? -1 : key, nk, more, carry, carry_key, a.out0, lane);
+    rc = rn;
+    e_c = e_n;
+    e_n = e_nn;
+  }
+}
+
 // Deterministic forward (same mapping as conv_fwd_edge1_det): warp w owns the edges of whole
 // receivers, its nominal range [w E / W, (w+1) E / W) moved forward to receiver boundaries,
 // and walks it in consecutive 32-edge blocks starting at the 4-aligned edge at or below the

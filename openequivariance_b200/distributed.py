@@ -258,6 +258,73 @@ class _HaloConvFn(torch.autograd.Function):
         return gX, gY, gW, None
 
 
+class _HaloConvRows8Fn(torch.autograd.Function):
+    """The atomic pass on node arrays in the kernels' padded-row layout (``[nodes, 8]``,
+    ``oeqb_conv_forward_rows8`` / ``oeqb_conv_backward_rows8``): halo rows arrive from the
+    other ranks straight into the padded X buffer, the boundary forward adds into the interior
+    result, and the boundary backward's dX rows leave straight from the padded accumulator, so
+    a step issues about half the operations of the unpadded path."""
+
+    @staticmethod
+    def forward(ctx, X_own, Y, W, pc):
+        part = pc.part
+        n_own, n_loc, ni = part.n_own, part.n_local_nodes, part.n_interior
+        conv = pc.conv
+        ops = torch.ops.oeqb200
+        d1 = X_own.shape[1]
+        xp = X_own.new_empty(n_loc, 8)
+        xp[:n_own, :d1].copy_(X_own)
+        work = None
+        if part.world > 1:
+            send = xp.index_select(0, part.send_idx)
+            work = dist.all_to_all_single(xp[n_own:], send, part.recv_counts, part.send_counts,
+                                          group=pc.group, async_op=True)
+        Z = X_own.new_empty(n_loc, conv.L3_dim)
+        ops.conv_forward_rows8(conv.kernel, conv.hash, xp, Y[:ni], W[:ni], Z, part.rows_int,
+                               part.cols_int, False, pc.reserve_sms if work is not None else 0)
+        if work is not None:
+            work.wait()
+        if part.n_boundary:
+            ops.conv_forward_rows8(conv.kernel, conv.hash, xp, Y[ni:], W[ni:], Z, part.rows_bnd,
+                                   part.cols_bnd, True, 0)
+        ctx.save_for_backward(xp, Y, W)
+        ctx.pc = pc
+        ctx.d1 = d1
+        return Z[:n_own]
+
+    @staticmethod
+    def backward(ctx, gZ):
+        if torch.is_grad_enabled():
+            raise RuntimeError("double backward through PartitionedConv is not supported")
+        xp, Y, W = ctx.saved_tensors
+        pc = ctx.pc
+        part = pc.part
+        conv = pc.conv
+        ops = torch.ops.oeqb200
+        n_own, n_loc, ni = part.n_own, part.n_local_nodes, part.n_interior
+        gp = xp.new_empty(n_loc, 8)  # only the receivers' (owned) rows are read
+        gp[:n_own, :gZ.shape[1]].copy_(gZ)
+        dxp = xp.new_zeros(n_loc, 8)
+        gY = torch.empty_like(Y)
+        gW = torch.empty_like(W)
+        work, back = None, None
+        if part.n_boundary:
+            ops.conv_backward_rows8(conv.kernel, conv.hash, xp, gp, Y[ni:], W[ni:], gY[ni:],
+                                    gW[ni:], dxp, part.rows_bnd, part.cols_bnd, 0)
+        if part.world > 1:
+            back = xp.new_empty(int(part.send_idx.numel()), 8)
+            work = dist.all_to_all_single(back, dxp[n_own:], part.send_counts, part.recv_counts,
+                                          group=pc.group, async_op=True)
+        ops.conv_backward_rows8(conv.kernel, conv.hash, xp, gp, Y[:ni], W[:ni], gY[:ni], gW[:ni],
+                                dxp, part.rows_int, part.cols_int,
+                                pc.reserve_sms if work is not None else 0)
+        if work is not None:
+            work.wait()
+            if back.shape[0]:
+                dxp.index_add_(0, part.send_idx, back)
+        return dxp[:n_own, :ctx.d1].contiguous(), gY, gW, None
+
+
 class PartitionedConv(torch.nn.Module):
     """Fused convolution of a receiver-partitioned graph (one rank per GPU).
 
@@ -276,16 +343,40 @@ class PartitionedConv(torch.nn.Module):
 
     def __init__(self, conv, part: ReceiverPartition, group=None,
                  local_ops: Optional[tuple[Callable, Callable]] = None,
-                 shared_weights: Optional[bool] = None, deterministic: Optional[bool] = None):
+                 shared_weights: Optional[bool] = None, deterministic: Optional[bool] = None,
+                 reserve_sms: int = 16):
         super().__init__()
         self.conv = conv
         self.part = part
         self.group = group
+        self._default_ops = local_ops is None
         self.fwd, self.bwd = local_ops if local_ops is not None else _local_conv_ops(conv)
         self.shared_weights = (bool(conv.config.shared_weights) if shared_weights is None
                                else shared_weights)
         self.deterministic = (bool(conv.deterministic) if deterministic is None
                               else deterministic)
+        # SMs the interior kernels leave free while an exchange is in flight, so that the
+        # collective's kernel runs beside them instead of after them.
+        self.reserve_sms = reserve_sms
+        self._rows8 = None
+
+    def _use_rows8(self, X_own):
+        """The padded-row path: atomic plans of the single-path class, on the GPU."""
+        if self._rows8 is None:
+            ok = (local_ops_default(self) and not self.deterministic and X_own.is_cuda
+                  and X_own.dtype == torch.float32)
+            if ok:
+                ok = bool(torch.ops.oeqb200.conv_rows8_ok(self.conv.kernel, self.conv.hash,
+                                                          X_own.device.index))
+            self._rows8 = ok
+        return self._rows8
 
     def forward(self, X_own, Y_local, W_local):
+        if self._use_rows8(X_own) and Y_local.is_contiguous() and W_local.is_contiguous():
+            return _HaloConvRows8Fn.apply(X_own, Y_local, W_local, self)
         return _HaloConvFn.apply(X_own, Y_local, W_local, self)
+
+
+def local_ops_default(pc) -> bool:
+    """True when ``pc`` runs this package's kernels (no ``local_ops`` replacement)."""
+    return pc._default_ops
