@@ -149,16 +149,17 @@ int oeqb_conv_double_backward(oeqb_plan* plan, const void* L1_in, const void* L2
  *             (accumulate != 0);
  *   backward: dY, dW written; dX contributions added into the padded accumulator dxp (the
  *             caller clears it).
- * reserve_sms leaves that many SMs without CTAs of the launch, for work that runs beside it
- * (e.g. a collective).  All arrays 16-byte aligned. */
+ * sm_budget bounds the SMs the launch puts CTAs on: 0 = all, > 0 = at most that many, < 0 =
+ * all but that many (for work that runs beside it, e.g. a collective or the other edge block
+ * on another stream).  All arrays 16-byte aligned. */
 int oeqb_conv_rows8_ok(const oeqb_plan* plan);
 int oeqb_conv_forward_rows8(oeqb_plan* plan, const float* xp, const float* Y, const float* W,
                             float* Z, const int64_t* rows, const int64_t* cols, int64_t nnz,
-                            int64_t node_count, int accumulate, int reserve_sms, void* stream);
+                            int64_t node_count, int accumulate, int sm_budget, void* stream);
 int oeqb_conv_backward_rows8(oeqb_plan* plan, const float* xp, const float* gp, const float* Y,
                              const float* W, float* dY, float* dW, float* dxp,
                              const int64_t* rows, const int64_t* cols, int64_t nnz,
-                             int64_t node_count, int reserve_sms, void* stream);
+                             int64_t node_count, int sm_budget, void* stream);
 
 /* ---- MACE symmetric contraction (replaces the group_gemm + torch pipeline of
  * _torch/symmetric_contraction/SymmetricContraction.py:124-336 and extension/group_mm.hpp) ----

@@ -1455,11 +1455,12 @@ int launch_unpad(const oeqb_plan& p, const float* src, float* dst, int d, long l
 // deterministic (pass A writes the per-edge records, pass B, conv_bwd_edge1_gather, sums them
 // per sender).
 // Main kernel of the pipelined single-path pass `kind` on node arrays already in the padded
-// layout (xp, gp, and out = the padded dX accumulator or the records).  reserve_sms SMs are
-// left without CTAs of this launch (so that, e.g., a collective running beside it gets SMs).
+// layout (xp, gp, and out = the padded dX accumulator or the records).  sm_budget: 0 = CTAs
+// for every SM, > 0 = for at most that many SMs, < 0 = for all but that many (so that work
+// running beside the launch, e.g. a collective or another kernel, finds SMs free).
 template <class T>
 int launch_edge1_pipe_main(oeqb_plan& p, int kind, const Args<T>& a, const float* xp,
-                           const float* gp, float* out, int reserve_sms, cudaStream_t stream) {
+                           const float* gp, float* out, int sm_budget, cudaStream_t stream) {
   const bool bwd = kind == 1 || kind == 5;
   const void* kernel = edge1_pipe_kernel(kind, p.edge1.code);
   if (!kernel) return fail(OEQB_ERR_UNSUPPORTED, "no pipelined kernel for this degree triple");
@@ -1482,7 +1483,8 @@ int launch_edge1_pipe_main(oeqb_plan& p, int kind, const Args<T>& a, const float
     }
     per_sm = it->second;
   }
-  const int sms = std::max(1, p.sm_count - std::max(0, reserve_sms));
+  const int sms = sm_budget > 0 ? std::min(sm_budget, p.sm_count)
+                                 : std::max(1, p.sm_count + std::min(0, sm_budget));
   const long long cap = (long long)sms * per_sm;
   const long long warps = (a.nitems + epw - 1) / epw;
   const long long blocks =
@@ -2052,7 +2054,7 @@ int rows8_check(const oeqb_plan* p, const void* xp, const float* Y, const float*
 
 int oeqb_conv_forward_rows8(oeqb_plan* p, const float* xp, const float* Y, const float* W,
                             float* Z, const int64_t* rows, const int64_t* cols, int64_t nnz,
-                            int64_t node_count, int accumulate, int reserve_sms, void* stream) {
+                            int64_t node_count, int accumulate, int sm_budget, void* stream) {
   if (int rc = rows8_check(p, xp, Y, W, rows, cols, nnz, node_count)) return rc;
   DeviceGuard g(p->device);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
@@ -2066,13 +2068,13 @@ int oeqb_conv_forward_rows8(oeqb_plan* p, const float* xp, const float* Y, const
   a.out0 = Z;
   a.rows = reinterpret_cast<const long long*>(rows);
   a.cols = reinterpret_cast<const long long*>(cols);
-  return launch_edge1_pipe_main<float>(*p, 0, a, xp, nullptr, nullptr, reserve_sms, s);
+  return launch_edge1_pipe_main<float>(*p, 0, a, xp, nullptr, nullptr, sm_budget, s);
 }
 
 int oeqb_conv_backward_rows8(oeqb_plan* p, const float* xp, const float* gp, const float* Y,
                              const float* W, float* dY, float* dW, float* dxp,
                              const int64_t* rows, const int64_t* cols, int64_t nnz,
-                             int64_t node_count, int reserve_sms, void* stream) {
+                             int64_t node_count, int sm_budget, void* stream) {
   if (int rc = rows8_check(p, xp, Y, W, rows, cols, nnz, node_count)) return rc;
   if (!aligned16(gp) || !aligned16(dY) || !aligned16(dW) || !aligned16(dxp))
     return fail(OEQB_ERR_INVALID, "padded-row entry points need 16-byte aligned arrays");
@@ -2088,7 +2090,7 @@ int oeqb_conv_backward_rows8(oeqb_plan* p, const float* xp, const float* gp, con
   a.out2 = dW;
   a.rows = reinterpret_cast<const long long*>(rows);
   a.cols = reinterpret_cast<const long long*>(cols);
-  return launch_edge1_pipe_main<float>(*p, 1, a, xp, gp, dxp, reserve_sms, s);
+  return launch_edge1_pipe_main<float>(*p, 1, a, xp, gp, dxp, sm_budget, s);
 }
 
 int oeqb_tp_forward_noalloc(const void* descriptor, size_t nbytes, int device, int64_t batch,

@@ -439,7 +439,7 @@ void check_rows8(const Tensor& t, int64_t rows, const char* name) {
 }
 
 void conv_forward_rows8(Tensor json_bytes, int64_t hash, Tensor xp, Tensor Y, Tensor W, Tensor Z,
-                        Tensor rows, Tensor cols, bool accumulate, int64_t reserve_sms) {
+                        Tensor rows, Tensor cols, bool accumulate, int64_t sm_budget) {
   const PlanInfo& k = get_plan(json_bytes, hash, tensor_device(xp));
   const int64_t nodes = xp.size(0), nnz = rows.size(0);
   check_rows8(xp, nodes, "xp");
@@ -457,13 +457,13 @@ void conv_forward_rows8(Tensor json_bytes, int64_t hash, Tensor xp, Tensor Y, Te
   check_rc(oeqb_conv_forward_rows8(k.plan, xp.data_ptr<float>(), Y.data_ptr<float>(),
                                    W.data_ptr<float>(), Z.data_ptr<float>(), rows.data_ptr<int64_t>(),
                                    cols.data_ptr<int64_t>(), nnz, nodes, accumulate ? 1 : 0,
-                                   static_cast<int>(reserve_sms), st));
+                                   static_cast<int>(sm_budget), st));
   if (chk) check_status(k, st);
 }
 
 void conv_backward_rows8(Tensor json_bytes, int64_t hash, Tensor xp, Tensor gp, Tensor Y, Tensor W,
                          Tensor dY, Tensor dW, Tensor dxp, Tensor rows, Tensor cols,
-                         int64_t reserve_sms) {
+                         int64_t sm_budget) {
   const PlanInfo& k = get_plan(json_bytes, hash, tensor_device(xp));
   const int64_t nodes = xp.size(0), nnz = rows.size(0);
   check_rows8(xp, nodes, "xp");
@@ -486,7 +486,7 @@ void conv_backward_rows8(Tensor json_bytes, int64_t hash, Tensor xp, Tensor gp, 
                                     Y.data_ptr<float>(), W.data_ptr<float>(), dY.data_ptr<float>(),
                                     dW.data_ptr<float>(), dxp.data_ptr<float>(),
                                     rows.data_ptr<int64_t>(), cols.data_ptr<int64_t>(), nnz, nodes,
-                                    static_cast<int>(reserve_sms), st));
+                                    static_cast<int>(sm_budget), st));
   if (chk) check_status(k, st);
 }
 
@@ -617,8 +617,8 @@ TORCH_LIBRARY(oeqb200, m) {
   m.def("set_device_checks(bool enabled) -> bool", &set_device_checks);
   m.def("check_device_status() -> ()", &check_device_status);
   m.def("conv_rows8_ok(Tensor json_bytes, int hash, int device) -> bool", &conv_rows8_ok);
-  m.def("conv_forward_rows8(Tensor json_bytes, int hash, Tensor xp, Tensor Y, Tensor W, Tensor(a!) Z, Tensor rows, Tensor cols, bool accumulate, int reserve_sms) -> ()");
-  m.def("conv_backward_rows8(Tensor json_bytes, int hash, Tensor xp, Tensor gp, Tensor Y, Tensor W, Tensor(a!) dY, Tensor(b!) dW, Tensor(c!) dxp, Tensor rows, Tensor cols, int reserve_sms) -> ()");
+  m.def("conv_forward_rows8(Tensor json_bytes, int hash, Tensor xp, Tensor Y, Tensor W, Tensor(a!) Z, Tensor rows, Tensor cols, bool accumulate, int sm_budget) -> ()");
+  m.def("conv_backward_rows8(Tensor json_bytes, int hash, Tensor xp, Tensor gp, Tensor Y, Tensor W, Tensor(a!) dY, Tensor(b!) dW, Tensor(c!) dxp, Tensor rows, Tensor cols, int sm_budget) -> ()");
   m.def("conv_backward_into(Tensor json_bytes, int hash, Tensor L1_in, Tensor L2_in, Tensor W, Tensor L3_grad, Tensor rows, Tensor cols, Tensor workspace, Tensor transpose_perm, Tensor(a!) L1_grad, Tensor(b!) L2_grad, Tensor(c!) W_grad) -> ()");
   m.def("sc_forward(Tensor x, Tensor perm, Tensor elem_offsets, Tensor coef, int[] out_col, int[] out_step, int out_dim, int degree) -> Tensor");
   m.def("sc_backward(Tensor x, Tensor perm, Tensor elem_offsets, Tensor coef, Tensor grad_out, int[] out_col, int[] out_step, int degree) -> (Tensor, Tensor)");

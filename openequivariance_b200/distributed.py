@@ -260,10 +260,15 @@ class _HaloConvFn(torch.autograd.Function):
 
 class _HaloConvRows8Fn(torch.autograd.Function):
     """The atomic pass on node arrays in the kernels' padded-row layout (``[nodes, 8]``,
-    ``oeqb_conv_forward_rows8`` / ``oeqb_conv_backward_rows8``): halo rows arrive from the
-    other ranks straight into the padded X buffer, the boundary forward adds into the interior
-    result, and the boundary backward's dX rows leave straight from the padded accumulator, so
-    a step issues about half the operations of the unpadded path."""
+    ``oeqb_conv_forward_rows8`` / ``oeqb_conv_backward_rows8``).
+
+    Halo rows arrive from the other ranks straight into the padded X buffer, and the boundary
+    backward's dX rows leave straight from the padded accumulator.  With more than one rank
+    the boundary block runs on a side stream, on the ``reserve_sms`` SMs the interior kernel
+    leaves free, in order with the exchange: forward = exchange, then boundary edges (adding
+    into Z) beside the interior edges; backward = boundary edges, then exchange, beside the
+    interior edges.  Both blocks add into Z / the dX accumulator with vector reductions, so
+    running them at the same time is fine in this (atomic) mode."""
 
     @staticmethod
     def forward(ctx, X_own, Y, W, pc):
@@ -272,21 +277,30 @@ class _HaloConvRows8Fn(torch.autograd.Function):
         conv = pc.conv
         ops = torch.ops.oeqb200
         d1 = X_own.shape[1]
+        cur = torch.cuda.current_stream(X_own.device)
         xp = X_own.new_empty(n_loc, 8)
         xp[:n_own, :d1].copy_(X_own)
-        work = None
-        if part.world > 1:
+        Z = X_own.new_zeros(n_loc, conv.L3_dim)
+        if part.world == 1:
+            ops.conv_forward_rows8(conv.kernel, conv.hash, xp, Y[:ni], W[:ni], Z, part.rows_int,
+                                   part.cols_int, True, 0)
+        else:
+            R = pc.reserve_sms
             send = xp.index_select(0, part.send_idx)
-            work = dist.all_to_all_single(xp[n_own:], send, part.recv_counts, part.send_counts,
-                                          group=pc.group, async_op=True)
-        Z = X_own.new_empty(n_loc, conv.L3_dim)
-        ops.conv_forward_rows8(conv.kernel, conv.hash, xp, Y[:ni], W[:ni], Z, part.rows_int,
-                               part.cols_int, False, pc.reserve_sms if work is not None else 0)
-        if work is not None:
-            work.wait()
-        if part.n_boundary:
-            ops.conv_forward_rows8(conv.kernel, conv.hash, xp, Y[ni:], W[ni:], Z, part.rows_bnd,
-                                   part.cols_bnd, True, 0)
+            side = pc.side_stream(X_own.device)
+            side.wait_stream(cur)
+            with torch.cuda.stream(side):
+                work = dist.all_to_all_single(xp[n_own:], send, part.recv_counts,
+                                              part.send_counts, group=pc.group, async_op=True)
+                work.wait()
+                if part.n_boundary:
+                    ops.conv_forward_rows8(conv.kernel, conv.hash, xp, Y[ni:], W[ni:], Z,
+                                           part.rows_bnd, part.cols_bnd, True, R)
+            ops.conv_forward_rows8(conv.kernel, conv.hash, xp, Y[:ni], W[:ni], Z, part.rows_int,
+                                   part.cols_int, True, -R)
+            cur.wait_stream(side)
+            for t in (xp, send, Z, Y, W):
+                t.record_stream(side)
         ctx.save_for_backward(xp, Y, W)
         ctx.pc = pc
         ctx.d1 = d1
@@ -302,24 +316,32 @@ class _HaloConvRows8Fn(torch.autograd.Function):
         conv = pc.conv
         ops = torch.ops.oeqb200
         n_own, n_loc, ni = part.n_own, part.n_local_nodes, part.n_interior
+        cur = torch.cuda.current_stream(xp.device)
         gp = xp.new_empty(n_loc, 8)  # only the receivers' (owned) rows are read
         gp[:n_own, :gZ.shape[1]].copy_(gZ)
         dxp = xp.new_zeros(n_loc, 8)
         gY = torch.empty_like(Y)
         gW = torch.empty_like(W)
-        work, back = None, None
-        if part.n_boundary:
-            ops.conv_backward_rows8(conv.kernel, conv.hash, xp, gp, Y[ni:], W[ni:], gY[ni:],
-                                    gW[ni:], dxp, part.rows_bnd, part.cols_bnd, 0)
-        if part.world > 1:
+        if part.world == 1:
+            ops.conv_backward_rows8(conv.kernel, conv.hash, xp, gp, Y[:ni], W[:ni], gY[:ni],
+                                    gW[:ni], dxp, part.rows_int, part.cols_int, 0)
+        else:
+            R = pc.reserve_sms
             back = xp.new_empty(int(part.send_idx.numel()), 8)
-            work = dist.all_to_all_single(back, dxp[n_own:], part.send_counts, part.recv_counts,
-                                          group=pc.group, async_op=True)
-        ops.conv_backward_rows8(conv.kernel, conv.hash, xp, gp, Y[:ni], W[:ni], gY[:ni], gW[:ni],
-                                dxp, part.rows_int, part.cols_int,
-                                pc.reserve_sms if work is not None else 0)
-        if work is not None:
-            work.wait()
+            side = pc.side_stream(xp.device)
+            side.wait_stream(cur)
+            with torch.cuda.stream(side):
+                if part.n_boundary:
+                    ops.conv_backward_rows8(conv.kernel, conv.hash, xp, gp, Y[ni:], W[ni:],
+                                            gY[ni:], gW[ni:], dxp, part.rows_bnd, part.cols_bnd, R)
+                work = dist.all_to_all_single(back, dxp[n_own:], part.send_counts,
+                                              part.recv_counts, group=pc.group, async_op=True)
+                work.wait()
+            ops.conv_backward_rows8(conv.kernel, conv.hash, xp, gp, Y[:ni], W[:ni], gY[:ni],
+                                    gW[:ni], dxp, part.rows_int, part.cols_int, -R)
+            cur.wait_stream(side)
+            for t in (xp, gp, dxp, back, gY, gW, Y, W):
+                t.record_stream(side)
             if back.shape[0]:
                 dxp.index_add_(0, part.send_idx, back)
         return dxp[:n_own, :ctx.d1].contiguous(), gY, gW, None
@@ -355,10 +377,18 @@ class PartitionedConv(torch.nn.Module):
                                else shared_weights)
         self.deterministic = (bool(conv.deterministic) if deterministic is None
                               else deterministic)
-        # SMs the interior kernels leave free while an exchange is in flight, so that the
-        # collective's kernel runs beside them instead of after them.
+        # SMs the interior kernels leave free for the exchange and the boundary block, which
+        # run beside them on a side stream (padded-row path, more than one rank).
         self.reserve_sms = reserve_sms
         self._rows8 = None
+        self._side = {}
+
+    def side_stream(self, device):
+        """This module's second stream on `device` (the boundary block and the exchange)."""
+        key = device.index
+        if key not in self._side:
+            self._side[key] = torch.cuda.Stream(device)
+        return self._side[key]
 
     def _use_rows8(self, X_own):
         """The padded-row path: atomic plans of the single-path class, on the GPU."""

@@ -52,10 +52,11 @@ def test_rows8_blocks_match_module(cuda_device):
     gp = torch.zeros(n, 8, device="cuda")
     gp[:, :5] = G
     Z = torch.empty(n, 5, device="cuda")
+    # sm_budget: -16 = all SMs but 16, 8 = at most 8 SMs, 0 = all.
     ops.conv_forward_rows8(conv.kernel, conv.hash, xp, Y[:cut], W[:cut], Z, rows[:cut].contiguous(),
-                           cols[:cut].contiguous(), False, 8)
+                           cols[:cut].contiguous(), False, -16)
     ops.conv_forward_rows8(conv.kernel, conv.hash, xp, Y[cut:], W[cut:], Z, rows[cut:].contiguous(),
-                           cols[cut:].contiguous(), True, 0)
+                           cols[cut:].contiguous(), True, 8)
     x, y, w = (t.clone().requires_grad_() for t in (X, Y, W))
     z = conv(x, y, w, rows, cols)
     z.backward(G)
@@ -63,9 +64,9 @@ def test_rows8_blocks_match_module(cuda_device):
     dY, dW = torch.empty_like(Y), torch.empty_like(W)
     dxp = torch.zeros(n, 8, device="cuda")
     ops.conv_backward_rows8(conv.kernel, conv.hash, xp, gp, Y[cut:], W[cut:], dY[cut:], dW[cut:],
-                            dxp, rows[cut:].contiguous(), cols[cut:].contiguous(), 0)
+                            dxp, rows[cut:].contiguous(), cols[cut:].contiguous(), 8)
     ops.conv_backward_rows8(conv.kernel, conv.hash, xp, gp, Y[:cut], W[:cut], dY[:cut], dW[:cut],
-                            dxp, rows[:cut].contiguous(), cols[:cut].contiguous(), 8)
+                            dxp, rows[:cut].contiguous(), cols[:cut].contiguous(), -16)
     assert _nerr(dxp[:, :5], x.grad) <= 1e-5
     assert _nerr(dY, y.grad) <= 1e-5
     assert _nerr(dW, w.grad) <= 1e-5
