@@ -200,8 +200,12 @@ def _dist():
         import torch.distributed as dist
 
         torch.cuda.set_device(local)
+        # High-priority NCCL streams: the halo exchange's kernel is scheduled ahead of the
+        # interior conv kernel that becomes ready at the same time.
+        opts = dist.ProcessGroupNCCL.Options()
+        opts.is_high_priority_stream = True
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
-                                device_id=torch.device("cuda", local))
+                                device_id=torch.device("cuda", local), pg_options=opts)
     else:
         if torch.cuda.is_available():
             torch.cuda.set_device(local)

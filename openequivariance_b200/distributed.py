@@ -384,10 +384,13 @@ class PartitionedConv(torch.nn.Module):
         self._side = {}
 
     def side_stream(self, device):
-        """This module's second stream on `device` (the boundary block and the exchange)."""
+        """This module's second stream on `device` (the boundary block and the exchange), of
+        high priority: when its kernels and the interior kernel become ready together, the
+        block scheduler places its CTAs first.  (Give NCCL high-priority streams too,
+        ``ProcessGroupNCCL.Options(is_high_priority_stream=True)``, for the same reason.)"""
         key = device.index
         if key not in self._side:
-            self._side[key] = torch.cuda.Stream(device)
+            self._side[key] = torch.cuda.Stream(device, priority=-1)
         return self._side[key]
 
     def _use_rows8(self, X_own):
