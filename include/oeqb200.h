@@ -66,10 +66,13 @@ int oeqb_plan_destroy(oeqb_plan* plan);
 /* Bytes of workspace oeqb_conv_forward / oeqb_conv_backward use for `nnz` edges and
  * `node_count` nodes (replaces the reference's workspace sizing,
  * core/LoopUnrollConv.py:138-170).  Nonzero only for single-path multiplicity-1 problems
- * (BASELINE C3's class): deterministic plans keep one 8-value record per edge in the
- * backward; float32 atomic plans with one weight per edge keep X, dZ and the dX accumulator in
- * 32-byte rows (3 x 32 x node_count bytes + 256).  With a smaller (or not 16-byte aligned)
- * workspace those plans run slower kernels that need none.  The double backward needs none. */
+ * (BASELINE C3's class).  Float32 plans with one weight per edge keep X and dZ in 32-byte
+ * rows, then the dX accumulator (atomic: 3 x 32 x node_count bytes + 256) or one 32-byte
+ * record per edge and 64 bytes per 32 edges for the backward's per-block sums (deterministic:
+ * 2 x 32 x node_count + 32 x nnz + 64 x ceil(nnz / 32) + 256); other deterministic plans keep
+ * one 8-value record per edge.  With a smaller (or, for the float32 kernels, not 32-byte
+ * aligned) workspace those plans run slower kernels that need none.  The double backward
+ * needs none. */
 size_t oeqb_conv_workspace_bytes(const oeqb_plan* plan, int64_t nnz, int64_t node_count);
 
 /* Synchronises `stream` and reports (then clears) the plan's device error flag:
@@ -151,7 +154,8 @@ int oeqb_conv_double_backward(oeqb_plan* plan, const void* L1_in, const void* L2
  *             caller clears it).
  * sm_budget bounds the SMs the launch puts CTAs on: 0 = all, > 0 = at most that many, < 0 =
  * all but that many (for work that runs beside it, e.g. a collective or the other edge block
- * on another stream).  All arrays 16-byte aligned. */
+ * on another stream).  The padded arrays (xp, gp, dxp) 32-byte aligned, the others 16-byte
+ * aligned. */
 int oeqb_conv_rows8_ok(const oeqb_plan* plan);
 int oeqb_conv_forward_rows8(oeqb_plan* plan, const float* xp, const float* Y, const float* W,
                             float* Z, const int64_t* rows, const int64_t* cols, int64_t nnz,

@@ -1004,6 +1004,7 @@ int launch(oeqb_plan& p, const void* kernel, const Args<T>& a, bool fwd_order, b
 }
 
 bool aligned16(const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15) == 0; }
+bool aligned32(const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 31) == 0; }
 
 template <class T>
 int launch_row(oeqb_plan& p, int kind, const Args<T>& a, cudaStream_t stream) {
@@ -1407,11 +1408,13 @@ bool edge1_pipe_class(const oeqb_plan& p) {
 }
 
 // Workspace of the pipelined kernels, in 32-byte node rows: X | dZ | then the dX accumulator
-// (atomic) or one 32-byte record per edge (deterministic backward pass A).
+// (atomic), or one 32-byte record per edge (deterministic backward pass A) followed by pass B's
+// 64-byte side slots, one per 32-position block.
 constexpr size_t kPadRowBytes = 32;
 size_t edge1_pipe_ws_bytes(const oeqb_plan& p, int64_t nnz, int64_t nodes) {
   const size_t rows = 2 * kPadRowBytes * size_t(std::max<int64_t>(nodes, 0));
-  return rows + (p.det ? kPadRowBytes * size_t(std::max<int64_t>(nnz, 0))
+  const size_t e = size_t(std::max<int64_t>(nnz, 0));
+  return rows + (p.det ? kPadRowBytes * e + sizeof(float) * kBandSlot * ((e + 31) / 32)
                        : kPadRowBytes * size_t(std::max<int64_t>(nodes, 0))) + 256;
 }
 
@@ -1420,7 +1423,7 @@ bool edge1_pipe_ok(const oeqb_plan& p, const Args<T>& a, const void* ws, size_t 
   if constexpr (!std::is_same_v<T, float>) {
     return false;
   } else {
-    return edge1_pipe_class(p) && ws && aligned16(ws) &&
+    return edge1_pipe_class(p) && ws && aligned32(ws) &&
            ws_bytes >= edge1_pipe_ws_bytes(p, a.nitems, a.nnodes) && aligned16(a.rows) &&
            aligned16(a.cols) && aligned16(a.W) && aligned16(a.Y);
   }
@@ -1452,8 +1455,8 @@ int launch_unpad(const oeqb_plan& p, const float* src, float* dst, int d, long l
 
 // Forward (pads X into the workspace first): kind 0 atomic, 4 deterministic.  Backward (pads
 // X and dZ): kind 1 atomic (clears the padded dX accumulator, then copies dX out), kind 5
-// deterministic (pass A writes the per-edge records, pass B, conv_bwd_edge1_gather, sums them
-// per sender).
+// deterministic (pass A writes the per-edge records, pass B, conv_bwd_edge1_band and its
+// fix-up, sums them per sender).
 // Main kernel of the pipelined single-path pass `kind` on node arrays already in the padded
 // layout (xp, gp, and out = the padded dX accumulator or the records).  sm_budget: 0 = CTAs
 // for every SM, > 0 = for at most that many SMs, < 0 = for all but that many (so that work
@@ -1526,10 +1529,11 @@ int launch_edge1_pipe(oeqb_plan& p, int kind, const Args<T>& a, void* ws, cudaSt
   if (kind == 1)
     return launch_unpad(p, tail, reinterpret_cast<float*>(a.out0), d1, a.nnodes, stream);
   if (kind == 5) {
-    // Pass B over a fixed partition (resident CTAs of the whole device): its summation order
-    // must not depend on the launch.
+    // Pass B: the banded per-block sums, then the fix-up that joins runs across blocks.  Both
+    // write plain dX rows; rows of nodes that send no edge stay at the cleared zero.
     const void* kb = edge1_pipe_kernel(6, p.edge1.code);
-    if (!kb) return launch_edge1<T>(p, 6, a, reinterpret_cast<T*>(tail), stream);
+    const void* kf = edge1_pipe_kernel(7, p.edge1.code);
+    if (!kb || !kf) return fail(OEQB_ERR_UNSUPPORTED, "no pass B kernel for this degree");
     int nb;
     {
       std::lock_guard<std::mutex> g(p.mu);
@@ -1542,10 +1546,20 @@ int launch_edge1_pipe(oeqb_plan& p, int kind, const Args<T>& a, void* ws, cudaSt
       }
       nb = it->second;
     }
+    OEQB_CUDA(cudaMemsetAsync(a.out0, 0, sizeof(T) * size_t(a.nnodes) * p.L1dim, stream));
     const float* recs = tail;
-    void* pb[] = {const_cast<Args<T>*>(&a), &e, &recs};
-    OEQB_CUDA(cudaLaunchKernel(kb, dim3(static_cast<unsigned>(p.sm_count * nb)),
-                               dim3(kEdgeWarps * 32), pb, 0, stream));
+    float* side = tail + size_t(kE1Rec) * size_t(a.nitems);
+    const long long blocks32 = (a.nitems + 31) / 32;
+    const long long ctas = std::max<long long>(
+        1, std::min<long long>((long long)p.sm_count * nb, (blocks32 + kEdgeWarps - 1) / kEdgeWarps));
+    void* pb[] = {const_cast<Args<T>*>(&a), &e, &recs, &side};
+    OEQB_CUDA(cudaLaunchKernel(kb, dim3(static_cast<unsigned>(ctas)), dim3(kEdgeWarps * 32), pb, 0,
+                               stream));
+    const float* cside = side;
+    void* pf[] = {const_cast<Args<T>*>(&a), &cside};
+    const unsigned fblocks = static_cast<unsigned>(
+        std::max<long long>(1, std::min<long long>((blocks32 + 255) / 256, (long long)p.sm_count * 8)));
+    OEQB_CUDA(cudaLaunchKernel(kf, dim3(fblocks), dim3(256), pf, 0, stream));
   }
   return 0;
 }
@@ -2046,7 +2060,9 @@ int rows8_check(const oeqb_plan* p, const void* xp, const float* Y, const float*
     return fail(OEQB_ERR_UNSUPPORTED, "the padded-row entry points take float32 atomic "
                                       "single-path plans with one weight per edge");
   if (nnz < 0 || nodes < 0) return fail(OEQB_ERR_INVALID, "negative size");
-  if (!aligned16(xp) || !aligned16(Y) || !aligned16(W) || !aligned16(rows) || !aligned16(cols))
+  if (!aligned32(xp))
+    return fail(OEQB_ERR_INVALID, "padded-row entry points need 32-byte aligned padded rows");
+  if (!aligned16(Y) || !aligned16(W) || !aligned16(rows) || !aligned16(cols))
     return fail(OEQB_ERR_INVALID, "padded-row entry points need 16-byte aligned arrays");
   return 0;
 }
@@ -2076,7 +2092,9 @@ int oeqb_conv_backward_rows8(oeqb_plan* p, const float* xp, const float* gp, con
                              const int64_t* rows, const int64_t* cols, int64_t nnz,
                              int64_t node_count, int sm_budget, void* stream) {
   if (int rc = rows8_check(p, xp, Y, W, rows, cols, nnz, node_count)) return rc;
-  if (!aligned16(gp) || !aligned16(dY) || !aligned16(dW) || !aligned16(dxp))
+  if (!aligned32(gp) || !aligned32(dxp))
+    return fail(OEQB_ERR_INVALID, "padded-row entry points need 32-byte aligned padded rows");
+  if (!aligned16(dY) || !aligned16(dW))
     return fail(OEQB_ERR_INVALID, "padded-row entry points need 16-byte aligned arrays");
   if (nnz == 0) return 0;
   DeviceGuard g(p->device);

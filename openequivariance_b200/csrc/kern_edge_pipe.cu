@@ -5,19 +5,23 @@
 namespace oeqb {
 
 // kind 0 / 1: pipelined atomic forward (two edges per lane) / backward of the triple `code`;
-// 4 / 5: deterministic forward / backward pass A; 6: deterministic backward pass B (by l1);
-// 4 / 5: deterministic
-// forward / backward pass A; 2 / 3: the row padding kernels.  nullptr for a triple without an
-// unrolled contraction.
+// 4 / 5: deterministic forward / backward pass A; 6 / 7: deterministic backward pass B, the
+// banded sums and their fix-up (by l1); 2 / 3: the row padding kernels.  nullptr for a triple
+// without an unrolled contraction.
 const void* edge1_pipe_kernel(int kind, int code) {
   if (kind == 2) return reinterpret_cast<const void*>(conv_pad_rows);
   if (kind == 3) return reinterpret_cast<const void*>(conv_unpad_rows);
-  if (kind == 6) {
+  if (kind == 6 || kind == 7) {
+    const bool fix = kind == 7;
     switch ((code >> 8) & 15) {
-      case 0: return reinterpret_cast<const void*>(conv_bwd_edge1_gather_pipe<0>);
-      case 1: return reinterpret_cast<const void*>(conv_bwd_edge1_gather_pipe<1>);
-      case 2: return reinterpret_cast<const void*>(conv_bwd_edge1_gather_pipe<2>);
-      case 3: return reinterpret_cast<const void*>(conv_bwd_edge1_gather_pipe<3>);
+      case 0: return fix ? reinterpret_cast<const void*>(conv_bwd_edge1_band_fix<0>)
+                         : reinterpret_cast<const void*>(conv_bwd_edge1_band<0>);
+      case 1: return fix ? reinterpret_cast<const void*>(conv_bwd_edge1_band_fix<1>)
+                         : reinterpret_cast<const void*>(conv_bwd_edge1_band<1>);
+      case 2: return fix ? reinterpret_cast<const void*>(conv_bwd_edge1_band_fix<2>)
+                         : reinterpret_cast<const void*>(conv_bwd_edge1_band<2>);
+      case 3: return fix ? reinterpret_cast<const void*>(conv_bwd_edge1_band_fix<3>)
+                         : reinterpret_cast<const void*>(conv_bwd_edge1_band<3>);
       default: return nullptr;
     }
   }

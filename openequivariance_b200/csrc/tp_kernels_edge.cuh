@@ -680,6 +680,10 @@ __global__ void __launch_bounds__(kEdgeWarps * 32) conv_fwd_edge1_det(const Args
 // 16-byte loads.
 constexpr int kE1Rec = 8;
 
+// Floats of side data per 32-position block in the banded deterministic pass B (a head and a
+// tail slot of 8 floats each).
+constexpr int kBandSlot = 16;
+
 template <class T>
 __device__ __forceinline__ T e1_key_bits(long long k) {
   if constexpr (sizeof(T) == 4)
