@@ -91,7 +91,8 @@ __device__ __forceinline__ void pipe_stage_in(PipeStage<D2>& st, const long long
   st.rows[lane] = lane < r ? rows[e] : -1;
   st.cols[lane] = lane < r ? cols[e] : 0;
   st.w[lane] = lane < r ? W[e] : 0.f;
-  for (int i = lane; i < r * D2; i += 32) st.y[i] = Y[base * D2 + i];
+#pragma unroll 1
+  for (int i = lane; i < 32 * D2; i += 32) st.y[i] = i < r * D2 ? Y[base * D2 + i] : 0.f;
 }
 
 // Node rows in the padded layout of these kernels: row n of a [nodes, D] tensor (D <= 8) at
@@ -184,93 +185,37 @@ __host__ __device__ constexpr size_t pipe_warp_bytes() {
   return sizeof(PipeStage<D2>) * kPipeStages;
 }
 
-// Range check of a staged edge (bad indices raise status 1 and drop the edge).
+// Validity of a staged edge: in_range = its position is before the end of the edge list (the
+// tail stage pads with row -1); an in-range edge with an index outside [0, nodes) raises
+// status 1 and is dropped.  One unsigned compare per index covers both bounds.
 __device__ __forceinline__ bool pipe_valid(long long row, long long col, long long nodes,
-                                           int* status) {
-  if (row == -1) return false;  // past the end of the edge list
-  if (row < 0 || row >= nodes || col < 0 || col >= nodes) {
-    flag(status, 1);
-    return false;
-  }
-  return true;
+                                           int* status, bool in_range) {
+  const bool ok = static_cast<unsigned long long>(row) < static_cast<unsigned long long>(nodes) &&
+                  static_cast<unsigned long long>(col) < static_cast<unsigned long long>(nodes);
+  if (in_range && !ok) flag(status, 1);
+  return in_range && ok;
 }
 
-// Forward.  xp: X in the padded layout.
-// One instantiation per degree triple (A, B, C), each with its own register allocation; the
-// host picks the plan's (edge1_pipe_kernel).
-template <int A, int B, int C>
-__global__ void __launch_bounds__(kEdgeWarps * 32) conv_fwd_edge1_pipe(const Args<float> a, const Edge1 p,
-                                                                       const float* __restrict__ xp) {
-  extern __shared__ __align__(16) unsigned char smem[];
-  const int lane = threadIdx.x & 31;
-  const long long nw = static_cast<long long>(gridDim.x) * kEdgeWarps;
-  const long long n = a.nitems;
-  const float pw = static_cast<float>(p.pw);
-  {
-    constexpr int D1 = 2 * A + 1, D2 = 2 * B + 1, D3 = 2 * C + 1;
-    auto* ring = reinterpret_cast<PipeStage<D2>*>(smem + (threadIdx.x >> 5) * pipe_warp_bytes<D2>());
-    const long long step = nw * 32;
-    long long base = (static_cast<long long>(blockIdx.x) * kEdgeWarps + (threadIdx.x >> 5)) * 32;
-    if (base >= n) return;
-    // Prologue: blocks 0 and 1 in flight, block 0's gathers issued.
-    pipe_stage_in<D2>(ring[0], a.rows, a.cols, a.W, a.Y, base, n, lane);
-    cp_async_commit();
-    pipe_stage_in<D2>(ring[1], a.rows, a.cols, a.W, a.Y, base + step, n, lane);
-    cp_async_commit();
-    cp_async_wait<1>();
-    __syncwarp();
-    bool vc = pipe_valid(ring[0].rows[lane], ring[0].cols[lane], a.nnodes, a.status);
-    float xc[D1];
-    if (vc) load_row8<D1>(xc, xp, ring[0].cols[lane]); else zero_row(xc);
-    int s = 0;
-    for (; base < n; base += step) {
-      const int s1 = s == kPipeStages - 1 ? 0 : s + 1;
-      const int s2 = s1 == kPipeStages - 1 ? 0 : s1 + 1;
-      // Block k+2 into the stage block k-1 used; block k+1 has landed after this wait.
-      pipe_stage_in<D2>(ring[s2], a.rows, a.cols, a.W, a.Y, base + 2 * step, n, lane);
-      cp_async_commit();
-      cp_async_wait<1>();
-      __syncwarp();
-      bool vn = false;
-      if (base + step < n) vn = pipe_valid(ring[s1].rows[lane], ring[s1].cols[lane], a.nnodes, a.status);
-      float xn[D1];
-      if (vn) load_row8<D1>(xn, xp, ring[s1].cols[lane]); else zero_row(xn);
-      // Block k.
-      const PipeStage<D2>& st = ring[s];
-      const long long row = vc ? st.rows[lane] : -1;
-      float z[D3];
+// Coalesced 16-byte stores of a staged full block [32, D] (base + 32 <= n; base a multiple of
+// 32, dst 16-byte aligned, src 16-byte aligned shared memory).
+template <int D>
+__device__ __forceinline__ void stage_out_full(float* dst, const float* src, long long base,
+                                               int lane) {
+  constexpr int NV = 32 * D / 4;
+  float4* g = reinterpret_cast<float4*>(dst + base * D);
+  const float4* s4 = reinterpret_cast<const float4*>(src);
 #pragma unroll
-      for (int k = 0; k < D3; ++k) z[k] = 0.f;
-      if (vc) {
-        float x[D1], y[D2];
-        const float w = st.w[lane] * pw;
-#pragma unroll
-        for (int i = 0; i < D1; ++i) x[i] = xc[i] * w;
-#pragma unroll
-        for (int j = 0; j < D2; ++j) y[j] = st.y[lane * D2 + j];
-        CG<A, B, C>::fwd(x, y, z);
-      }
-      const int r32 = static_cast<int>(row);
-      const int prev = __shfl_up_sync(0xffffffffu, r32, 1);
-      const bool head = row >= 0 && (lane == 0 || prev != r32);
-      e1_seg_sum<float, D3>(z, r32, lane);
-      if (head) red_vec(a.out0 + row * D3, z);
-      __syncwarp();  // every lane is done with stage s before it is refilled
-#pragma unroll
-      for (int i = 0; i < D1; ++i) xc[i] = xn[i];
-      vc = vn;
-      s = s1;
-    }
-    cp_async_wait<0>();
+  for (int q0 = 0; q0 < NV; q0 += 32) {
+    const int q = q0 + lane;
+    if (NV % 32 == 0 || q < NV) g[q] = s4[q];
   }
 }
 
 // Backward: per edge dY = w evec(g, x), dW = x . hvec(g, y), dX[col] += w hvec(g, y), with
 // g = pw dZ[row].  xp, gp: X and dZ in the padded layout; dxp: the padded dX accumulator
 // (zeroed by the caller).  dY and dW leave through a per-warp staging buffer as coalesced
-// 16-byte stores; dX is one vector reduction into a 32-byte row per edge.  dZ rows are
-// gathered at the start of the block's iteration (edges are receiver-sorted, so a block's dZ
-// rows are one or two rows, served by L1); X rows one block ahead.
+// 16-byte stores; dX is one vector reduction into a 32-byte row per edge.  The X and dZ rows
+// of a block are gathered one block ahead.
 template <int D2>
 __host__ __device__ constexpr size_t pipe_bwd_warp_bytes() {
   return pipe_warp_bytes<D2>() + sizeof(float) * 32 * (D2 + 1);
@@ -279,7 +224,8 @@ __host__ __device__ constexpr size_t pipe_bwd_warp_bytes() {
 // REC = false: atomic mode, dX reduced into the padded accumulator `out`.  REC = true: pass A
 // of the deterministic backward, each edge's message to its sender (D1 values and the
 // sender's index in the last of 8 slots: kE1Rec) written to `out` as one 32-byte record, in
-// edge order; pass B (conv_bwd_edge1_gather) sums them per sender in transpose_perm order.
+// edge order; pass B (conv_bwd_edge1_band and its fix-up) sums them per sender in
+// transpose_perm order.
 template <int D2, bool REC>
 __host__ __device__ constexpr size_t pipe_bwd_warp_bytes_m() {
   return pipe_bwd_warp_bytes<D2>() + (REC ? sizeof(float) * 32 * kE1Rec : 0);
@@ -311,9 +257,15 @@ __global__ void __launch_bounds__(kEdgeWarps * 32) conv_bwd_edge1_pipe(const Arg
     cp_async_commit();
     cp_async_wait<1>();
     __syncwarp();
-    bool vc = pipe_valid(ring[0].rows[lane], ring[0].cols[lane], a.nnodes, a.status);
-    float xc[D1];
-    if (vc) load_row8<D1>(xc, xp, ring[0].cols[lane]); else zero_row(xc);
+    bool vc = pipe_valid(ring[0].rows[lane], ring[0].cols[lane], a.nnodes, a.status, base + lane < n);
+    float xc[D1], gc[D3];
+    if (vc) {
+      load_row8<D1>(xc, xp, ring[0].cols[lane]);
+      load_row8<D3>(gc, gp, ring[0].rows[lane]);
+    } else {
+      zero_row(xc);
+      zero_row(gc);
+    }
     int s = 0;
     for (; base < n; base += step) {
       const int s1 = s == kPipeStages - 1 ? 0 : s + 1;
@@ -322,58 +274,67 @@ __global__ void __launch_bounds__(kEdgeWarps * 32) conv_bwd_edge1_pipe(const Arg
       cp_async_commit();
       cp_async_wait<1>();
       __syncwarp();
-      // Block k's dZ rows first (receiver-sorted: one or two rows per block, L1 hits), so that
-      // their latency overlaps the next block's checks and X gathers issued below.
+      // The next block's X and dZ rows are gathered now, a block ahead of their use.
       const PipeStage<D2>& st = ring[s];
+      const bool vn = pipe_valid(ring[s1].rows[lane], ring[s1].cols[lane], a.nnodes, a.status,
+                                 base + step + lane < n);
+      float xn[D1], gn[D3];
+      if (vn) {
+        load_row8<D1>(xn, xp, ring[s1].cols[lane]);
+        load_row8<D3>(gn, gp, ring[s1].rows[lane]);
+      } else {
+        zero_row(xn);
+        zero_row(gn);
+      }
       float g[D3];
-      if (vc) load_row8<D3>(g, gp, st.rows[lane]); else zero_row(g);
-      bool vn = false;
-      if (base + step < n) vn = pipe_valid(ring[s1].rows[lane], ring[s1].cols[lane], a.nnodes, a.status);
-      float xn[D1];
-      if (vn) load_row8<D1>(xn, xp, ring[s1].cols[lane]); else zero_row(xn);
-      // Block k.
-      float h[D1], ev[D2];
+#pragma unroll
+      for (int k = 0; k < D3; ++k) g[k] = gc[k];
+      // Block k.  The contraction runs on every lane: a dropped edge has g = x = 0 (and the
+      // tail stage pads Y and W with zeros), so its h, dY and dW are zero.
+      const long long col = st.cols[lane];
+      float h[D1], ev[D2], y[D2];
+#pragma unroll
+      for (int k = 0; k < D3; ++k) g[k] *= pw;
+#pragma unroll
+      for (int j = 0; j < D2; ++j) y[j] = st.y[lane * D2 + j];
+      CG<A, B, C>::hvec(g, y, h);
+      CG<A, B, C>::evec(g, xc, ev);
+      const float w = st.w[lane];
       float sdot = 0.f;
 #pragma unroll
-      for (int i = 0; i < D1; ++i) h[i] = 0.f;
-#pragma unroll
-      for (int j = 0; j < D2; ++j) ev[j] = 0.f;
-      const long long col = st.cols[lane];
-      if (vc) {
-        float y[D2];
-#pragma unroll
-        for (int k = 0; k < D3; ++k) g[k] *= pw;
-#pragma unroll
-        for (int j = 0; j < D2; ++j) y[j] = st.y[lane * D2 + j];
-        CG<A, B, C>::hvec(g, y, h);
-        CG<A, B, C>::evec(g, xc, ev);
-        const float w = st.w[lane];
-#pragma unroll
-        for (int i = 0; i < D1; ++i) {
-          sdot += xc[i] * h[i];
-          h[i] *= w;
-        }
-#pragma unroll
-        for (int j = 0; j < D2; ++j) ev[j] *= w;
+      for (int i = 0; i < D1; ++i) {
+        sdot += xc[i] * h[i];
+        h[i] *= w;
       }
 #pragma unroll
-      for (int j = 0; j < D2; ++j) yo[lane * D2 + j] = ev[j];
+      for (int j = 0; j < D2; ++j) yo[lane * D2 + j] = ev[j] * w;
       wo[lane] = sdot;
       if constexpr (REC) {
+        float r8[kE1Rec];
 #pragma unroll
-        for (int i = 0; i < kE1Rec - 1; ++i) ho[lane * kE1Rec + i] = i < D1 ? h[i] : 0.f;
-        ho[lane * kE1Rec + kE1Rec - 1] = e1_key_bits<float>(vc ? col : -1);
+        for (int i = 0; i < kE1Rec - 1; ++i) r8[i] = i < D1 ? h[i] : 0.f;
+        r8[kE1Rec - 1] = e1_key_bits<float>(vc ? col : -1);
+        float4* hr = reinterpret_cast<float4*>(ho + lane * kE1Rec);
+        hr[0] = make_float4(r8[0], r8[1], r8[2], r8[3]);
+        hr[1] = make_float4(r8[4], r8[5], r8[6], r8[7]);
       }
       __syncwarp();
-      e1_stage_out<float, D2>(a.out1, yo, base, n, lane);
-      e1_stage_out<float, 1>(a.out2, wo, base, n, lane);
-      if constexpr (REC)
-        e1_stage_out<float, kE1Rec>(out, ho, base, n, lane);
-      else if (vc)
-        red_row8<D1>(out + col * kPadRow, h);
+      if (base + 32 <= n) {
+        stage_out_full<D2>(a.out1, yo, base, lane);
+        stage_out_full<1>(a.out2, wo, base, lane);
+        if constexpr (REC) stage_out_full<kE1Rec>(out, ho, base, lane);
+      } else {
+        e1_stage_out<float, D2>(a.out1, yo, base, n, lane);
+        e1_stage_out<float, 1>(a.out2, wo, base, n, lane);
+        if constexpr (REC) e1_stage_out<float, kE1Rec>(out, ho, base, n, lane);
+      }
+      if constexpr (!REC)
+        if (vc) red_row8<D1>(out + col * kPadRow, h);
       __syncwarp();  // stage s and the output buffers are free again
 #pragma unroll
       for (int i = 0; i < D1; ++i) xc[i] = xn[i];
+#pragma unroll
+      for (int k = 0; k < D3; ++k) gc[k] = gn[k];
       vc = vn;
       s = s1;
     }
@@ -386,7 +347,7 @@ __global__ void __launch_bounds__(kEdgeWarps * 32) conv_bwd_edge1_pipe(const Arg
 // when they do, so one segmented shuffle sum serves 64 edges (it is a third of the one-edge
 // kernel's instructions); where the pair straddles a receiver boundary the first message goes
 // to its receiver with its own vector reduction.  The stage ring, the padded X gathers one
-// step ahead and the tail handling are as in conv_fwd_edge1_pipe, with 64-edge stages.
+// step ahead and the tail handling are as in conv_bwd_edge1_pipe, with 64-edge stages.
 template <int D2>
 struct PipeStage2 {
   long long rows[64];
@@ -440,7 +401,8 @@ __device__ __forceinline__ void pipe2_stage_in(PipeStage2<D2>& st, const long lo
     st.cols[i] = i < r ? cols[base + i] : 0;
     st.w[i] = i < r ? W[base + i] : 0.f;
   }
-  for (int i = lane; i < r * D2; i += 32) st.y[i] = Y[base * D2 + i];
+#pragma unroll 1
+  for (int i = lane; i < 64 * D2; i += 32) st.y[i] = i < r * D2 ? Y[base * D2 + i] : 0.f;
 }
 
 template <int A, int B, int C>
@@ -463,8 +425,8 @@ __global__ void __launch_bounds__(kEdgeWarps * 32) conv_fwd_edge1_pipe2(const Ar
   cp_async_commit();
   cp_async_wait<1>();
   __syncwarp();
-  bool v0c = pipe_valid(ring[0].rows[e0], ring[0].cols[e0], a.nnodes, a.status);
-  bool v1c = pipe_valid(ring[0].rows[e1], ring[0].cols[e1], a.nnodes, a.status);
+  bool v0c = pipe_valid(ring[0].rows[e0], ring[0].cols[e0], a.nnodes, a.status, base + e0 < n);
+  bool v1c = pipe_valid(ring[0].rows[e1], ring[0].cols[e1], a.nnodes, a.status, base + e1 < n);
   float x0c[D1], x1c[D1];
   if (v0c) load_row8<D1>(x0c, xp, ring[0].cols[e0]); else zero_row(x0c);
   if (v1c) load_row8<D1>(x1c, xp, ring[0].cols[e1]); else zero_row(x1c);
@@ -476,20 +438,21 @@ __global__ void __launch_bounds__(kEdgeWarps * 32) conv_fwd_edge1_pipe2(const Ar
     cp_async_commit();
     cp_async_wait<1>();
     __syncwarp();
-    bool v0n = false, v1n = false;
-    if (base + step < n) {
-      v0n = pipe_valid(ring[s1].rows[e0], ring[s1].cols[e0], a.nnodes, a.status);
-      v1n = pipe_valid(ring[s1].rows[e1], ring[s1].cols[e1], a.nnodes, a.status);
-    }
+    const bool v0n = pipe_valid(ring[s1].rows[e0], ring[s1].cols[e0], a.nnodes, a.status,
+                                base + step + e0 < n);
+    const bool v1n = pipe_valid(ring[s1].rows[e1], ring[s1].cols[e1], a.nnodes, a.status,
+                                base + step + e1 < n);
     float x0n[D1], x1n[D1];
     if (v0n) load_row8<D1>(x0n, xp, ring[s1].cols[e0]); else zero_row(x0n);
     if (v1n) load_row8<D1>(x1n, xp, ring[s1].cols[e1]); else zero_row(x1n);
     const PipeStage2<D2>& st = ring[s];
     const long long r0 = v0c ? st.rows[e0] : -1, r1 = v1c ? st.rows[e1] : -1;
+    // Both contractions run on every lane: a dropped edge has x = 0 (and the tail stage pads Y
+    // and W with zeros), so its message is zero.
     float z0[D3], z1[D3];
 #pragma unroll
     for (int k = 0; k < D3; ++k) z0[k] = z1[k] = 0.f;
-    if (v0c) {
+    {
       float x[D1], y[D2];
       const float w = st.w[e0] * pw;
 #pragma unroll
@@ -498,7 +461,7 @@ __global__ void __launch_bounds__(kEdgeWarps * 32) conv_fwd_edge1_pipe2(const Ar
       for (int j = 0; j < D2; ++j) y[j] = st.y[e0 * D2 + j];
       CG<A, B, C>::fwd(x, y, z0);
     }
-    if (v1c) {
+    {
       float x[D1], y[D2];
       const float w = st.w[e1] * pw;
 #pragma unroll
@@ -706,7 +669,7 @@ __global__ void __launch_bounds__(256) conv_bwd_edge1_band_fix(const Args<float>
 // row is written once with plain stores: the result does not depend on timing.  The per-edge
 // streams go through the cp.async ring, the X rows (padded layout) are gathered a block ahead.
 template <int A, int B, int C>
-__global__ void __launch_bounds__(kEdgeWarps * 32) conv_fwd_edge1_det_pipe(const Args<float> a, const Edge1 p,
+__global__ void __launch_bounds__(kEdgeWarps * 32, A + C >= 6 ? 4 : 5) conv_fwd_edge1_det_pipe(const Args<float> a, const Edge1 p,
                                                                            const float* __restrict__ xp) {
   extern __shared__ __align__(16) unsigned char smem[];
   const int lane = threadIdx.x & 31;
@@ -724,7 +687,7 @@ __global__ void __launch_bounds__(kEdgeWarps * 32) conv_fwd_edge1_det_pipe(const
   auto valid = [&](const PipeStage<D2>& st, long long base) {
     const long long e = base + lane;
     if (e < p0 || e >= p1) return false;
-    return pipe_valid(st.rows[lane], st.cols[lane], a.nnodes, a.status);
+    return pipe_valid(st.rows[lane], st.cols[lane], a.nnodes, a.status, true);
   };
   long long base = p0 & ~3LL;
   pipe_stage_in<D2>(ring[0], a.rows, a.cols, a.W, a.Y, base, p1, lane);
