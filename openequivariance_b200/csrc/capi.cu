@@ -1468,7 +1468,7 @@ int launch_edge1_pipe_main(oeqb_plan& p, int kind, const Args<T>& a, const float
   const void* kernel = edge1_pipe_kernel(kind, p.edge1.code);
   if (!kernel) return fail(OEQB_ERR_UNSUPPORTED, "no pipelined kernel for this degree triple");
   const int d2 = 2 * ((p.edge1.code >> 4) & 15) + 1;
-  const int epw = kind == 0 ? 64 : 32;  // edges per warp step (the atomic forward takes two per lane)
+  const int epw = kind == 0 || kind == 4 ? 64 : 32;  // edges per warp step (the forwards take two per lane)
   const size_t stage = 2 * epw * sizeof(long long) + epw * sizeof(float) * (1 + d2);
   const size_t per_warp = 3 * stage + (bwd ? 32 * sizeof(float) * (d2 + 1) : 0) +
                           (kind == 5 ? 32 * sizeof(float) * kE1Rec : 0);

@@ -5,7 +5,7 @@
 namespace oeqb {
 
 // kind 0 / 1: pipelined atomic forward (two edges per lane) / backward of the triple `code`;
-// 4 / 5: deterministic forward / backward pass A; 6 / 7: deterministic backward pass B, the
+// 4 / 5: deterministic forward (two edges per lane) / backward pass A; 6 / 7: deterministic backward pass B, the
 // banded sums and their fix-up (by l1); 2 / 3: the row padding kernels.  nullptr for a triple
 // without an unrolled contraction.
 const void* edge1_pipe_kernel(int kind, int code) {
@@ -30,7 +30,7 @@ const void* edge1_pipe_kernel(int kind, int code) {
     switch (kind) {                                                                           \
       case 0: return reinterpret_cast<const void*>(conv_fwd_edge1_pipe2<A, B, C>);            \
       case 1: return reinterpret_cast<const void*>(conv_bwd_edge1_pipe<A, B, C, false>);      \
-      case 4: return reinterpret_cast<const void*>(conv_fwd_edge1_det_pipe<A, B, C>);         \
+      case 4: return reinterpret_cast<const void*>(conv_fwd_edge1_det_pipe2<A, B, C>);        \
       case 5: return reinterpret_cast<const void*>(conv_bwd_edge1_pipe<A, B, C, true>);       \
       default: return nullptr;                                                                \
     }                                                                                         \

@@ -661,16 +661,21 @@ __global__ void __launch_bounds__(256) conv_bwd_edge1_band_fix(const Args<float>
   }
 }
 
-// Deterministic forward (same mapping as conv_fwd_edge1_det): warp w owns the edges of whole
-// receivers, its nominal range [w E / W, (w+1) E / W) moved forward to receiver boundaries,
-// and walks it in consecutive 32-edge blocks starting at the 4-aligned edge at or below the
-// range start (so Y rows start 16-byte aligned; lanes before the range are masked).  Sums of
-// receivers that continue into the next block are carried in registers, and every receiver
-// row is written once with plain stores: the result does not depend on timing.  The per-edge
-// streams go through the cp.async ring, the X rows (padded layout) are gathered a block ahead.
+// Deterministic forward, two edges per lane.  Warp w owns the edges of whole receivers: its
+// nominal range [w E / W, (w+1) E / W) moved forward to receiver boundaries, walked in 64-edge
+// blocks from the 4-aligned edge at or below the range start (so Y rows start 16-byte aligned;
+// edges outside the range are masked).  Lane l holds edges 2l and 2l+1 (keys a <= b, the
+// receivers).  When a == b the lane sums its pair.  Otherwise edge 2l ends run a inside the
+// lane: its message goes to lane l-1 when that lane's second edge is in the same run (added
+// to that lane's value, so the run's shuffle-tree sum includes it), and is stored as a
+// complete row when the run has no other edge in this block (or, on lane 0, added to the
+// sum carried from the previous block).  The lanes' second-edge runs are then summed as in
+// conv_fwd_edge1_det: a segmented shuffle tree per block, sums of runs that continue into the
+// next block carried in registers, and every receiver row written once with plain stores, in
+// an order fixed by the partition (the grid is the device's resident CTAs), not by timing.
 template <int A, int B, int C>
-__global__ void __launch_bounds__(kEdgeWarps * 32, A + C >= 6 ? 4 : 5) conv_fwd_edge1_det_pipe(const Args<float> a, const Edge1 p,
-                                                                           const float* __restrict__ xp) {
+__global__ void __launch_bounds__(kEdgeWarps * 32) conv_fwd_edge1_det_pipe2(const Args<float> a, const Edge1 p,
+                                                                            const float* __restrict__ xp) {
   extern __shared__ __align__(16) unsigned char smem[];
   const int lane = threadIdx.x & 31;
   const long long nwarps = static_cast<long long>(gridDim.x) * kEdgeWarps;
@@ -682,59 +687,101 @@ __global__ void __launch_bounds__(kEdgeWarps * 32, A + C >= 6 ? 4 : 5) conv_fwd_
   const long long p1 = e1_snap(static_cast<long long>((static_cast<__int128>(n) * (wg + 1)) / nwarps), n, key, lane);
   if (p0 >= p1) return;
   constexpr int D1 = 2 * A + 1, D2 = 2 * B + 1, D3 = 2 * C + 1;
-  auto* ring = reinterpret_cast<PipeStage<D2>*>(smem + (threadIdx.x >> 5) * pipe_warp_bytes<D2>());
-  // Validity of lane `lane` of the block at `base`: inside [p0, p1) with good indices.
-  auto valid = [&](const PipeStage<D2>& st, long long base) {
-    const long long e = base + lane;
-    if (e < p0 || e >= p1) return false;
-    return pipe_valid(st.rows[lane], st.cols[lane], a.nnodes, a.status, true);
+  auto* ring = reinterpret_cast<PipeStage2<D2>*>(smem + (threadIdx.x >> 5) * pipe2_warp_bytes<D2>());
+  const int e0 = 2 * lane, e1 = 2 * lane + 1;
+  // Validity of edge e of the block at `base`: inside [p0, p1) with good indices.
+  auto valid = [&](const PipeStage2<D2>& st, long long base, int e) {
+    const long long t = base + e;
+    if (t < p0 || t >= p1) return false;
+    return pipe_valid(st.rows[e], st.cols[e], a.nnodes, a.status, true);
   };
   long long base = p0 & ~3LL;
-  pipe_stage_in<D2>(ring[0], a.rows, a.cols, a.W, a.Y, base, p1, lane);
+  pipe2_stage_in<D2>(ring[0], a.rows, a.cols, a.W, a.Y, base, p1, lane);
   cp_async_commit();
-  pipe_stage_in<D2>(ring[1], a.rows, a.cols, a.W, a.Y, base + 32, p1, lane);
+  pipe2_stage_in<D2>(ring[1], a.rows, a.cols, a.W, a.Y, base + 64, p1, lane);
   cp_async_commit();
   cp_async_wait<1>();
   __syncwarp();
-  bool vc = valid(ring[0], base);
-  float xc[D1];
-  if (vc) load_row8<D1>(xc, xp, ring[0].cols[lane]); else zero_row(xc);
+  bool v0c = valid(ring[0], base, e0), v1c = valid(ring[0], base, e1);
+  float x0c[D1], x1c[D1];
+  if (v0c) load_row8<D1>(x0c, xp, ring[0].cols[e0]); else zero_row(x0c);
+  if (v1c) load_row8<D1>(x1c, xp, ring[0].cols[e1]); else zero_row(x1c);
   float carry[D3];
   long long carry_key = -2;
   int s = 0;
-  for (; base < p1; base += 32) {
+  for (; base < p1; base += 64) {
     const int s1 = s == kPipeStages - 1 ? 0 : s + 1;
     const int s2 = s1 == kPipeStages - 1 ? 0 : s1 + 1;
-    pipe_stage_in<D2>(ring[s2], a.rows, a.cols, a.W, a.Y, base + 64, p1, lane);
+    pipe2_stage_in<D2>(ring[s2], a.rows, a.cols, a.W, a.Y, base + 128, p1, lane);
     cp_async_commit();
     cp_async_wait<1>();
     __syncwarp();
-    const bool more = base + 32 < p1;
-    bool vn = false;
-    if (more) vn = valid(ring[s1], base + 32);
-    float xn[D1];
-    if (vn) load_row8<D1>(xn, xp, ring[s1].cols[lane]); else zero_row(xn);
-    const PipeStage<D2>& st = ring[s];
-    float z[D3];
+    const bool more = base + 64 < p1;
+    const bool v0n = more && valid(ring[s1], base + 64, e0);
+    const bool v1n = more && valid(ring[s1], base + 64, e1);
+    float x0n[D1], x1n[D1];
+    if (v0n) load_row8<D1>(x0n, xp, ring[s1].cols[e0]); else zero_row(x0n);
+    if (v1n) load_row8<D1>(x1n, xp, ring[s1].cols[e1]); else zero_row(x1n);
+    const PipeStage2<D2>& st = ring[s];
+    // Both contractions run on every lane: a masked or dropped edge has x = 0 (and the tail
+    // stage pads Y and W with zeros), so its message is zero.
+    float z0[D3], z1[D3];
 #pragma unroll
-    for (int k = 0; k < D3; ++k) z[k] = 0.f;
-    if (vc) {
+    for (int k = 0; k < D3; ++k) z0[k] = z1[k] = 0.f;
+    {
       float x[D1], y[D2];
-      const float w = st.w[lane] * pw;
+      const float w = st.w[e0] * pw;
 #pragma unroll
-      for (int i = 0; i < D1; ++i) x[i] = xc[i] * w;
+      for (int i = 0; i < D1; ++i) x[i] = x0c[i] * w;
 #pragma unroll
-      for (int j = 0; j < D2; ++j) y[j] = st.y[lane * D2 + j];
-      CG<A, B, C>::fwd(x, y, z);
+      for (int j = 0; j < D2; ++j) y[j] = st.y[e0 * D2 + j];
+      CG<A, B, C>::fwd(x, y, z0);
     }
-    // First receiver of the next block (lane 0 of its stage), to tell whether the last run
+    {
+      float x[D1], y[D2];
+      const float w = st.w[e1] * pw;
+#pragma unroll
+      for (int i = 0; i < D1; ++i) x[i] = x1c[i] * w;
+#pragma unroll
+      for (int j = 0; j < D2; ++j) y[j] = st.y[e1 * D2 + j];
+      CG<A, B, C>::fwd(x, y, z1);
+    }
+    const long long ka = v0c ? st.rows[e0] : -1, kb = v1c ? st.rows[e1] : -1;
+    if (ka >= 0 && ka == kb) {
+#pragma unroll
+      for (int k = 0; k < D3; ++k) z1[k] += z0[k];
+    }
+    // Edge 2l ending run ka inside the lane: to lane l-1 if its second edge is in the run.
+    const bool endp = ka >= 0 && ka != kb;
+    int prev_b = __shfl_up_sync(0xffffffffu, static_cast<int>(kb), 1);
+    if (lane == 0) prev_b = -3;
+    const bool push = endp && prev_b == static_cast<int>(ka);
+    const bool recv = __shfl_down_sync(0xffffffffu, push ? 1 : 0, 1) != 0 && lane < 31;
+#pragma unroll
+    for (int k = 0; k < D3; ++k) {
+      const float t = __shfl_down_sync(0xffffffffu, z0[k], 1);
+      if (recv) z1[k] += t;
+    }
+    if (endp && !push) {
+      // Run ka has no other edge in this block: complete, unless lane 0 continues the carry.
+      if (lane == 0 && ka == carry_key) {
+#pragma unroll
+        for (int k = 0; k < D3; ++k) z0[k] = carry[k] + z0[k];
+      }
+      e1_store_row(a.out0 + ka * D3, z0);
+    }
+    // First receiver of the next block (edge 0 of its stage), to tell whether the last run
     // continues.
     const long long nk = more ? ring[s1].rows[0] : -3;
-    e1_seg_block<float, D3>(z, vc ? st.rows[lane] : -1, nk, more, carry, carry_key, a.out0, lane);
+    e1_seg_block<float, D3>(z1, kb, nk, more, carry, carry_key, a.out0, lane);
     __syncwarp();
 #pragma unroll
-    for (int i = 0; i < D1; ++i) xc[i] = xn[i];
-    vc = vn;
+    for (int i = 0; i < D1; ++i) {
+      x0c[i] = x0n[i];
+      x1c[i] = x1n[i];
+    }
+    v0c = v0n;
+    v1c = v1n;
     s = s1;
   }
   cp_async_wait<0>();
