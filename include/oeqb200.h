@@ -143,7 +143,7 @@ int oeqb_conv_double_backward(oeqb_plan* plan, const void* L1_in, const void* L2
 /* ---- convolution on node arrays in padded rows (no counterpart in the reference) ----
  * For float32 atomic plans of the single-path multiplicity-1 class with one weight per edge
  * (oeqb_conv_rows8_ok returns 1).  Node arrays are [node_count, 8] floats: row n of X (or dZ,
- * dX) in the first L1 (L3) of its 8 slots, 32-byte aligned rows, the padding slots zero.  This
+ * dX) in the first L1 (L3) of its 8 slots, 32-byte aligned rows; the padding slots are never read.  This
  * is the kernels' own layout, so callers that keep node data in it for many calls (the
  * multi-GPU partition of openequivariance_b200.distributed, whose halo rows arrive from other
  * GPUs straight into such a buffer) skip the per-call layout copies of oeqb_conv_forward /
