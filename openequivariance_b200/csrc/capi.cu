@@ -1828,9 +1828,8 @@ const char* status_message(int code) {
 }  // namespace
 
 // ---------------------------------------------------------------------------------------
-// Allocation-free forward (oeqb_tp_forward_noalloc).  The problem tables and the status
-// flag live in this file-scope device array instead of plan memory, so the call needs no
-// device allocation.  Every call on a device shares the array and leaves its contents
+// Allocation-free forward (oeqb_tp_forward_noalloc).  The problem tables live in this
+// file-scope device array instead of plan memory, so the call needs no device allocation.  Every call on a device shares the array and leaves its contents
 // behind; calls whose GPU work overlaps (e.g. on two streams) race on it.
 constexpr size_t kNoAllocBytes = 64 * 1024;
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocBytes];

@@ -139,3 +139,84 @@ def test_validate_through_the_c_abi(cuda_device):
     assert lib.oeqb_conv_validate(p(r), p(c), p(t), ctypes.c_int64(E), ctypes.c_int64(n), 1,
                                   p(scratch), ctypes.c_size_t(8), stream) == 1
     assert b"scratch" in lib.oeqb_last_error()
+
+
+def _clear_status():
+    """Reads every plan's flag until none is set (a flag left by an earlier test is not this
+    test's concern)."""
+    import openequivariance_b200 as oeq
+
+    for _ in range(1000):
+        try:
+            oeq.check_device_status()
+            return
+        except RuntimeError:
+            continue
+    raise AssertionError("device status flags keep being set")
+
+
+@pytest.mark.parametrize("deterministic", [False, True])
+def test_kernels_drop_and_flag_bad_edges_with_checks_off(deterministic, cuda_device):
+    """With the device checks off the bad graph reaches the single-path (C3-class) kernels.
+    They skip the bad edge, raise the plan's status flag, and ``check_device_status`` reports
+    it.  The other edges' results equal the oracle on the graph without that edge."""
+    import openequivariance_b200 as oeq
+    import tp_oracle as O
+    from gpu_util import assert_close
+
+    oeq.set_device_checks(False)
+    _clear_status()
+    n, rows, cols, tperm = _graph()
+    bad = 17
+    cols = cols.copy()
+    cols[bad] = n + 3
+    prob = oeq.TPProblem("1x2e", "1x3e", "1x2e", [(0, 0, 0, "uvu", True)],
+                         shared_weights=False, internal_weights=False)
+    conv = oeq.TensorProductConv(prob, deterministic=deterministic)
+    E = len(rows)
+    rng = np.random.default_rng(3)
+    X, Y = rng.normal(size=(n, 5)), rng.normal(size=(E, 7))
+    W, G = rng.normal(size=(E, 1)), rng.normal(size=(n, 5))
+    dev = lambda a: torch.tensor(a, device="cuda")  # noqa: E731
+    x, y, w = (dev(a.astype(np.float32)).requires_grad_() for a in (X, Y, W))
+    z = conv(x, y, w, dev(rows), dev(cols), dev(tperm) if deterministic else None)
+    z.backward(dev(G.astype(np.float32)))
+    torch.cuda.synchronize()
+    with pytest.raises(RuntimeError, match="edge index out of range"):
+        oeq.check_device_status()
+    oeq.check_device_status()  # reading the flag cleared it
+    keep = np.arange(E) != bad
+    p = O.make_problem("1x2e", "1x3e", "1x2e", [(0, 0, 0, "uvu", True)])
+    r, c = rows[keep], cols[keep]
+    assert_close(z, O.conv_forward(p, X, Y[keep], W[keep], r, c), np.float32, "forward")
+    gX, gY, gW = O.conv_backward(p, X, Y[keep], W[keep], G, r, c)
+    assert_close(x.grad, gX, np.float32, "dX")
+    assert_close(y.grad[torch.from_numpy(keep).cuda()], gY, np.float32, "dY")
+    assert_close(w.grad[torch.from_numpy(keep).cuda()], gW, np.float32, "dW")
+
+
+def test_band_pass_flags_bad_permutation_entry_with_checks_off(cuda_device):
+    """An out-of-range transpose_perm entry reaches the deterministic backward's pass B with
+    the checks off: the position is skipped and status 2 is reported."""
+    import openequivariance_b200 as oeq
+
+    oeq.set_device_checks(False)
+    _clear_status()
+    n, rows, cols, tperm = _graph()
+    tperm = tperm.copy()
+    tperm[0] = len(rows) + 10
+    prob = oeq.TPProblem("1x2e", "1x3e", "1x2e", [(0, 0, 0, "uvu", True)],
+                         shared_weights=False, internal_weights=False)
+    conv = oeq.TensorProductConv(prob, deterministic=True)
+    E = len(rows)
+    gen = torch.Generator(device="cuda").manual_seed(0)
+    x = torch.randn(n, 5, device="cuda", generator=gen, requires_grad=True)
+    y = torch.randn(E, 7, device="cuda", generator=gen)
+    w = torch.randn(E, 1, device="cuda", generator=gen)
+    dev = lambda a: torch.tensor(a, device="cuda")  # noqa: E731
+    z = conv(x, y, w, dev(rows), dev(cols), dev(tperm))
+    z.backward(torch.ones_like(z))
+    torch.cuda.synchronize()
+    assert torch.isfinite(x.grad).all()
+    with pytest.raises(RuntimeError, match="transpose_perm entry out of range"):
+        oeq.check_device_status()
