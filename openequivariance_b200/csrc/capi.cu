@@ -39,6 +39,8 @@ const void* row_kernel_ptr(int kind, int nwarps);
 template <class T>
 const void* seg_kernel_ptr(int kind);
 template <class T>
+const void* edge1_band_kernel(int l1, bool fix);
+template <class T>
 const void* lk_kernel_ptr(int cpl);
 template <class T>
 const void* lkf_kernel_ptr(int cpl);
@@ -1357,6 +1359,7 @@ template <class T>
 int launch_edge1(oeqb_plan& p, int kind, const Args<T>& a, T* ws, cudaStream_t stream) {
   if (a.nitems <= 0) return 0;
   const void* kernel = edge_kernel_ptr<T>(kind);
+  if (!kernel) return fail(OEQB_ERR_UNSUPPORTED, "no single-path edge kernel of this kind");
   const int d2 = 2 * ((p.edge1.code >> 4) & 15) + 1;
   const int per_warp = kind == 2 || kind == 4 ? 32 * d2 : kind == 3 ? 64 * d2
                        : kind == 5 ? 64 * d2 + 32 * kE1Rec : 0;
@@ -1375,7 +1378,7 @@ int launch_edge1(oeqb_plan& p, int kind, const Args<T>& a, T* ws, cudaStream_t s
   }
   const long long cap = (long long)p.sm_count * per_sm;
   long long blocks;
-  if (kind == 4 || kind == 6) {
+  if (kind == 4) {
     blocks = cap;  // fixed partition (deterministic summation order)
   } else {
     const long long warps = (a.nitems + 31) / 32;
@@ -1388,7 +1391,6 @@ int launch_edge1(oeqb_plan& p, int kind, const Args<T>& a, T* ws, cudaStream_t s
   return 0;
 }
 
-// Workspace of the single-path deterministic backward: one record per edge.
 // Pipelined single-path kernels (tp_kernels_edge_pipe.cuh): float32, one weight per edge,
 // 16-byte aligned streams.  OEQB_EDGE_PIPE=0 selects the unpipelined kernels instead.
 bool edge1_pipe_enabled() {
@@ -1450,6 +1452,43 @@ int launch_unpad(const oeqb_plan& p, const float* src, float* dst, int d, long l
       std::min<long long>((work + 255) / 256, static_cast<long long>(p.sm_count) * 8));
   void* params[] = {&src, &dst, &d, &nodes};
   OEQB_CUDA(cudaLaunchKernel(edge1_pipe_kernel(3, 0), dim3(blocks), dim3(256), params, 0, stream));
+  return 0;
+}
+
+// Deterministic backward pass B of the single-path class: the banded per-block sums of the
+// records `recs` (written by pass A in edge order), then the fix-up that joins runs across
+// 32-position blocks through the side slots `side` (kBandSlot values per block).  The caller
+// has cleared dX (a.out0): rows of nodes that send no edge are not written.
+template <class T>
+int launch_band(oeqb_plan& p, const Args<T>& a, const T* recs, T* side, cudaStream_t stream) {
+  const int l1 = (p.edge1.code >> 8) & 15;
+  const void* kb = edge1_band_kernel<T>(l1, false);
+  const void* kf = edge1_band_kernel<T>(l1, true);
+  if (!kb || !kf) return fail(OEQB_ERR_UNSUPPORTED, "no pass B kernel for this degree");
+  int nb;
+  {
+    std::lock_guard<std::mutex> g(p.mu);
+    auto it = p.occ.find(kb);
+    if (it == p.occ.end()) {
+      int m = 0;
+      OEQB_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&m, kb, kEdgeWarps * 32, 0));
+      if (m <= 0) return fail(OEQB_ERR_UNSUPPORTED, "pass B kernel does not fit");
+      it = p.occ.emplace(kb, m).first;
+    }
+    nb = it->second;
+  }
+  const long long blocks32 = (a.nitems + 31) / 32;
+  const long long ctas = std::max<long long>(
+      1, std::min<long long>((long long)p.sm_count * nb, (blocks32 + kEdgeWarps - 1) / kEdgeWarps));
+  Edge1 e = p.edge1;
+  void* pb[] = {const_cast<Args<T>*>(&a), &e, &recs, &side};
+  OEQB_CUDA(cudaLaunchKernel(kb, dim3(static_cast<unsigned>(ctas)), dim3(kEdgeWarps * 32), pb, 0,
+                             stream));
+  const T* cside = side;
+  void* pf[] = {const_cast<Args<T>*>(&a), &cside};
+  const unsigned fblocks = static_cast<unsigned>(
+      std::max<long long>(1, std::min<long long>((blocks32 + 255) / 256, (long long)p.sm_count * 8)));
+  OEQB_CUDA(cudaLaunchKernel(kf, dim3(fblocks), dim3(256), pf, 0, stream));
   return 0;
 }
 
@@ -1525,48 +1564,24 @@ int launch_edge1_pipe(oeqb_plan& p, int kind, const Args<T>& a, void* ws, cudaSt
       return rc;
   }
   if (int rc = launch_edge1_pipe_main<T>(p, kind, a, xp, gp, tail, 0, stream)) return rc;
-  Edge1 e = p.edge1;
   if (kind == 1)
     return launch_unpad(p, tail, reinterpret_cast<float*>(a.out0), d1, a.nnodes, stream);
   if (kind == 5) {
-    // Pass B: the banded per-block sums, then the fix-up that joins runs across blocks.  Both
-    // write plain dX rows; rows of nodes that send no edge stay at the cleared zero.
-    const void* kb = edge1_pipe_kernel(6, p.edge1.code);
-    const void* kf = edge1_pipe_kernel(7, p.edge1.code);
-    if (!kb || !kf) return fail(OEQB_ERR_UNSUPPORTED, "no pass B kernel for this degree");
-    int nb;
-    {
-      std::lock_guard<std::mutex> g(p.mu);
-      auto it = p.occ.find(kb);
-      if (it == p.occ.end()) {
-        int m = 0;
-        OEQB_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&m, kb, kEdgeWarps * 32, 0));
-        if (m <= 0) return fail(OEQB_ERR_UNSUPPORTED, "pass B kernel does not fit");
-        it = p.occ.emplace(kb, m).first;
-      }
-      nb = it->second;
-    }
+    // Pass B writes plain dX rows; rows of nodes that send no edge stay at the cleared zero.
     OEQB_CUDA(cudaMemsetAsync(a.out0, 0, sizeof(T) * size_t(a.nnodes) * p.L1dim, stream));
-    const float* recs = tail;
-    float* side = tail + size_t(kE1Rec) * size_t(a.nitems);
-    const long long blocks32 = (a.nitems + 31) / 32;
-    const long long ctas = std::max<long long>(
-        1, std::min<long long>((long long)p.sm_count * nb, (blocks32 + kEdgeWarps - 1) / kEdgeWarps));
-    void* pb[] = {const_cast<Args<T>*>(&a), &e, &recs, &side};
-    OEQB_CUDA(cudaLaunchKernel(kb, dim3(static_cast<unsigned>(ctas)), dim3(kEdgeWarps * 32), pb, 0,
-                               stream));
-    const float* cside = side;
-    void* pf[] = {const_cast<Args<T>*>(&a), &cside};
-    const unsigned fblocks = static_cast<unsigned>(
-        std::max<long long>(1, std::min<long long>((blocks32 + 255) / 256, (long long)p.sm_count * 8)));
-    OEQB_CUDA(cudaLaunchKernel(kf, dim3(fblocks), dim3(256), pf, 0, stream));
+    if constexpr (std::is_same_v<T, float>)
+      return launch_band<float>(p, a, tail, tail + size_t(kE1Rec) * size_t(a.nitems), stream);
+    else
+      return fail(OEQB_ERR_UNSUPPORTED, "the pipelined kernels are float32 only");
   }
   return 0;
 }
 
+// Workspace of the unpipelined single-path deterministic backward: one record per edge, then
+// pass B's side slots (kBandSlot values per 32 edges).
 size_t edge1_det_ws_bytes(const oeqb_plan& p, int64_t nnz) {
   if (!(p.edge1_ok && p.det && !p.kahan) || nnz <= 0) return 0;
-  return size_t(nnz) * kE1Rec * p.elem();
+  return (size_t(nnz) * kE1Rec + size_t(kBandSlot) * ((size_t(nnz) + 31) / 32)) * p.elem();
 }
 
 // Shared-weight uvw forward on CUDA cores (float64).
@@ -1757,9 +1772,12 @@ int conv_bwd_t(oeqb_plan* p, bool db, const void* X, const void* Y, const void* 
   if (p->det) {
     if (!perm) return fail(OEQB_ERR_INVALID, "deterministic convolution needs transpose_perm");
     const size_t need = edge1_det_ws_bytes(*p, nnz);
-    if (!db && need && ws && ws_bytes >= need && aligned16(ws) && aligned16(Y) && aligned16(gY)) {
-      if (int rc = launch_edge1<T>(*p, 5, a, static_cast<T*>(ws), s)) return rc;
-      return launch_edge1<T>(*p, 6, a, static_cast<T*>(ws), s);
+    // Records are read with 32-byte loads (float) or 16-byte loads (double).
+    const bool ws_ok = ws && (sizeof(T) == 4 ? aligned32(ws) : aligned16(ws));
+    if (!db && need && ws_ok && ws_bytes >= need && aligned16(Y) && aligned16(gY)) {
+      T* recs = static_cast<T*>(ws);
+      if (int rc = launch_edge1<T>(*p, 5, a, recs, s)) return rc;
+      return launch_band<T>(*p, a, recs, recs + size_t(kE1Rec) * size_t(nnz), s);
     }
     OEQB_CUDA(cudaMemsetAsync(gY, 0, sizeof(T) * size_t(nnz) * p->L2dim, s));
     return launch(*p, det_kernel_ptr<T>(1, p->uvw, db, p->kahan), a, false, true, s);

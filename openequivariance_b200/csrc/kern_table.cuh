@@ -75,7 +75,7 @@ const void* edge_kernel_ptr(int kind);
       case 3: return (const void*)conv_bwd_edge1<T>;                              \
       case 4: return (const void*)conv_fwd_edge1_det<T>;                          \
       case 5: return (const void*)conv_bwd_edge1_msg<T>;                          \
-      default: return (const void*)conv_bwd_edge1_gather<T>;                      \
+      default: return nullptr;                                                    \
     }                                                                             \
   }
 

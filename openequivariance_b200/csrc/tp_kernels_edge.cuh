@@ -700,6 +700,189 @@ __device__ __forceinline__ long long e1_bits_key(T v) {
     return __double_as_longlong(v);
 }
 
+// 32-byte read-only load of 8 floats (ld.global.v8, sm_100); p must be 32-byte aligned.
+__device__ __forceinline__ void ldg_v8(float (&v)[8], const float* p) {
+  asm("ld.global.nc.v8.f32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+      : "=f"(v[0]), "=f"(v[1]), "=f"(v[2]), "=f"(v[3]), "=f"(v[4]), "=f"(v[5]), "=f"(v[6]), "=f"(v[7])
+      : "l"(p));
+}
+
+// One 8-value record: a 32-byte load for float (32-byte aligned), four 16-byte loads for double.
+template <class T>
+__device__ __forceinline__ void load_rec8(T (&r)[kE1Rec], const T* src) {
+  if constexpr (sizeof(T) == 4) {
+    ldg_v8(r, src);
+  } else {
+#pragma unroll
+    for (int q = 0; q < kE1Rec / 2; ++q) {
+      const double2 u = __ldg(reinterpret_cast<const double2*>(src) + q);
+      r[2 * q] = u.x;
+      r[2 * q + 1] = u.y;
+    }
+  }
+}
+
+// Deterministic backward pass B, banded.  transpose_perm lists the edges in sender order; pass
+// B sums each sender's records (written by pass A in edge order) along it.  The positions are
+// cut into absolute 32-position blocks, and warp w of W takes blocks w, w + W, w + 2W, ...: at
+// any moment the warps work on one band of about W blocks, so the records of one cache line
+// (consecutive edges of one receiver, whose senders are near one another in the node order)
+// are read while the line is still in L2.  (Contiguous per-warp ranges spread the warps over
+// the whole array at once, and nearly every record read then fetched its line from DRAM
+// again.)
+//
+// Per block, the runs of equal senders are summed with a segmented shuffle tree.  A run that
+// neither contains lane 0 nor lane 31 is complete and is stored into dX directly.  The run
+// holding lane 0 goes to the block's head slot, the run holding lane 31 (if it is another run)
+// to its tail slot; conv_bwd_edge1_band_fix joins the slots of consecutive blocks.  Every sum
+// is taken in one fixed order (the tree inside each block, then the blocks left to right), so
+// the result does not depend on the grid, the SM count or timing.
+//
+// Side slots: kBandSlot values per block, head at [0, 8), tail at [8, 16), the sum in the
+// first D1 values and the sender key's bits in the last.  Head key -1: lane 0 holds no valid
+// record.  Tail key -1: lane 31 holds none; -2: the head run reaches lane 31 (one run fills
+// the block).  The transpose_perm entries are loaded two blocks ahead and the records one
+// block ahead.  dX rows of nodes that send no edge are not written (the caller clears dX).
+template <class T, int D1>
+__device__ __forceinline__ void band_slot_store(T* dst, const T (&h)[D1], long long key) {
+  T v[8];
+#pragma unroll
+  for (int i = 0; i < 7; ++i) v[i] = i < D1 ? h[i] : T(0);
+  v[7] = e1_key_bits<T>(key);
+  if constexpr (sizeof(T) == 4) {
+    reinterpret_cast<float4*>(dst)[0] = make_float4(v[0], v[1], v[2], v[3]);
+    reinterpret_cast<float4*>(dst)[1] = make_float4(v[4], v[5], v[6], v[7]);
+  } else {
+#pragma unroll
+    for (int q = 0; q < 4; ++q) reinterpret_cast<double2*>(dst)[q] = make_double2(v[2 * q], v[2 * q + 1]);
+  }
+}
+
+template <class T, int A>
+__global__ void __launch_bounds__(kEdgeWarps * 32) conv_bwd_edge1_band(const Args<T> a,
+                                                                       const Edge1 p,
+                                                                       const T* __restrict__ ws,
+                                                                       T* __restrict__ side) {
+  (void)p;
+  constexpr int D1 = 2 * A + 1, R = kE1Rec;
+  const int lane = threadIdx.x & 31;
+  const long long nw = static_cast<long long>(gridDim.x) * kEdgeWarps;
+  const long long n = a.nitems;
+  const long long nb = (n + 31) / 32;
+  long long b = static_cast<long long>(blockIdx.x) * kEdgeWarps + (threadIdx.x >> 5);
+  if (b >= nb) return;
+  // Edge at position 32 blk + lane, or -1 (past the end, or a bad permutation entry: status 2).
+  auto edge_at = [&](long long blk) -> long long {
+    const long long t = blk * 32 + lane;
+    if (blk >= nb || t >= n) return -1;
+    const long long e = a.perm[t];
+    if (e < 0 || e >= n) {
+      flag(a.status, 2);
+      return -1;
+    }
+    return e;
+  };
+  auto load = [&](T (&r)[R], long long e) {
+    if (e >= 0) {
+      load_rec8<T>(r, ws + e * R);
+    } else {
+#pragma unroll
+      for (int i = 0; i < R - 1; ++i) r[i] = T(0);
+      r[R - 1] = e1_key_bits<T>(-1);
+    }
+  };
+  long long e_c = edge_at(b);
+  long long e_n = edge_at(b + nw);
+  T rc[R];
+  load(rc, e_c);
+  for (; b < nb; b += nw) {
+    const long long e_nn = edge_at(b + 2 * nw);  // two blocks ahead
+    T rn[R];
+    load(rn, e_n);  // one block ahead
+    T h[D1];
+#pragma unroll
+    for (int i = 0; i < D1; ++i) h[i] = rc[i];
+    const long long k64 = e1_bits_key<T>(rc[R - 1]);
+    const int key = (k64 < 0 || k64 >= a.nnodes) ? -1 : static_cast<int>(k64);
+    const int prev = __shfl_up_sync(0xffffffffu, key, 1);
+    const bool head = key >= 0 && (lane == 0 || prev != key);
+    e1_seg_sum<T, D1>(h, key, lane);
+    const unsigned hm = __ballot_sync(0xffffffffu, head);
+    const int last_head = hm ? 31 - __clz(hm) : -1;
+    const bool v31 = __shfl_sync(0xffffffffu, key, 31) >= 0;
+    T* hs = side + b * kBandSlot;
+    if (head) {
+      if (lane == 0)
+        band_slot_store<T, D1>(hs, h, key);
+      else if (lane == last_head && v31)
+        band_slot_store<T, D1>(hs + 8, h, key);
+      else
+        e1_store_row(a.out0 + static_cast<long long>(key) * D1, h);
+    }
+    if (lane == 0) {
+      if (!head) hs[7] = e1_key_bits<T>(-1);
+      if (!v31)
+        hs[15] = e1_key_bits<T>(-1);
+      else if (last_head == 0)
+        hs[15] = e1_key_bits<T>(-2);
+    }
+#pragma unroll
+    for (int i = 0; i < R; ++i) rc[i] = rn[i];
+    e_c = e_n;
+    e_n = e_nn;
+  }
+}
+
+// Joins the head / tail slots of conv_bwd_edge1_band, one thread per block b.  The run in b's
+// head slot is written here if it starts in b (block b - 1 does not end with the same sender)
+// and ends in b.  A run that starts in b and reaches lane 31 (b's tail slot, or its head slot
+// when one run fills b) is summed with the head slots of the following blocks, left to right,
+// as long as they continue it, and written.  Each run is written once.
+template <class T, int A>
+__global__ void __launch_bounds__(256) conv_bwd_edge1_band_fix(const Args<T> a,
+                                                               const T* __restrict__ side) {
+  constexpr int D1 = 2 * A + 1;
+  const long long nb = (a.nitems + 31) / 32;
+  const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
+  auto hkey = [&](long long m) { return e1_bits_key<T>(side[m * kBandSlot + 7]); };
+  auto tkey = [&](long long m) { return e1_bits_key<T>(side[m * kBandSlot + 15]); };
+  for (long long b = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; b < nb;
+       b += stride) {
+    const long long k0 = hkey(b), t0 = tkey(b);
+    long long prev_last = -1;
+    if (b > 0) {
+      const long long tp = tkey(b - 1);
+      prev_last = tp >= 0 ? tp : (tp == -2 ? hkey(b - 1) : -1);
+    }
+    const bool starts = k0 >= 0 && prev_last != k0;
+    const T* hs = side + b * kBandSlot;
+    T s[D1];
+    if (starts && t0 != -2) {
+#pragma unroll
+      for (int i = 0; i < D1; ++i) s[i] = hs[i];
+      e1_store_row(a.out0 + k0 * D1, s);
+    }
+    long long k = -1;
+    if (t0 >= 0) {
+      k = t0;
+#pragma unroll
+      for (int i = 0; i < D1; ++i) s[i] = hs[8 + i];
+    } else if (t0 == -2 && starts) {
+      k = k0;
+#pragma unroll
+      for (int i = 0; i < D1; ++i) s[i] = hs[i];
+    }
+    if (k < 0) continue;
+    for (long long m = b + 1; m < nb; ++m) {
+      if (hkey(m) != k) break;
+#pragma unroll
+      for (int i = 0; i < D1; ++i) s[i] += side[m * kBandSlot + i];
+      if (tkey(m) != -2) break;
+    }
+    e1_store_row(a.out0 + k * D1, s);
+  }
+}
+
 template <class T>
 __global__ void __launch_bounds__(kEdgeWarps * 32) conv_bwd_edge1_msg(const Args<T> a, const Edge1 p,
                                                                       T* ws) {
@@ -732,61 +915,5 @@ __global__ void __launch_bounds__(kEdgeWarps * 32) conv_bwd_edge1_msg(const Args
   });
 }
 
-template <class T>
-__global__ void __launch_bounds__(kEdgeWarps * 32) conv_bwd_edge1_gather(const Args<T> a,
-                                                                         const Edge1 p, const T* ws) {
-  const int lane = threadIdx.x & 31;
-  const long long nwarps = static_cast<long long>(gridDim.x) * kEdgeWarps;
-  const long long wg = static_cast<long long>(blockIdx.x) * kEdgeWarps + (threadIdx.x >> 5);
-  const long long n = a.nitems;
-  dispatch_l(p.code >> 8, [&]<int A>() {
-    constexpr int D1 = 2 * A + 1, R = kE1Rec;
-    // Sender of sender-sorted position t (the permutation is range-checked).
-    auto sender = [&](long long t) -> long long {
-      const long long e = a.perm[t];
-      if (e < 0 || e >= n) return -1;
-      return e1_bits_key(ws[e * R + R - 1]);
-    };
-    const long long p0 = e1_snap(static_cast<long long>((static_cast<__int128>(n) * wg) / nwarps), n, sender, lane);
-    const long long p1 = e1_snap(static_cast<long long>((static_cast<__int128>(n) * (wg + 1)) / nwarps), n, sender, lane);
-    T carry[D1];
-    long long carry_key = -2;
-    for (long long base = p0; base < p1; base += 32) {
-      const long long t = base + lane;
-      long long key = -1;
-      T h[D1];
-#pragma unroll
-      for (int i = 0; i < D1; ++i) h[i] = T(0);
-      if (t < p1) {
-        const long long e = a.perm[t];
-        if (e < 0 || e >= n) {
-          flag(a.status, 2);
-        } else {
-          T rec[R];
-          const T* r = ws + e * R;
-          if constexpr (sizeof(T) == 4) {
-            const float4 u = __ldg(reinterpret_cast<const float4*>(r));
-            const float4 v = __ldg(reinterpret_cast<const float4*>(r) + 1);
-            rec[0] = u.x; rec[1] = u.y; rec[2] = u.z; rec[3] = u.w;
-            rec[4] = v.x; rec[5] = v.y; rec[6] = v.z; rec[7] = v.w;
-          } else {
-#pragma unroll
-            for (int q = 0; q < R / 2; ++q) {
-              const double2 u = __ldg(reinterpret_cast<const double2*>(r) + q);
-              rec[2 * q] = u.x;
-              rec[2 * q + 1] = u.y;
-            }
-          }
-#pragma unroll
-          for (int i = 0; i < D1; ++i) h[i] = rec[i];
-          key = e1_bits_key(rec[R - 1]);
-        }
-      }
-      const bool more = base + 32 < p1;
-      const long long nk = more ? sender(base + 32) : -3;
-      e1_seg_block<T, D1>(h, key, nk, more, carry, carry_key, a.out0, lane);
-    }
-  });
-}
 
 }  // namespace oeqb

@@ -100,13 +100,6 @@ __device__ __forceinline__ void pipe_stage_in(PipeStage<D2>& st, const long long
 // D <= 4, a 32-byte load (ld.global.v8, sm_100) above, with no alignment arithmetic on the lane.
 constexpr int kPadRow = 8;
 
-// 32-byte read-only load of 8 floats; p must be 32-byte aligned.
-__device__ __forceinline__ void ldg_v8(float (&v)[8], const float* p) {
-  asm("ld.global.nc.v8.f32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
-      : "=f"(v[0]), "=f"(v[1]), "=f"(v[2]), "=f"(v[3]), "=f"(v[4]), "=f"(v[5]), "=f"(v[6]), "=f"(v[7])
-      : "l"(p));
-}
-
 template <int D>
 __device__ __forceinline__ void load_row8(float (&v)[D], const float* src, long long node) {
   static_assert(D <= kPadRow, "row wider than the padded layout");
@@ -494,171 +487,6 @@ __global__ void __launch_bounds__(kEdgeWarps * 32) conv_fwd_edge1_pipe2(const Ar
     s = s1;
   }
   cp_async_wait<0>();
-}
-
-// Deterministic backward pass B, banded.  transpose_perm lists the edges in sender order; pass
-// B sums each sender's records along it.  The positions are cut into absolute 32-position
-// blocks, and warp w of W takes blocks w, w + W, w + 2W, ...: at any moment the warps work on
-// one band of about W blocks, so the four records of a 128-byte line (four consecutive edges
-// of one receiver, whose senders are near one another in the node order) are read while the
-// line is still in L2.  (Contiguous per-warp ranges spread the warps over the whole array at
-// once, and nearly every record read then fetched its line from DRAM again.)
-//
-// Per block, the runs of equal senders are summed with a segmented shuffle tree.  A run that
-// neither contains lane 0 nor lane 31 is complete and is stored into dX directly.  The run
-// holding lane 0 goes to the block's head slot, the run holding lane 31 (if it is another run)
-// to its tail slot; conv_bwd_edge1_band_fix joins the slots of consecutive blocks.  Every sum
-// is taken in one fixed order (the tree inside each block, then the blocks left to right), so
-// the result does not depend on the grid, the SM count or timing.
-//
-// Side slots: 16 floats per block, head at [0, 8), tail at [8, 16), the sum in the first D1
-// floats and the sender key's bits in the last.  Head key -1: lane 0 holds no valid record.
-// Tail key -1: lane 31 holds none; -2: the head run reaches lane 31 (one run fills the block).
-// The transpose_perm entries are loaded two blocks ahead and the 32-byte records one block
-// ahead.
-struct PipeRec {
-  float4 u, v;
-};
-
-__device__ __forceinline__ PipeRec load_rec(const float* ws, long long e, bool ok) {
-  PipeRec r;
-  if (ok) {
-    float t[8];
-    ldg_v8(t, ws + e * kE1Rec);
-    r.u = make_float4(t[0], t[1], t[2], t[3]);
-    r.v = make_float4(t[4], t[5], t[6], t[7]);
-  } else {
-    r.u = make_float4(0.f, 0.f, 0.f, 0.f);
-    r.v = make_float4(0.f, 0.f, 0.f, __int_as_float(-1));
-  }
-  return r;
-}
-
-template <int D1>
-__device__ __forceinline__ void band_slot_store(float* dst, const float (&h)[D1], int key) {
-  float v[8];
-#pragma unroll
-  for (int i = 0; i < 7; ++i) v[i] = i < D1 ? h[i] : 0.f;
-  v[7] = __int_as_float(key);
-  reinterpret_cast<float4*>(dst)[0] = make_float4(v[0], v[1], v[2], v[3]);
-  reinterpret_cast<float4*>(dst)[1] = make_float4(v[4], v[5], v[6], v[7]);
-}
-
-template <int A>
-__global__ void __launch_bounds__(kEdgeWarps * 32) conv_bwd_edge1_band(const Args<float> a,
-                                                                       const Edge1 p,
-                                                                       const float* __restrict__ ws,
-                                                                       float* __restrict__ side) {
-  (void)p;
-  constexpr int D1 = 2 * A + 1;
-  const int lane = threadIdx.x & 31;
-  const long long nw = static_cast<long long>(gridDim.x) * kEdgeWarps;
-  const long long n = a.nitems;
-  const long long nb = (n + 31) / 32;
-  long long b = static_cast<long long>(blockIdx.x) * kEdgeWarps + (threadIdx.x >> 5);
-  if (b >= nb) return;
-  // Edge at position 32 blk + lane, or -1 (past the end, or a bad permutation entry: status 2).
-  auto edge_at = [&](long long blk) -> long long {
-    const long long t = blk * 32 + lane;
-    if (blk >= nb || t >= n) return -1;
-    const long long e = a.perm[t];
-    if (e < 0 || e >= n) {
-      flag(a.status, 2);
-      return -1;
-    }
-    return e;
-  };
-  long long e_c = edge_at(b);
-  long long e_n = edge_at(b + nw);
-  PipeRec rc = load_rec(ws, e_c, e_c >= 0);
-  for (; b < nb; b += nw) {
-    const long long e_nn = edge_at(b + 2 * nw);  // two blocks ahead
-    const PipeRec rn = load_rec(ws, e_n, e_n >= 0);  // one block ahead
-    const float rec[8] = {rc.u.x, rc.u.y, rc.u.z, rc.u.w, rc.v.x, rc.v.y, rc.v.z, rc.v.w};
-    float h[D1];
-#pragma unroll
-    for (int i = 0; i < D1; ++i) h[i] = rec[i];
-    int key = __float_as_int(rec[kE1Rec - 1]);
-    if (key < 0 || key >= a.nnodes) key = -1;
-    const int prev = __shfl_up_sync(0xffffffffu, key, 1);
-    const bool head = key >= 0 && (lane == 0 || prev != key);
-    e1_seg_sum<float, D1>(h, key, lane);
-    const unsigned hm = __ballot_sync(0xffffffffu, head);
-    const int last_head = hm ? 31 - __clz(hm) : -1;
-    const bool v31 = __shfl_sync(0xffffffffu, key, 31) >= 0;
-    float* hs = side + b * kBandSlot;
-    if (head) {
-      if (lane == 0)
-        band_slot_store<D1>(hs, h, key);
-      else if (lane == last_head && v31)
-        band_slot_store<D1>(hs + 8, h, key);
-      else
-        e1_store_row(a.out0 + static_cast<long long>(key) * D1, h);
-    }
-    if (lane == 0) {
-      if (!head) hs[7] = __int_as_float(-1);
-      if (!v31)
-        hs[15] = __int_as_float(-1);
-      else if (last_head == 0)
-        hs[15] = __int_as_float(-2);
-    }
-    rc = rn;
-    e_c = e_n;
-    e_n = e_nn;
-  }
-}
-
-// Joins the head / tail slots of conv_bwd_edge1_band, one thread per block b.  The run in b's
-// head slot is written here if it starts in b (block b - 1 does not end with the same sender)
-// and ends in b.  A run that starts in b and reaches lane 31 (b's tail slot, or its head slot
-// when one run fills b) is summed with the head slots of the following blocks, left to right,
-// as long as they continue it, and written.  Each run is written once.
-template <int A>
-__global__ void __launch_bounds__(256) conv_bwd_edge1_band_fix(const Args<float> a,
-                                                               const float* __restrict__ side) {
-  constexpr int D1 = 2 * A + 1;
-  const long long nb = (a.nitems + 31) / 32;
-  const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
-  auto hkey = [&](long long m) { return __float_as_int(side[m * kBandSlot + 7]); };
-  auto tkey = [&](long long m) { return __float_as_int(side[m * kBandSlot + 15]); };
-  auto add = [&](float (&s)[D1], const float* src) {
-#pragma unroll
-    for (int i = 0; i < D1; ++i) s[i] += src[i];
-  };
-  for (long long b = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; b < nb;
-       b += stride) {
-    const int k0 = hkey(b), t0 = tkey(b);
-    int prev_last = -1;
-    if (b > 0) {
-      const int tp = tkey(b - 1);
-      prev_last = tp >= 0 ? tp : (tp == -2 ? hkey(b - 1) : -1);
-    }
-    const bool starts = k0 >= 0 && prev_last != k0;
-    const float* hs = side + b * kBandSlot;
-    float s[D1];
-    if (starts && t0 != -2) {
-#pragma unroll
-      for (int i = 0; i < D1; ++i) s[i] = hs[i];
-      e1_store_row(a.out0 + static_cast<long long>(k0) * D1, s);
-    }
-    int k = -1;
-    if (t0 >= 0) {
-      k = t0;
-#pragma unroll
-      for (int i = 0; i < D1; ++i) s[i] = hs[8 + i];
-    } else if (t0 == -2 && starts) {
-      k = k0;
-#pragma unroll
-      for (int i = 0; i < D1; ++i) s[i] = hs[i];
-    }
-    if (k < 0) continue;
-    for (long long m = b + 1; m < nb; ++m) {
-      if (hkey(m) != k) break;
-      add(s, side + m * kBandSlot);
-      if (tkey(m) != -2) break;
-    }
-    e1_store_row(a.out0 + static_cast<long long>(k) * D1, s);
-  }
 }
 
 // Deterministic forward, two edges per lane.  Warp w owns the edges of whole receivers: its

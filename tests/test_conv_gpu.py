@@ -113,11 +113,13 @@ def test_radius_graph_c1_irreps_vs_oracle(mode, cuda_device):
     assert_close(w.grad, gW, dtype, "dW")
 
 
+@pytest.mark.parametrize("dtype", [np.float32, np.float64], ids=["f32", "f64"])
 @pytest.mark.parametrize("mode", ["atomic", "deterministic"])
-def test_single_path_silent_senders_and_hub(mode, cuda_device):
+def test_single_path_silent_senders_and_hub(mode, dtype, cuda_device):
     """C3-class conv on a graph where nodes 0-49 send no edge (their dX rows must be zero),
     nodes 50-59 receive none (zero Z rows), and node 60 sends to every receiver, so its run in
-    transpose_perm order spans several 32-edge blocks."""
+    transpose_perm order spans several 32-edge blocks.  float32 runs the pipelined kernels,
+    float64 the generic ones (both with the banded pass B when deterministic)."""
     import openequivariance_b200 as oeq
 
     n = 300
@@ -132,27 +134,28 @@ def test_single_path_silent_senders_and_hub(mode, cuda_device):
     tperm = np.argsort(cols * n + rows, kind="stable")
     E = len(rows)
     prob = oeq.TPProblem("1x2e", "1x3e", "1x2e", [(0, 0, 0, "uvu", True)],
-                         shared_weights=False, internal_weights=False)
+                         shared_weights=False, internal_weights=False, irrep_dtype=dtype,
+                         weight_dtype=dtype)
     conv = oeq.TensorProductConv(prob, deterministic=mode != "atomic")
     p = O.make_problem("1x2e", "1x3e", "1x2e", [(0, 0, 0, "uvu", True)])
     X, Y = rng.normal(size=(n, 5)), rng.normal(size=(E, 7))
     W, G = rng.normal(size=(E, 1)), rng.normal(size=(n, 5))
     args = [_idx(rows), _idx(cols), _idx(tperm) if mode != "atomic" else None]
-    x, y, w = (to_dev(X, np.float32).requires_grad_(), to_dev(Y, np.float32).requires_grad_(),
-               to_dev(W, np.float32).requires_grad_())
+    x, y, w = (to_dev(X, dtype).requires_grad_(), to_dev(Y, dtype).requires_grad_(),
+               to_dev(W, dtype).requires_grad_())
     Z = conv(x, y, w, *args)
     # Leave NaN behind in freed blocks of the caching allocator, so a dX row the kernels skip
     # does not read as zero by chance.
-    junk = torch.full((64, n * 5), float("nan"), device="cuda")
+    junk = torch.full((64, n * 5), float("nan"), device="cuda", dtype=x.dtype)
     del junk
-    Z.backward(to_dev(G, np.float32))
-    assert_close(Z, O.conv_forward(p, X, Y, W, rows, cols), np.float32, "forward")
+    Z.backward(to_dev(G, dtype))
+    assert_close(Z, O.conv_forward(p, X, Y, W, rows, cols), dtype, "forward")
     gX, gY, gW = O.conv_backward(p, X, Y, W, G, rows, cols)
     assert torch.all(x.grad[:50] == 0)
     assert torch.all(Z[50:60] == 0)
-    assert_close(x.grad, gX, np.float32, "dX")
-    assert_close(y.grad, gY, np.float32, "dY")
-    assert_close(w.grad, gW, np.float32, "dW")
+    assert_close(x.grad, gX, dtype, "dX")
+    assert_close(y.grad, gY, dtype, "dY")
+    assert_close(w.grad, gW, dtype, "dW")
 
 
 @pytest.mark.parametrize("kahan", [False, True])
