@@ -70,7 +70,7 @@ int oeqb_plan_destroy(oeqb_plan* plan);
  * rows, then the dX accumulator (atomic: 3 x 32 x node_count bytes + 256) or one 32-byte
  * record per edge and 64 bytes per 32 edges for the backward's per-block sums (deterministic:
  * 2 x 32 x node_count + 32 x nnz + 64 x ceil(nnz / 32) + 256); other deterministic plans keep
- * one 8-value record per edge.  With a smaller (or, for the float32 kernels, not 32-byte
+ * one 8-value record per edge and 16 values per 32 edges for the backward's per-block sums.  With a smaller (or, for the float32 kernels, not 32-byte
  * aligned) workspace those plans run slower kernels that need none.  The double backward
  * needs none. */
 size_t oeqb_conv_workspace_bytes(const oeqb_plan* plan, int64_t nnz, int64_t node_count);
