@@ -604,9 +604,10 @@ C5_EDGES = {200000: 33509164}
 
 
 def _conv_desc(n, E, mode):
+    edges = f"{E} directed edges" if E is not None else "C3's edge density"
     return (f"conv: C3 irreps (1x2e x 1x3e -> 1x2e, uvu, per-edge weights) fused conv fwd+bwd "
-            f"on the C5 graph: periodic radius graph, {n} nodes (Morton-numbered), {E} directed "
-            f"edges, {mode}")
+            f"on the C5 graph: periodic radius graph, {n} nodes (Morton-numbered), {edges}, "
+            f"{mode}")
 
 
 def _ev_ms(fn, reps=10, warm=3):
