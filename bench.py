@@ -15,8 +15,10 @@ uvu, 24 paths, 50,000 rows, fwd+bwd) and the symmetric contraction (``sc_c5``), 
 own roofline.  Other workloads: ``--workload c2 | c2ml | c4 | sc``.
 
 Timing: W warm-up steps, then K steps between barriers + device syncs, CUDA events on the
-launching stream, max over ranks.  Inputs are larger than L2 (126 MB) so no flush is
-needed.  ``e2e`` repeats the step through the public module API with pinned host buffers,
+launching stream, max over ranks.  The conv and C2 inputs are larger than L2 (126 MB), so no
+flush is needed; a batch-TP step whose algorithmic bytes are under twice L2 (C4 at 20,000
+rows) flushes L2 before every step with a 256 MB memset outside the timed events, and its
+time is the sum of the steps' own event intervals.  ``e2e`` repeats the step through the public module API with pinned host buffers,
 host->device copies of the inputs and device->host copies of every output inside the timed
 region.  ``--impl reference`` times the CPU port of the reference's e3nn-backed path (the
 reference ships no CPU implementation of its own) on the host cores.
@@ -72,6 +74,9 @@ def _peaks():
         return float(pk["hbm_gbs"]), "measured"
     except Exception:
         return HBM_FALLBACK_GBS, "fallback"
+
+
+L2_BYTES = 126 * 1024 * 1024  # B200 L2
 
 
 def _traffic(kernel_key):
@@ -293,6 +298,16 @@ def bench_tp(args, world, rank, local):
         step()
     torch.cuda.synchronize()
     launches = _launches_per_step(step)
+    s = 4
+    d1, d2, d3, wn = (problem.irreps_in1.dim, problem.irreps_in2.dim, problem.irreps_out.dim,
+                      problem.weight_numel)
+    wrow = 0 if shared else wn
+    bytes_fwd = B * (d1 + d2 + d3 + wrow) * s + (wn * s if shared else 0)
+    bytes_bwd = B * (2 * d1 + 2 * d2 + d3 + 2 * wrow) * s + (2 * wn * s if shared else 0)
+    # A step that fits in L2 would find its inputs there on the next step: flush L2 before
+    # every step (outside the step's own events) and time the steps alone.
+    flush = bytes_fwd + bytes_bwd < 2 * L2_BYTES
+    flush_buf = torch.empty(2 * L2_BYTES, dtype=torch.uint8, device=dev) if flush else None
     K = args.steps
     ev = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(K)]
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -302,6 +317,8 @@ def bench_tp(args, world, rank, local):
         start.record()
         for k in range(K):
             e = ev[k]
+            if flush:
+                flush_buf.zero_()
             e[0].record()
             Z = ops.jit_tp_forward(tp.kernel, tp.hash, X, Y, W, tp.L3_dim)
             e[1].record()
@@ -315,15 +332,12 @@ def bench_tp(args, world, rank, local):
         end.record()
         torch.cuda.synchronize()
     _barrier(world)
-    elapsed_ms = _max_over_ranks(start.elapsed_time(end), world)
+    if flush:
+        elapsed_ms = _max_over_ranks(float(sum(e[0].elapsed_time(e[3]) for e in ev)), world)
+    else:
+        elapsed_ms = _max_over_ranks(start.elapsed_time(end), world)
     t_fwd = float(np.mean([e[0].elapsed_time(e[1]) for e in ev]))
     t_bwd = float(np.mean([e[2].elapsed_time(e[3]) for e in ev]))
-    s = 4
-    d1, d2, d3, wn = (problem.irreps_in1.dim, problem.irreps_in2.dim, problem.irreps_out.dim,
-                      problem.weight_numel)
-    wrow = 0 if shared else wn
-    bytes_fwd = B * (d1 + d2 + d3 + wrow) * s + (wn * s if shared else 0)
-    bytes_bwd = B * (2 * d1 + 2 * d2 + d3 + 2 * wrow) * s + (2 * wn * s if shared else 0)
     peak, peak_src = _peaks()
     dom = ("tp_bwd", bytes_bwd, t_bwd) if t_bwd >= t_fwd else ("tp_fwd", bytes_fwd, t_fwd)
     achieved = dom[1] / (dom[2] * 1e-3) / 1e9
@@ -395,7 +409,9 @@ def bench_tp(args, world, rank, local):
         "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": {"workload": _workload_desc(args.workload, problem),
                    "rows_per_gpu": B, "global_rows": B * world,
-                   "l2": "inputs larger than L2 (no flush needed)",
+                   "l2": ("L2 flushed before every step (256 MB memset outside the timed "
+                          "events); steps timed alone" if flush
+                          else "inputs larger than L2 (no flush needed)"),
                    "parallelism": f"dp{world} (independent row shards)"},
         "kernels_ms": {"tp_fwd": t_fwd, "tp_bwd": t_bwd},
         "roofline": {"bound": "hbm", "kernel": dom[0], "achieved": achieved, "peak": peak,
